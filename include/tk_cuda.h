@@ -1,0 +1,177 @@
+/*
+ * tk_cuda.h -- C ABI of the B200 (sm_100a) INT4 GEMV / INT4 Llama-FFN path.
+ *
+ * This header is the drop-in boundary that replaces the Metal runtime under the
+ * reference's Zig kernel API (Lulzx/tiny-kernel):
+ *
+ *   reference (Zig + Metal)                         this ABI
+ *   ---------------------------------------------   ----------------------------------
+ *   src/main.zig:17-23        tk.init / tk.deinit   tk_device_create / tk_device_destroy
+ *   src/metal/device.zig:42-45  Device.name         tk_device_name
+ *   src/metal/device.zig:85-91  Device.createBuffer tk_buffer_alloc / tk_buffer_free
+ *   src/metal/device.zig:123-133 Buffer.slice       tk_buffer_upload / tk_buffer_download
+ *   src/kernels/quantized.zig:15-50 QMatMulInt4     tk_qmatmul_int4(_async)
+ *   src/kernels/rmsnorm.zig:15-42   RMSNorm         tk_rmsnorm(_async)
+ *   src/kernels/fused.zig:15-50     FusedRMSNormRoPE tk_fused_rmsnorm_rope(_async)
+ *   src/kernels/fused.zig:187-212   FusedSiluMul    tk_silu_mul(_async)
+ *   src/bench.zig:266-341  INT4 FFN composition     tk_int4_ffn(_async)   (adds the down projection)
+ *
+ * Conventions
+ *  - Every entry point returns TK_OK (0) or a negative TK_ERR_* status; the text of
+ *    the last failure on the calling thread is available from tk_last_error_string().
+ *  - All tensor pointers are DEVICE pointers (from tk_buffer_alloc or any CUDA
+ *    allocation) unless a function says otherwise.  Buffers are owned by the caller,
+ *    as Buffer(T) is in the reference (bench.zig:225-240, `defer x.deinit()`).
+ *  - The plain entry points are synchronous, like the reference's forward()
+ *    (commit + waitUntilCompleted, quantized.zig:47-49): outputs are ready on return.
+ *    The *_async variants enqueue on the given CUDA stream (NULL = the device's
+ *    stream) and return immediately.
+ *  - f16 scales are passed as raw IEEE binary16 bit patterns (uint16_t).
+ *
+ * INT4 weight layout (identical to qmatmul_int4, src/kernels/shaders.zig:442-501):
+ *   w_packed u8 [K/2][N]          byte (k/2)*N + n; even k = low nibble, odd k = high nibble
+ *   scales   f16 [K/group][N]     index g*N + n
+ *   zeros    u8 [K/group][N/2]    byte g*(N/2) + n/2; even n = low nibble, odd n = high nibble
+ *   y[m][n] = sum_k x[m][k] * scale[g][n] * (q[k][n] - zero[g][n]),   g = k / group
+ */
+#ifndef TK_CUDA_H
+#define TK_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TK_ABI_VERSION 1
+
+/* status codes */
+#define TK_OK 0
+#define TK_ERR_ARG (-1)         /* bad shape, null pointer, misaligned pointer   */
+#define TK_ERR_CUDA (-2)        /* a CUDA runtime / driver call failed            */
+#define TK_ERR_NCCL (-3)        /* a NCCL call failed                              */
+#define TK_ERR_TIMEOUT (-4)     /* a bounded device-side wait gave up              */
+#define TK_ERR_UNSUPPORTED (-5) /* shape or feature not supported on this build    */
+#define TK_ERR_NOMEM (-6)       /* device or host allocation failed                */
+
+/* buffer kinds for tk_buffer_alloc */
+#define TK_MEM_DEVICE 0 /* cudaMalloc: device-resident HBM                          */
+#define TK_MEM_SHARED 1 /* cudaMallocManaged: host-visible like MTLStorageModeShared */
+#define TK_MEM_HOST 2   /* cudaMallocHost: pinned host memory (staging for copies)  */
+
+/* flags for tk_int4_ffn */
+#define TK_FFN_RESIDUAL 1u /* out = x + FFN(x)  (Llama residual, llama.zig:216-231)  */
+
+typedef struct tk_device tk_device;
+
+/* One INT4 matrix in the qmatmul_int4 layout above (K and N given by the call). */
+typedef struct tk_int4_matrix {
+  const uint8_t *w_packed;  /* [K/2][N]       */
+  const uint16_t *scales;   /* [K/group][N]   */
+  const uint8_t *zeros;     /* [K/group][N/2] */
+} tk_int4_matrix;
+
+/* ---- device ---------------------------------------------------------------------- */
+
+/* Replaces tk.init() / Device.init (src/main.zig:17-19, src/metal/device.zig:10-29):
+ * selects CUDA device `ordinal`, creates its stream and the scratch the kernels use. */
+int tk_device_create(int ordinal, tk_device **out);
+/* Replaces tk.deinit() / Device.deinit (src/main.zig:21-23, device.zig:31-40). */
+void tk_device_destroy(tk_device *dev);
+/* Replaces Device.name (src/metal/device.zig:42-45). Valid until destroy. */
+const char *tk_device_name(tk_device *dev);
+/* Number of SMs the persistent kernels size their grid to. */
+int tk_device_sm_count(tk_device *dev);
+/* The device's CUDA stream (cudaStream_t) used by the synchronous entry points. */
+void *tk_device_stream(tk_device *dev);
+/* Waits for all work queued on the device's stream; returns any deferred kernel error. */
+int tk_device_synchronize(tk_device *dev);
+/* Reads and clears the device-side error word that bounded waits set (TK_ERR_TIMEOUT). */
+int tk_device_check_error(tk_device *dev);
+
+const char *tk_last_error_string(void);
+const char *tk_status_string(int status);
+int tk_abi_version(void);
+
+/* ---- buffers (Device.createBuffer / Buffer(T), src/metal/device.zig:85-135) ------- */
+
+int tk_buffer_alloc(tk_device *dev, size_t bytes, int kind, void **ptr);
+int tk_buffer_free(tk_device *dev, void *ptr);
+/* Synchronous host<->device copies on the device's stream. */
+int tk_buffer_upload(tk_device *dev, void *dst_device, const void *src_host, size_t bytes);
+int tk_buffer_download(tk_device *dev, void *dst_host, const void *src_device, size_t bytes);
+
+/* ---- kernels --------------------------------------------------------------------- */
+
+/* QMatMulInt4.forward (src/kernels/quantized.zig:15-50; kernel shaders.zig:442-501).
+ * x f32 [m][k], out f32 [m][n].  The reference computes row 0 only and requires
+ * k <= 4096; this entry point computes all m rows and any k with k % group_size == 0,
+ * group_size % 8 == 0, n even.  Shapes with n % 128 == 0, k % 128 == 0 and
+ * group_size in {16, 32, 64, 128} run the TMA-fed tensor-core GEMV engine; other
+ * legal shapes run a plain CUDA-core kernel. */
+int tk_qmatmul_int4(tk_device *dev, const float *x, const uint8_t *w_packed,
+                    const uint16_t *scales, const uint8_t *zeros, float *out, uint32_t m,
+                    uint32_t k, uint32_t n, uint32_t group_size);
+int tk_qmatmul_int4_async(tk_device *dev, const float *x, const uint8_t *w_packed,
+                          const uint16_t *scales, const uint8_t *zeros, float *out,
+                          uint32_t m, uint32_t k, uint32_t n, uint32_t group_size,
+                          void *stream);
+
+/* RMSNorm.forward (src/kernels/rmsnorm.zig:15-42; kernel shaders.zig:16-56).
+ * out[r][i] = x[r][i] * rsqrt(mean_i(x[r]^2) + eps) * weight[i] for r < rows.
+ * The reference derives rows from x.count / dim (rmsnorm.zig:33). */
+int tk_rmsnorm(tk_device *dev, const float *x, const float *weight, float *out,
+               uint32_t rows, uint32_t dim, float eps);
+int tk_rmsnorm_async(tk_device *dev, const float *x, const float *weight, float *out,
+                     uint32_t rows, uint32_t dim, float eps, void *stream);
+
+/* FusedRMSNormRoPE.forward (src/kernels/fused.zig:15-50; kernel shaders.zig:124-182).
+ * rmsnorm, then rotate-half RoPE per head_dim chunk with cos/sin[pos*head_dim/2 + j]. */
+int tk_fused_rmsnorm_rope(tk_device *dev, const float *x, const float *weight,
+                          const float *cos_cache, const float *sin_cache, float *out,
+                          uint32_t rows, uint32_t dim, uint32_t head_dim, uint32_t pos,
+                          float eps);
+int tk_fused_rmsnorm_rope_async(tk_device *dev, const float *x, const float *weight,
+                                const float *cos_cache, const float *sin_cache, float *out,
+                                uint32_t rows, uint32_t dim, uint32_t head_dim,
+                                uint32_t pos, float eps, void *stream);
+
+/* FusedSiluMul.forward (src/kernels/fused.zig:187-212; kernel shaders.zig:344-357).
+ * out[i] = gate[i] / (1 + exp(-gate[i])) * up[i] for i < n (n = gate.count). */
+int tk_silu_mul(tk_device *dev, const float *gate, const float *up, float *out, uint32_t n);
+int tk_silu_mul_async(tk_device *dev, const float *gate, const float *up, float *out,
+                      uint32_t n, void *stream);
+
+/* INT4 Llama FFN (the reference composes gate/up in src/bench.zig:266-341; the down
+ * projection and residual follow src/model/llama.zig:220-231):
+ *   h   = silu(gate(rmsnorm(x))) * up(rmsnorm(x))      [m][inter]
+ *   out = down(h)            (+ x when flags & TK_FFN_RESIDUAL)   [m][hidden]
+ * gate/up: K = hidden, N = inter.  down: K = inter, N = hidden.  eps as in RMSNorm.
+ * h_out (optional, may be NULL) receives the f32 intermediate.
+ * Fast path: hidden % 128 == 0, inter % 128 == 0, group_size in {16,32,64,128}. */
+int tk_int4_ffn(tk_device *dev, const float *x, const float *norm_weight,
+                const tk_int4_matrix *gate, const tk_int4_matrix *up,
+                const tk_int4_matrix *down, float *out, float *h_out, uint32_t m,
+                uint32_t hidden, uint32_t inter, uint32_t group_size, float eps,
+                uint32_t flags);
+int tk_int4_ffn_async(tk_device *dev, const float *x, const float *norm_weight,
+                      const tk_int4_matrix *gate, const tk_int4_matrix *up,
+                      const tk_int4_matrix *down, float *out, float *h_out, uint32_t m,
+                      uint32_t hidden, uint32_t inter, uint32_t group_size, float eps,
+                      uint32_t flags, void *stream);
+
+/* Test hook (bit-exactness of dequantisation, shaders.zig:474-495):
+ * out f32 [k][n] = float(scale[g][n]) * (float(q[k][n]) - float(zero[g][n])). */
+int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *scales,
+                    const uint8_t *zeros, float *out, uint32_t k, uint32_t n,
+                    uint32_t group_size);
+
+/* Which path tk_qmatmul_int4 / tk_int4_ffn would take for a shape:
+ * 1 = tensor-core engine, 0 = CUDA-core fallback, <0 = invalid shape. */
+int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t group_size);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TK_CUDA_H */

@@ -1,0 +1,36 @@
+"""Shared pytest setup: markers, import paths, GPU fixtures.
+
+`-m "not gpu"` runs on a CPU-only machine; `-m gpu` needs a B200 and the built
+tiny-kernel_b200/lib/libtkcuda.so (no CPU fallback exists).
+"""
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "tiny-kernel_b200")
+for p in (ROOT, PKG, os.path.join(ROOT, "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 GPU and the built libtkcuda")
+    config.addinivalue_line("markers", "slow: long-running CPU test")
+
+
+@pytest.fixture(scope="session")
+def tkdev():
+    import tiny_kernel as tk
+    dev = tk.init(0)
+    yield dev
+    dev.deinit()
+
+
+@pytest.fixture(scope="session")
+def torch_cuda():
+    import torch
+    assert torch.cuda.is_available(), "GPU test needs CUDA"
+    torch.cuda.init()
+    return torch

@@ -1,0 +1,52 @@
+"""CPU checks of the C-ABI boundary: the library loads without a GPU and exports every
+entry point include/tk_cuda.h declares; calls that need no device behave."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from tiny_kernel import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "tk_cuda.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tk_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_symbols()
+    for must in ("tk_qmatmul_int4", "tk_int4_ffn", "tk_rmsnorm", "tk_fused_rmsnorm_rope",
+                 "tk_silu_mul", "tk_device_create", "tk_buffer_alloc", "tk_dequant_int4"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    L = C.CDLL(_lib.LIB_PATH)
+    missing = [n for n in declared_symbols() if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    assert set(declared_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_calls_without_gpu():
+    L = _lib.lib()
+    assert L.tk_abi_version() == 1
+    assert L.tk_status_string(_lib.TK_ERR_TIMEOUT) == b"device-side wait timed out"
+    assert L.tk_qmatmul_int4_path(1, 4096, 14336, 64) == 1
+    assert L.tk_qmatmul_int4_path(1, 4800, 14336, 48) == 0
+    assert L.tk_qmatmul_int4_path(1, 4096, 14335, 64) == -1
+    assert L.tk_qmatmul_int4_path(1, 100, 64, 8) == -1
+
+
+def test_null_arguments_rejected():
+    L = _lib.lib()
+    assert L.tk_device_create(0, None) == _lib.TK_ERR_ARG
+    assert L.tk_qmatmul_int4(None, None, None, None, None, None, 1, 64, 32, 8) == _lib.TK_ERR_ARG
+    assert b"NULL" in L.tk_last_error_string()

@@ -1,0 +1,650 @@
+// tk_runtime.cu -- the C ABI of include/tk_cuda.h: device, buffers, scratch, dispatch.
+//
+// Replaces the reference's Metal runtime (src/metal/device.zig, src/metal/objc.zig) with a
+// CUDA device context: one stream per device, a scratch arena for the engine (activation
+// records, split-K partials, tile counters, grid barrier, error word) and a cache of TMA
+// tensor maps keyed by weight pointer.  Entry points validate their arguments (the
+// reference validates none) and report errors as negative status codes.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tk_cuda.h"
+#include "tk_engine.h"
+#include "tk_internal.h"
+
+using namespace tk;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+#define TK_CUDA_TRY(expr)                                                                     \
+  do {                                                                                        \
+    cudaError_t e__ = (expr);                                                                 \
+    if (e__ != cudaSuccess)                                                                   \
+      return fail(TK_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e__), __FILE__, \
+                  __LINE__);                                                                  \
+  } while (0)
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+std::once_flag g_encode_once;
+
+struct ScratchBuf {
+  void* ptr = nullptr;
+  size_t cap = 0;
+};
+
+struct TmapEntry {
+  const void* base;
+  uint64_t cols, rows;
+  CUtensorMap map;
+};
+
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // 2 s per bounded wait
+
+}  // namespace
+
+struct tk_device {
+  int ordinal = 0;
+  cudaStream_t stream = nullptr;
+  cudaDeviceProp prop{};
+  char name[256] = {0};
+  int sm_count = 0;
+  int smem_optin = 0;
+  unsigned long long timeout_ns = kDefaultTimeoutNs;
+  int stages_override = 0;
+  GridBar* bar = nullptr;
+  unsigned* err = nullptr;
+  ScratchBuf frag[2];
+  ScratchBuf partials[2];
+  ScratchBuf counters[2];
+  std::vector<TmapEntry> tmaps;
+};
+
+namespace {
+
+int set_device(tk_device* d) {
+  TK_CUDA_TRY(cudaSetDevice(d->ordinal));
+  return TK_OK;
+}
+
+cudaStream_t pick_stream(tk_device* d, void* stream) {
+  return stream ? static_cast<cudaStream_t>(stream) : d->stream;
+}
+
+// Grows a scratch buffer; new memory is zeroed (tile counters must start at zero).
+int scratch_ensure(tk_device* d, ScratchBuf& b, size_t need) {
+  if (b.cap >= need) return TK_OK;
+  TK_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  TK_CUDA_TRY(cudaDeviceSynchronize());
+  if (b.ptr) TK_CUDA_TRY(cudaFree(b.ptr));
+  b.ptr = nullptr;
+  b.cap = 0;
+  size_t cap = std::max<size_t>(need, 4096);
+  TK_CUDA_TRY(cudaMalloc(&b.ptr, cap));
+  TK_CUDA_TRY(cudaMemset(b.ptr, 0, cap));
+  b.cap = cap;
+  return TK_OK;
+}
+
+int get_encoder() {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode_tiled) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  return TK_OK;
+}
+
+// 2-D u8 tensor map over packed weights [rows = K/2][cols = N bytes], box 128 B x 8 rows,
+// 128-byte swizzle (bank-conflict-free 16 B fragment loads in the engine).
+int weight_tmap(tk_device* d, const void* base, uint64_t cols, uint64_t rows, CUtensorMap* out) {
+  for (auto& e : d->tmaps)
+    if (e.base == base && e.cols == cols && e.rows == rows) {
+      *out = e.map;
+      return TK_OK;
+    }
+  int st = get_encoder();
+  if (st != TK_OK) return st;
+  TmapEntry e;
+  e.base = base;
+  e.cols = cols;
+  e.rows = rows;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {(cuuint32_t)kTileCols, (cuuint32_t)kStepRows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(&e.map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base),
+                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  if (d->tmaps.size() >= 256) d->tmaps.erase(d->tmaps.begin());
+  d->tmaps.push_back(e);
+  *out = e.map;
+  return TK_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_qshape(uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
+  if (m == 0 || k == 0 || n == 0 || gs == 0) return fail(TK_ERR_ARG, "zero dimension");
+  if (gs % 8 != 0) return fail(TK_ERR_ARG, "group_size %u is not a multiple of 8", gs);
+  if (k % gs != 0) return fail(TK_ERR_ARG, "k=%u is not a multiple of group_size=%u", k, gs);
+  if (n % 2 != 0) return fail(TK_ERR_ARG, "n=%u is odd (zero points pack two columns per byte)", n);
+  if ((uint64_t)m * k > (1ull << 31) || (uint64_t)k * n > (1ull << 33))
+    return fail(TK_ERR_ARG, "shape too large");
+  return TK_OK;
+}
+
+bool engine_shape(uint32_t k, uint32_t n, uint32_t gs) {
+  return n % kTileCols == 0 && k % kTileCols == 0 &&
+         (gs == 16 || gs == 32 || gs == 64 || gs == 128);
+}
+
+int mt_for(uint32_t m) { return m <= 1 ? 1 : (m <= 2 ? 2 : 4); }
+
+long long warp_of_unit_h(long long u, long long units, long long W) {
+  return ((u + 1) * W - 1) / units;
+}
+
+int max_segments(const PhaseParams& P, long long Wtot) {
+  const long long W = std::min<long long>(Wtot, P.units);
+  const long long per = (long long)P.groups * P.spg;
+  int mx = 1;
+  for (long long cu = 0; cu < (long long)P.tiles * P.nmat; ++cu) {
+    const long long a = cu * per;
+    const int ns = (int)(warp_of_unit_h(a + per - 1, P.units, W) - warp_of_unit_h(a, P.units, W) + 1);
+    mx = std::max(mx, ns);
+  }
+  return mx;
+}
+
+void fill_phase(PhaseParams& P, int K, int N, int gs, int nmat, int mt) {
+  std::memset(&P, 0, sizeof(P));
+  P.K = K;
+  P.N = N;
+  P.gs = gs;
+  P.nmat = nmat;
+  P.spg = gs / 16;
+  P.groups = K / gs;
+  P.tiles = N / kTileCols;
+  P.units = (long long)P.tiles * nmat * P.groups * P.spg;
+  P.frag_bytes = frag_record_bytes(P.spg, mt);
+}
+
+// Sizes the split-K scratch of phase `idx` and points P at it.
+int bind_phase_scratch(tk_device* d, PhaseParams& P, int idx, int mt, long long Wtot) {
+  P.maxseg = max_segments(P, Wtot);
+  const size_t pbytes = (size_t)P.tiles * P.nmat * P.maxseg * mt * kTileCols * sizeof(float);
+  int st = scratch_ensure(d, d->partials[idx], pbytes);
+  if (st != TK_OK) return st;
+  st = scratch_ensure(d, d->counters[idx], (size_t)P.tiles * sizeof(unsigned));
+  if (st != TK_OK) return st;
+  P.partials = static_cast<float*>(d->partials[idx].ptr);
+  P.counters = static_cast<unsigned*>(d->counters[idx].ptr);
+  return TK_OK;
+}
+
+int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, cudaStream_t st) {
+  const int spg_max = std::max(p.ph[0].spg, p.nphases > 1 ? p.ph[1].spg : 0);
+  int fb_max = std::max(p.ph[0].frag_bytes, p.nphases > 1 ? p.ph[1].frag_bytes : 0);
+  p.tile_stage_bytes = spg_max * kStepBytes;
+  p.aux_stage_bytes = (kScaleBytes + kZeroBytes + fb_max + 15) & ~15;
+  int stages = d->stages_override > 0 ? d->stages_override : 4;
+  while (stages > 2 &&
+         engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes) > (size_t)d->smem_optin - 2048)
+    --stages;
+  size_t smem = engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes);
+  if (smem > (size_t)d->smem_optin - 2048)
+    return fail(TK_ERR_UNSUPPORTED, "engine ring does not fit in shared memory");
+  p.stages = stages;
+  p.bar = d->bar;
+  p.err = d->err;
+  p.timeout_ns = d->timeout_ns;
+  int blocks = 0;
+  TK_CUDA_TRY(engine_occupancy(mt, smem, &blocks));
+  if (blocks < 1) return fail(TK_ERR_UNSUPPORTED, "engine kernel cannot be resident");
+  TK_CUDA_TRY(engine_launch(mt, maps, p, d->sm_count, smem, st));
+  return TK_OK;
+}
+
+int sync_and_check(tk_device* d, cudaStream_t st) {
+  TK_CUDA_TRY(cudaStreamSynchronize(st));
+  return tk_device_check_error(d);
+}
+
+// One engine launch for <= 4 rows of qmatmul_int4.
+int qmatmul_engine_chunk(tk_device* d, const float* x, const uint8_t* w, const uint16_t* s,
+                         const uint8_t* z, float* out, int m, int k, int n, int gs,
+                         cudaStream_t st) {
+  const int mt = mt_for(m);
+  const long long Wtot = (long long)d->sm_count * engine_warps_per_cta();
+  EngineParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.m = m;
+  p.nphases = 1;
+  PhaseParams& P = p.ph[0];
+  fill_phase(P, k, n, gs, 1, mt);
+  P.map_base = 0;
+  P.scales[0] = s;
+  P.zeros[0] = z;
+  int stt = scratch_ensure(d, d->frag[0], (size_t)P.groups * P.frag_bytes);
+  if (stt != TK_OK) return stt;
+  P.frag_in = static_cast<const uint8_t*>(d->frag[0].ptr);
+  stt = bind_phase_scratch(d, P, 0, mt, Wtot);
+  if (stt != TK_OK) return stt;
+  P.epi = kEpiStore;
+  P.out = out;
+  P.ldo = n;
+  p.x = x;
+  p.ldx = k;
+  p.K0 = k;
+  p.do_norm = 0;
+  p.frag0 = static_cast<uint8_t*>(d->frag[0].ptr);
+  p.gs0 = gs;
+  p.frag0_bytes = P.frag_bytes;
+  TmapPack maps;
+  std::memset(&maps, 0, sizeof(maps));
+  stt = weight_tmap(d, w, n, k / 2, &maps.map[0]);
+  if (stt != TK_OK) return stt;
+  return launch_engine(d, mt, maps, p, st);
+}
+
+int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk_int4_matrix* gate,
+                     const tk_int4_matrix* up, const tk_int4_matrix* down, float* out,
+                     float* h_out, int m, int hidden, int inter, int gs, float eps, bool residual,
+                     cudaStream_t st) {
+  const int mt = mt_for(m);
+  const long long Wtot = (long long)d->sm_count * engine_warps_per_cta();
+  EngineParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.m = m;
+  p.nphases = 2;
+  PhaseParams& A = p.ph[0];
+  PhaseParams& B = p.ph[1];
+  fill_phase(A, hidden, inter, gs, 2, mt);
+  fill_phase(B, inter, hidden, gs, 1, mt);
+  A.map_base = 0;
+  A.scales[0] = gate->scales;
+  A.scales[1] = up->scales;
+  A.zeros[0] = gate->zeros;
+  A.zeros[1] = up->zeros;
+  B.map_base = 2;
+  B.scales[0] = down->scales;
+  B.zeros[0] = down->zeros;
+  int stt = scratch_ensure(d, d->frag[0], (size_t)A.groups * A.frag_bytes);
+  if (stt != TK_OK) return stt;
+  stt = scratch_ensure(d, d->frag[1], (size_t)B.groups * B.frag_bytes);
+  if (stt != TK_OK) return stt;
+  A.frag_in = static_cast<const uint8_t*>(d->frag[0].ptr);
+  B.frag_in = static_cast<const uint8_t*>(d->frag[1].ptr);
+  stt = bind_phase_scratch(d, A, 0, mt, Wtot);
+  if (stt != TK_OK) return stt;
+  stt = bind_phase_scratch(d, B, 1, mt, Wtot);
+  if (stt != TK_OK) return stt;
+  A.epi = kEpiSiluMul;
+  A.out = h_out;
+  A.ldo = inter;
+  A.frag_out = static_cast<uint8_t*>(d->frag[1].ptr);
+  A.next_gs = gs;
+  A.next_frag_bytes = B.frag_bytes;
+  B.epi = kEpiStore;
+  B.out = out;
+  B.ldo = hidden;
+  B.residual = residual ? x : nullptr;
+  B.ldr = hidden;
+  p.x = x;
+  p.ldx = hidden;
+  p.K0 = hidden;
+  p.norm_w = norm_w;
+  p.eps = eps;
+  p.do_norm = 1;
+  p.frag0 = static_cast<uint8_t*>(d->frag[0].ptr);
+  p.gs0 = gs;
+  p.frag0_bytes = A.frag_bytes;
+  TmapPack maps;
+  std::memset(&maps, 0, sizeof(maps));
+  stt = weight_tmap(d, gate->w_packed, inter, hidden / 2, &maps.map[0]);
+  if (stt != TK_OK) return stt;
+  stt = weight_tmap(d, up->w_packed, inter, hidden / 2, &maps.map[1]);
+  if (stt != TK_OK) return stt;
+  stt = weight_tmap(d, down->w_packed, hidden, inter / 2, &maps.map[2]);
+  if (stt != TK_OK) return stt;
+  return launch_engine(d, mt, maps, p, st);
+}
+
+bool matrix_aligned(const tk_int4_matrix* a) {
+  return a && aligned16(a->w_packed) && aligned16(a->scales) && aligned16(a->zeros);
+}
+
+}  // namespace
+
+extern "C" {
+
+int tk_abi_version(void) { return TK_ABI_VERSION; }
+
+const char* tk_last_error_string(void) { return g_last_error.c_str(); }
+
+const char* tk_status_string(int status) {
+  switch (status) {
+    case TK_OK: return "ok";
+    case TK_ERR_ARG: return "invalid argument";
+    case TK_ERR_CUDA: return "CUDA error";
+    case TK_ERR_NCCL: return "NCCL error";
+    case TK_ERR_TIMEOUT: return "device-side wait timed out";
+    case TK_ERR_UNSUPPORTED: return "unsupported";
+    case TK_ERR_NOMEM: return "out of memory";
+    default: return "unknown status";
+  }
+}
+
+int tk_device_create(int ordinal, tk_device** out) {
+  if (!out) return fail(TK_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0)
+    return fail(TK_ERR_CUDA, "no CUDA device: %s", cudaGetErrorString(e));
+  if (ordinal < 0 || ordinal >= count) return fail(TK_ERR_ARG, "device ordinal %d out of range", ordinal);
+  tk_device* d = new tk_device();
+  d->ordinal = ordinal;
+  auto cleanup = [&](int st) {
+    tk_device_destroy(d);
+    return st;
+  };
+  if (cudaSetDevice(ordinal) != cudaSuccess) return cleanup(fail(TK_ERR_CUDA, "cudaSetDevice failed"));
+  if (cudaGetDeviceProperties(&d->prop, ordinal) != cudaSuccess)
+    return cleanup(fail(TK_ERR_CUDA, "cudaGetDeviceProperties failed"));
+  if (d->prop.major < 10)
+    return cleanup(fail(TK_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", ordinal,
+                        d->prop.major, d->prop.minor));
+  std::snprintf(d->name, sizeof(d->name), "%s", d->prop.name);
+  d->sm_count = d->prop.multiProcessorCount;
+  d->smem_optin = (int)d->prop.sharedMemPerBlockOptin;
+  if (const char* env = std::getenv("TK_ENGINE_STAGES")) d->stages_override = std::atoi(env);
+  if (const char* env = std::getenv("TK_WAIT_TIMEOUT_MS"))
+    d->timeout_ns = (unsigned long long)std::atoll(env) * 1000000ull;
+  if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return cleanup(fail(TK_ERR_CUDA, "cudaStreamCreate failed"));
+  if (cudaMalloc(&d->bar, sizeof(GridBar)) != cudaSuccess ||
+      cudaMalloc(&d->err, 256) != cudaSuccess)
+    return cleanup(fail(TK_ERR_NOMEM, "scratch allocation failed"));
+  if (cudaMemset(d->bar, 0, sizeof(GridBar)) != cudaSuccess || cudaMemset(d->err, 0, 256) != cudaSuccess)
+    return cleanup(fail(TK_ERR_CUDA, "scratch init failed"));
+  *out = d;
+  return TK_OK;
+}
+
+void tk_device_destroy(tk_device* d) {
+  if (!d) return;
+  cudaSetDevice(d->ordinal);
+  if (d->stream) cudaStreamSynchronize(d->stream);
+  for (auto* b : {&d->frag[0], &d->frag[1], &d->partials[0], &d->partials[1], &d->counters[0],
+                  &d->counters[1]})
+    if (b->ptr) cudaFree(b->ptr);
+  if (d->bar) cudaFree(d->bar);
+  if (d->err) cudaFree(d->err);
+  if (d->stream) cudaStreamDestroy(d->stream);
+  delete d;
+}
+
+const char* tk_device_name(tk_device* d) { return d ? d->name : ""; }
+int tk_device_sm_count(tk_device* d) { return d ? d->sm_count : 0; }
+void* tk_device_stream(tk_device* d) { return d ? static_cast<void*>(d->stream) : nullptr; }
+
+int tk_device_synchronize(tk_device* d) {
+  if (!d) return fail(TK_ERR_ARG, "device is NULL");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
+int tk_device_check_error(tk_device* d) {
+  if (!d) return fail(TK_ERR_ARG, "device is NULL");
+  unsigned h = 0;
+  TK_CUDA_TRY(cudaMemcpy(&h, d->err, sizeof(h), cudaMemcpyDeviceToHost));
+  if (h == 0) return TK_OK;
+  // Clear the error word and return the engine's scratch to its launch-ready state.
+  TK_CUDA_TRY(cudaDeviceSynchronize());
+  TK_CUDA_TRY(cudaMemset(d->err, 0, 256));
+  TK_CUDA_TRY(cudaMemset(d->bar, 0, sizeof(GridBar)));
+  for (auto* b : {&d->counters[0], &d->counters[1]})
+    if (b->ptr) TK_CUDA_TRY(cudaMemset(b->ptr, 0, b->cap));
+  return fail(TK_ERR_TIMEOUT, "device-side bounded wait gave up (error bits 0x%x)", h);
+}
+
+int tk_buffer_alloc(tk_device* d, size_t bytes, int kind, void** ptr) {
+  if (!d || !ptr) return fail(TK_ERR_ARG, "NULL argument");
+  *ptr = nullptr;
+  if (bytes == 0) bytes = 16;
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  cudaError_t e;
+  switch (kind) {
+    case TK_MEM_DEVICE: e = cudaMalloc(ptr, bytes); break;
+    case TK_MEM_SHARED: e = cudaMallocManaged(ptr, bytes); break;
+    case TK_MEM_HOST: e = cudaMallocHost(ptr, bytes); break;
+    default: return fail(TK_ERR_ARG, "unknown buffer kind %d", kind);
+  }
+  if (e != cudaSuccess) return fail(TK_ERR_NOMEM, "allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+  return TK_OK;
+}
+
+int tk_buffer_free(tk_device* d, void* ptr) {
+  if (!d) return fail(TK_ERR_ARG, "device is NULL");
+  if (!ptr) return TK_OK;
+  cudaPointerAttributes a;
+  TK_CUDA_TRY(cudaPointerGetAttributes(&a, ptr));
+  if (a.type == cudaMemoryTypeHost) TK_CUDA_TRY(cudaFreeHost(ptr));
+  else TK_CUDA_TRY(cudaFree(ptr));
+  return TK_OK;
+}
+
+int tk_buffer_upload(tk_device* d, void* dst, const void* src, size_t bytes) {
+  if (!d || (!dst && bytes) || (!src && bytes)) return fail(TK_ERR_ARG, "NULL argument");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, d->stream));
+  TK_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  return TK_OK;
+}
+
+int tk_buffer_download(tk_device* d, void* dst, const void* src, size_t bytes) {
+  if (!d || (!dst && bytes) || (!src && bytes)) return fail(TK_ERR_ARG, "NULL argument");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, d->stream));
+  TK_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  return TK_OK;
+}
+
+int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
+  if (m == 0 || k == 0 || n == 0 || gs == 0 || gs % 8 || k % gs || n % 2) return -1;
+  return engine_shape(k, n, gs) ? 1 : 0;
+}
+
+int tk_qmatmul_int4_async(tk_device* d, const float* x, const uint8_t* w, const uint16_t* s,
+                          const uint8_t* z, float* out, uint32_t m, uint32_t k, uint32_t n,
+                          uint32_t gs, void* stream) {
+  if (!d || !x || !w || !s || !z || !out) return fail(TK_ERR_ARG, "NULL argument");
+  int st = check_qshape(m, k, n, gs);
+  if (st != TK_OK) return st;
+  st = set_device(d);
+  if (st != TK_OK) return st;
+  cudaStream_t cs = pick_stream(d, stream);
+  const bool fast = engine_shape(k, n, gs) && aligned16(x) && aligned16(w) && aligned16(s) &&
+                    aligned16(z) && aligned16(out);
+  if (!fast) {
+    TK_CUDA_TRY(launch_qmatmul_int4_generic(x, w, s, z, out, (int)m, (int)k, (int)n, (int)gs, cs));
+    return TK_OK;
+  }
+  for (uint32_t r = 0; r < m; r += 4) {
+    const uint32_t mm = std::min<uint32_t>(4, m - r);
+    st = qmatmul_engine_chunk(d, x + (size_t)r * k, w, s, z, out + (size_t)r * n, (int)mm, (int)k,
+                              (int)n, (int)gs, cs);
+    if (st != TK_OK) return st;
+  }
+  return TK_OK;
+}
+
+int tk_qmatmul_int4(tk_device* d, const float* x, const uint8_t* w, const uint16_t* s,
+                    const uint8_t* z, float* out, uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
+  int st = tk_qmatmul_int4_async(d, x, w, s, z, out, m, k, n, gs, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
+int tk_dequant_int4(tk_device* d, const uint8_t* w, const uint16_t* s, const uint8_t* z,
+                    float* out, uint32_t k, uint32_t n, uint32_t gs) {
+  if (!d || !w || !s || !z || !out) return fail(TK_ERR_ARG, "NULL argument");
+  int st = check_qshape(1, k, n, gs);
+  if (st != TK_OK) return st;
+  st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(launch_dequant_int4(w, s, z, out, (int)k, (int)n, (int)gs, d->stream));
+  return sync_and_check(d, d->stream);
+}
+
+int tk_rmsnorm_async(tk_device* d, const float* x, const float* w, float* out, uint32_t rows,
+                     uint32_t dim, float eps, void* stream) {
+  if (!d || !x || !w || !out) return fail(TK_ERR_ARG, "NULL argument");
+  if (rows == 0 || dim == 0) return fail(TK_ERR_ARG, "zero dimension");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(launch_rmsnorm(x, w, out, (int)rows, (int)dim, eps, pick_stream(d, stream)));
+  return TK_OK;
+}
+
+int tk_rmsnorm(tk_device* d, const float* x, const float* w, float* out, uint32_t rows,
+               uint32_t dim, float eps) {
+  int st = tk_rmsnorm_async(d, x, w, out, rows, dim, eps, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
+int tk_fused_rmsnorm_rope_async(tk_device* d, const float* x, const float* w, const float* cosc,
+                                const float* sinc, float* out, uint32_t rows, uint32_t dim,
+                                uint32_t head_dim, uint32_t pos, float eps, void* stream) {
+  if (!d || !x || !w || !cosc || !sinc || !out) return fail(TK_ERR_ARG, "NULL argument");
+  if (rows == 0 || dim == 0 || head_dim == 0 || head_dim % 2 || dim % head_dim)
+    return fail(TK_ERR_ARG, "dim=%u must be a positive multiple of an even head_dim=%u", dim, head_dim);
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(launch_fused_rmsnorm_rope(x, w, cosc, sinc, out, (int)rows, (int)dim, (int)head_dim,
+                                        (int)pos, eps, pick_stream(d, stream)));
+  return TK_OK;
+}
+
+int tk_fused_rmsnorm_rope(tk_device* d, const float* x, const float* w, const float* cosc,
+                          const float* sinc, float* out, uint32_t rows, uint32_t dim,
+                          uint32_t head_dim, uint32_t pos, float eps) {
+  int st = tk_fused_rmsnorm_rope_async(d, x, w, cosc, sinc, out, rows, dim, head_dim, pos, eps, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
+int tk_silu_mul_async(tk_device* d, const float* g, const float* u, float* out, uint32_t n,
+                      void* stream) {
+  if (!d || !g || !u || !out) return fail(TK_ERR_ARG, "NULL argument");
+  if (n == 0) return TK_OK;
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(launch_silu_mul(g, u, out, (int)n, pick_stream(d, stream)));
+  return TK_OK;
+}
+
+int tk_silu_mul(tk_device* d, const float* g, const float* u, float* out, uint32_t n) {
+  int st = tk_silu_mul_async(d, g, u, out, n, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
+int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const tk_int4_matrix* gate,
+                      const tk_int4_matrix* up, const tk_int4_matrix* down, float* out,
+                      float* h_out, uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs,
+                      float eps, uint32_t flags, void* stream) {
+  if (!d || !x || !norm_w || !gate || !up || !down || !out) return fail(TK_ERR_ARG, "NULL argument");
+  for (const tk_int4_matrix* a : {gate, up, down})
+    if (!a->w_packed || !a->scales || !a->zeros) return fail(TK_ERR_ARG, "NULL matrix pointer");
+  int st = check_qshape(m, hidden, inter, gs);
+  if (st != TK_OK) return st;
+  st = check_qshape(m, inter, hidden, gs);
+  if (st != TK_OK) return st;
+  if (flags & ~TK_FFN_RESIDUAL) return fail(TK_ERR_ARG, "unknown flags 0x%x", flags);
+  st = set_device(d);
+  if (st != TK_OK) return st;
+  cudaStream_t cs = pick_stream(d, stream);
+  const bool residual = (flags & TK_FFN_RESIDUAL) != 0;
+  const bool fast = engine_shape(hidden, inter, gs) && engine_shape(inter, hidden, gs) &&
+                    aligned16(x) && aligned16(norm_w) && aligned16(out) &&
+                    (!h_out || aligned16(h_out)) && matrix_aligned(gate) && matrix_aligned(up) &&
+                    matrix_aligned(down);
+  if (fast) {
+    for (uint32_t r = 0; r < m; r += 4) {
+      const uint32_t mm = std::min<uint32_t>(4, m - r);
+      st = ffn_engine_chunk(d, x + (size_t)r * hidden, norm_w, gate, up, down,
+                            out + (size_t)r * hidden, h_out ? h_out + (size_t)r * inter : nullptr,
+                            (int)mm, (int)hidden, (int)inter, (int)gs, eps, residual, cs);
+      if (st != TK_OK) return st;
+    }
+    return TK_OK;
+  }
+  // CUDA-core composition for shapes the engine does not take.
+  float *normed = nullptr, *g = nullptr, *u = nullptr, *h = nullptr, *y = nullptr;
+  const size_t mh = (size_t)m * hidden, mi = (size_t)m * inter;
+  TK_CUDA_TRY(cudaMallocAsync(&normed, mh * 4, cs));
+  TK_CUDA_TRY(cudaMallocAsync(&g, mi * 4, cs));
+  TK_CUDA_TRY(cudaMallocAsync(&u, mi * 4, cs));
+  TK_CUDA_TRY(cudaMallocAsync(&h, mi * 4, cs));
+  TK_CUDA_TRY(cudaMallocAsync(&y, mh * 4, cs));
+  TK_CUDA_TRY(launch_rmsnorm(x, norm_w, normed, (int)m, (int)hidden, eps, cs));
+  TK_CUDA_TRY(launch_qmatmul_int4_generic(normed, gate->w_packed, gate->scales, gate->zeros, g, (int)m,
+                                          (int)hidden, (int)inter, (int)gs, cs));
+  TK_CUDA_TRY(launch_qmatmul_int4_generic(normed, up->w_packed, up->scales, up->zeros, u, (int)m,
+                                          (int)hidden, (int)inter, (int)gs, cs));
+  TK_CUDA_TRY(launch_silu_mul(g, u, h, (int)mi, cs));
+  if (h_out) TK_CUDA_TRY(cudaMemcpyAsync(h_out, h, mi * 4, cudaMemcpyDeviceToDevice, cs));
+  TK_CUDA_TRY(launch_qmatmul_int4_generic(h, down->w_packed, down->scales, down->zeros, y, (int)m,
+                                          (int)inter, (int)hidden, (int)gs, cs));
+  if (residual) TK_CUDA_TRY(launch_add(x, y, out, (int)mh, cs));
+  else TK_CUDA_TRY(cudaMemcpyAsync(out, y, mh * 4, cudaMemcpyDeviceToDevice, cs));
+  for (float* p : {normed, g, u, h, y}) TK_CUDA_TRY(cudaFreeAsync(p, cs));
+  return TK_OK;
+}
+
+int tk_int4_ffn(tk_device* d, const float* x, const float* norm_w, const tk_int4_matrix* gate,
+                const tk_int4_matrix* up, const tk_int4_matrix* down, float* out, float* h_out,
+                uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs, float eps,
+                uint32_t flags) {
+  int st = tk_int4_ffn_async(d, x, norm_w, gate, up, down, out, h_out, m, hidden, inter, gs, eps,
+                             flags, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,173 @@
+// tk_simple.cu -- CUDA-core kernels for the small ops of the path and the fallback GEMV.
+//
+//  * qmatmul_int4_generic: any legal qmatmul_int4 shape (k % group == 0, group % 8 == 0,
+//    n even).  One thread per output column; accumulates in exactly the order of the
+//    reference shader (src/kernels/shaders.zig:481-497): acc += (x * scale) * (q - zero),
+//    k ascending, with no FMA contraction, so it matches the f32 oracle bit for bit.
+//  * dequant_int4: the test hook for dequantisation bit-exactness (shaders.zig:474-495).
+//  * rmsnorm, fused_rmsnorm_rope, silu_mul, add: shaders.zig:16-56, 124-182, 344-357,
+//    812-824; one CTA per row for the reductions.
+#include <cuda_fp16.h>
+
+#include "tk_internal.h"
+
+namespace tk {
+namespace {
+
+__global__ void qmatmul_int4_generic_kernel(const float* __restrict__ x,
+                                            const uint8_t* __restrict__ w,
+                                            const __half* __restrict__ s,
+                                            const uint8_t* __restrict__ z, float* __restrict__ out,
+                                            int k, int n, int gs) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = blockIdx.y;
+  if (col >= n) return;
+  const float* xr = x + (size_t)row * k;
+  const int shift = (col & 1) * 4;
+  const int ng = k / gs;
+  float acc = 0.0f;
+  for (int g = 0; g < ng; ++g) {
+    const float scale = __half2float(s[(size_t)g * n + col]);
+    const float fz = (float)((z[(size_t)g * (n / 2) + col / 2] >> shift) & 15);
+    for (int i = 0; i < gs; i += 2) {
+      const int kk = g * gs + i;
+      const uint32_t p = w[(size_t)(kk / 2) * n + col];
+      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(xr[kk], scale), __fsub_rn((float)(p & 15u), fz)));
+      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(xr[kk + 1], scale), __fsub_rn((float)(p >> 4), fz)));
+    }
+  }
+  out[(size_t)row * n + col] = acc;
+}
+
+__global__ void dequant_int4_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ s,
+                                    const uint8_t* __restrict__ z, float* __restrict__ out, int k,
+                                    int n, int gs) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  const int kp = blockIdx.y;  // packed row = k pair
+  if (col >= n) return;
+  const int kk = 2 * kp;
+  const int g = kk / gs;
+  const float scale = __half2float(s[(size_t)g * n + col]);
+  const float fz = (float)((z[(size_t)g * (n / 2) + col / 2] >> ((col & 1) * 4)) & 15);
+  const uint32_t p = w[(size_t)kp * n + col];
+  out[(size_t)kk * n + col] = __fmul_rn(scale, __fsub_rn((float)(p & 15u), fz));
+  out[(size_t)(kk + 1) * n + col] = __fmul_rn(scale, __fsub_rn((float)(p >> 4), fz));
+}
+
+// Block-wide sum, deterministic: warp shuffles then the warps' partials in order.
+__device__ float block_sum(float v, float* red) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float tot = 0.0f;
+  const int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; ++i) tot += red[i];
+  __syncthreads();
+  return tot;
+}
+
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               float* __restrict__ out, int dim, float eps) {
+  __shared__ float red[32];
+  const size_t off = (size_t)blockIdx.x * dim;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float v = x[off + i];
+    ss = fmaf(v, v, ss);
+  }
+  const float tot = block_sum(ss, red);
+  const float rms = rsqrtf(tot / (float)dim + eps);
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) out[off + i] = x[off + i] * rms * w[i];
+}
+
+__global__ void fused_rmsnorm_rope_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                          const float* __restrict__ cosc,
+                                          const float* __restrict__ sinc, float* __restrict__ out,
+                                          int dim, int head_dim, int pos, float eps) {
+  __shared__ float red[32];
+  const size_t off = (size_t)blockIdx.x * dim;
+  const int half_head = head_dim / 2;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float v = x[off + i];
+    ss = fmaf(v, v, ss);
+  }
+  const float tot = block_sum(ss, red);
+  const float rms = rsqrtf(tot / (float)dim + eps);
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float normed = x[off + i] * rms * w[i];
+    const int ph = i % head_dim;
+    if (ph < half_head) {
+      const float pair = x[off + i + half_head] * rms * w[i + half_head];
+      const float c = cosc[(size_t)pos * half_head + ph];
+      const float s = sinc[(size_t)pos * half_head + ph];
+      out[off + i] = normed * c - pair * s;
+    } else {
+      const float pair = x[off + i - half_head] * rms * w[i - half_head];
+      const int fi = ph - half_head;
+      const float c = cosc[(size_t)pos * half_head + fi];
+      const float s = sinc[(size_t)pos * half_head + fi];
+      out[off + i] = normed * c + pair * s;
+    }
+  }
+}
+
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                                float* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float gv = g[i];
+  out[i] = gv / (1.0f + expf(-gv)) * u[i];
+}
+
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                           float* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  out[i] = a[i] + b[i];
+}
+
+}  // namespace
+
+cudaError_t launch_qmatmul_int4_generic(const float* x, const uint8_t* w, const uint16_t* s,
+                                        const uint8_t* z, float* out, int m, int k, int n,
+                                        int gs, cudaStream_t st) {
+  dim3 grid((n + 127) / 128, m);
+  qmatmul_int4_generic_kernel<<<grid, 128, 0, st>>>(x, w, reinterpret_cast<const __half*>(s), z,
+                                                    out, k, n, gs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_int4(const uint8_t* w, const uint16_t* s, const uint8_t* z,
+                                float* out, int k, int n, int gs, cudaStream_t st) {
+  dim3 grid((n + 127) / 128, k / 2);
+  dequant_int4_kernel<<<grid, 128, 0, st>>>(w, reinterpret_cast<const __half*>(s), z, out, k, n,
+                                            gs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int rows, int dim,
+                           float eps, cudaStream_t st) {
+  rmsnorm_kernel<<<rows, 256, 0, st>>>(x, w, out, dim, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fused_rmsnorm_rope(const float* x, const float* w, const float* cosc,
+                                      const float* sinc, float* out, int rows, int dim,
+                                      int head_dim, int pos, float eps, cudaStream_t st) {
+  fused_rmsnorm_rope_kernel<<<rows, 256, 0, st>>>(x, w, cosc, sinc, out, dim, head_dim, pos, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu_mul(const float* g, const float* u, float* out, int n, cudaStream_t st) {
+  silu_mul_kernel<<<(n + 255) / 256, 256, 0, st>>>(g, u, out, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add(const float* a, const float* b, float* out, int n, cudaStream_t st) {
+  add_kernel<<<(n + 255) / 256, 256, 0, st>>>(a, b, out, n);
+  return cudaGetLastError();
+}
+
+}  // namespace tk

@@ -1,0 +1,104 @@
+"""ctypes binding of libtkcuda (include/tk_cuda.h).
+
+Loads the in-tree ``lib/libtkcuda.so`` built by the package Makefile.  There is no
+fallback: if the library is missing, every call raises, so a GPU run can never pass on
+a CPU or library stand-in.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get(
+    "TK_LIB_PATH", os.path.join(os.path.dirname(_HERE), "lib", "libtkcuda.so"))
+
+TK_OK = 0
+TK_ERR_ARG = -1
+TK_ERR_CUDA = -2
+TK_ERR_NCCL = -3
+TK_ERR_TIMEOUT = -4
+TK_ERR_UNSUPPORTED = -5
+TK_ERR_NOMEM = -6
+
+TK_MEM_DEVICE = 0
+TK_MEM_SHARED = 1
+TK_MEM_HOST = 2
+
+TK_FFN_RESIDUAL = 1
+
+vp = C.c_void_p
+u32 = C.c_uint32
+f32 = C.c_float
+i32 = C.c_int
+
+
+class Int4MatrixC(C.Structure):
+    """tk_int4_matrix: device pointers of one packed INT4 matrix."""
+    _fields_ = [("w_packed", vp), ("scales", vp), ("zeros", vp)]
+
+
+# name -> (restype, argtypes); the exported surface of include/tk_cuda.h
+SIGNATURES = {
+    "tk_abi_version": (i32, []),
+    "tk_last_error_string": (C.c_char_p, []),
+    "tk_status_string": (C.c_char_p, [i32]),
+    "tk_device_create": (i32, [i32, C.POINTER(vp)]),
+    "tk_device_destroy": (None, [vp]),
+    "tk_device_name": (C.c_char_p, [vp]),
+    "tk_device_sm_count": (i32, [vp]),
+    "tk_device_stream": (vp, [vp]),
+    "tk_device_synchronize": (i32, [vp]),
+    "tk_device_check_error": (i32, [vp]),
+    "tk_buffer_alloc": (i32, [vp, C.c_size_t, i32, C.POINTER(vp)]),
+    "tk_buffer_free": (i32, [vp, vp]),
+    "tk_buffer_upload": (i32, [vp, vp, vp, C.c_size_t]),
+    "tk_buffer_download": (i32, [vp, vp, vp, C.c_size_t]),
+    "tk_qmatmul_int4": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),
+    "tk_qmatmul_int4_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
+    "tk_qmatmul_int4_path": (i32, [u32, u32, u32, u32]),
+    "tk_rmsnorm": (i32, [vp, vp, vp, vp, u32, u32, f32]),
+    "tk_rmsnorm_async": (i32, [vp, vp, vp, vp, u32, u32, f32, vp]),
+    "tk_fused_rmsnorm_rope": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, f32]),
+    "tk_fused_rmsnorm_rope_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, f32, vp]),
+    "tk_silu_mul": (i32, [vp, vp, vp, vp, u32]),
+    "tk_silu_mul_async": (i32, [vp, vp, vp, vp, u32, vp]),
+    "tk_int4_ffn": (i32, [vp, vp, vp, C.POINTER(Int4MatrixC), C.POINTER(Int4MatrixC),
+                          C.POINTER(Int4MatrixC), vp, vp, u32, u32, u32, u32, f32, u32]),
+    "tk_int4_ffn_async": (i32, [vp, vp, vp, C.POINTER(Int4MatrixC), C.POINTER(Int4MatrixC),
+                                C.POINTER(Int4MatrixC), vp, vp, u32, u32, u32, u32, f32, u32,
+                                vp]),
+    "tk_dequant_int4": (i32, [vp, vp, vp, vp, vp, u32, u32, u32]),
+}
+
+
+class TKError(RuntimeError):
+    """A negative status returned by libtkcuda."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{message} (status {status})")
+        self.status = status
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded library (raises OSError if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"libtkcuda is not built: {LIB_PATH} (run `make -C tiny-kernel_b200`)")
+        handle = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != TK_OK:
+        msg = lib().tk_last_error_string()
+        raise TKError(status, msg.decode() if msg else "libtkcuda error")
