@@ -167,6 +167,16 @@ int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *sca
                     const uint8_t *zeros, float *out, uint32_t k, uint32_t n,
                     uint32_t group_size);
 
+/* ---- profiling ---------------------------------------------------------------------
+ * Device-side event trace of the engine (the reference times with a wall clock only,
+ * src/bench.zig:4-15).  When enabled, every engine launch overwrites a buffer of
+ * sm_count * TK_TRACE_EVENTS global-timer stamps (ns) per CTA: start, prologue done,
+ * phase-0 barrier passed, phase-0 items done, phase-1 barrier passed, phase-1 items done,
+ * end, producer first issue, producer last issue, first stage landed (0 = not reached). */
+#define TK_TRACE_EVENTS 10
+int tk_device_trace_enable(tk_device *dev, int enable);
+int tk_device_trace_read(tk_device *dev, uint64_t *out, size_t max_values, size_t *n_values);
+
 /* Which path tk_qmatmul_int4 / tk_int4_ffn would take for a shape:
  * 1 = tensor-core engine, 0 = CUDA-core fallback, <0 = invalid shape. */
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t group_size);

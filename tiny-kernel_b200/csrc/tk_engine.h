@@ -2,30 +2,44 @@
 //
 // The engine runs one or two "phases" of INT4 fused-dequant GEMV in one persistent,
 // cooperative launch (one CTA per SM):
-//   qmatmul_int4 (src/kernels/shaders.zig:442-501):   prologue(x -> fragments) | phase 0
-//   INT4 FFN (src/bench.zig:266-341 + down proj):     prologue(rmsnorm(x) -> fragments) |
+//   qmatmul_int4 (src/kernels/shaders.zig:442-501):   prologue(x -> records) | phase 0
+//   INT4 FFN (src/bench.zig:266-341 + down proj):     prologue(rmsnorm(x) -> records) |
 //                                                     phase 0 gate+up -> silu*up -> h |
 //                                                     phase 1 down (+ residual)
-// Work unit = one k-step (16 k values = 8 packed rows) of one 128-column tile of one
-// matrix; each warp owns a contiguous range of k-steps (stream-K), partial sums of a
-// tile are reduced deterministically (in warp order) by the last warp to finish it.
+// Work unit = one k-step (16 k values = 8 packed rows) of a 1024-column wide tile of one
+// matrix; each CTA owns a contiguous range of units (stream-K) and its 8 consumer warps
+// take one 128-column slice each.  Partial sums of a 128-column sub-tile are reduced
+// deterministically (in CTA order) by the last warp to finish it.  There is no grid-wide
+// barrier: every CTA builds its own phase-0 activation records, and a phase-1 record is
+// consumed only after its producer sub-tile has published a ready flag for this launch.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
 
 namespace tk {
 
-constexpr int kTileCols = 128;   // output columns per tile == bytes per packed row slice
+constexpr int kTileCols = 128;   // output columns per slice == bytes per packed row slice
+constexpr int kSlices = 8;       // slices per wide tile == consumer warps per CTA
+constexpr int kWideCols = kTileCols * kSlices;  // 1024 columns per wide tile
 constexpr int kStepRows = 8;     // packed rows (k pairs) per k-step
-constexpr int kStepBytes = 1024; // one k-step of one tile: 8 rows x 128 B (TMA box)
+// A wide tile's packed row is read as one 1040-byte TMA box row (130 u64): 1024 payload
+// bytes plus 16 bytes of the next tile, so consecutive rows land 16 bytes apart modulo
+// 128 in shared memory and the fragment loads are bank-conflict free.
+constexpr int kRowBytes = 1040;
+constexpr int kRowElems = kRowBytes / 8;  // u64 elements per box row
 constexpr int kMaxPhases = 2;
 constexpr int kMaxMats = 2;
-constexpr int kScaleBytes = kTileCols * 2;  // f16 scales of one tile, one group
-constexpr int kZeroBytes = kTileCols / 2;   // packed zero points of one tile, one group
+constexpr int kScaleBytes = kTileCols * 2;  // f16 scales of one slice, one group
+constexpr int kZeroBytes = kTileCols / 2;   // packed zero points of one slice, one group
+
+// Device-side event trace (per CTA, global-timer ns), written when EngineParams.trace
+// is set: start, prologue done, (unused), phase-0 items done, (unused), phase-1 items
+// done, end, producer first issue, producer last issue, first stage landed.
+constexpr int kTraceEvents = 10;
 
 // error bits written to the device error word
 constexpr unsigned kErrTmaWait = 1u;
-constexpr unsigned kErrGridBarrier = 2u;
+constexpr unsigned kErrFlagWait = 2u;
 
 // One group's activation record: the B-operand fragments of the m16n8k16 MMA for every
 // k-step of the group, followed by per-step metadata:
@@ -41,10 +55,11 @@ enum EpilogueKind : int {
   kEpiSiluMul = 1,  // h = silu(mat0) * mat1 -> optional h out + next phase's records
 };
 
-struct GridBar {
-  unsigned count;
+// Launch-to-launch synchronisation state (device memory, zeroed once).
+struct SyncState {
+  unsigned epoch;  // launches completed; ready flags of launch E carry E + 1
   unsigned pad0[31];
-  unsigned gen;
+  unsigned done;   // CTAs finished in the current launch
   unsigned pad1[31];
 };
 
@@ -52,15 +67,17 @@ struct PhaseParams {
   int K, N, gs, nmat;
   int spg;      // k-steps per group = gs / 16
   int groups;   // K / gs
-  int tiles;    // N / 128
+  int tiles;    // wide tiles: ceil(N / 1024); the last may have fewer than 8 slices
   long long units;  // tiles * nmat * groups * spg
-  int map_base;     // tensor map index of matrix 0 in TmapPack
+  int map_base;     // tensor maps of matrix i: map[map_base + 2i] (group box), +1 (step box)
   const uint16_t* scales[kMaxMats];
   const uint8_t* zeros[kMaxMats];
-  const uint8_t* frag_in;  // activation records, one per group of K
+  const uint8_t* frag_in;     // activation records, one per group of K
+  long long frag_cta_stride;  // bytes between CTAs' private copies (0: one shared copy)
   int frag_bytes;
-  float* partials;         // [tiles*nmat][maxseg][MT][128]
-  unsigned* counters;      // [tiles], zero between launches
+  const unsigned* ready_in;   // per 128-value sub-tile of K: record ready when == epoch + 1
+  float* partials;         // [tiles*nmat][maxseg][kSlices][MT][128]
+  unsigned* counters;      // [N / 128] per sub-tile, zero between launches
   int maxseg;
   int epi;
   float* out;              // kEpiStore: y; kEpiSiluMul: optional h
@@ -68,6 +85,7 @@ struct PhaseParams {
   const float* residual;   // kEpiStore: optional
   int ldr;
   uint8_t* frag_out;       // kEpiSiluMul: records for the next phase
+  unsigned* ready_out;     // kEpiSiluMul: per 128-column sub-tile flags
   int next_gs;
   int next_frag_bytes;
 };
@@ -76,7 +94,8 @@ struct EngineParams {
   int m;        // live tokens (rows of x), <= MT of the instantiation
   int nphases;
   PhaseParams ph[kMaxPhases];
-  // prologue: x[m][K0] (optionally rmsnorm'ed) -> records frag0 with group size gs0
+  // prologue: every CTA turns x[m][K0] (optionally rmsnorm'ed) into its own records at
+  // frag0 + blockIdx.x * frag0_cta_stride, group size gs0
   const float* x;
   int ldx;
   int K0;
@@ -84,6 +103,7 @@ struct EngineParams {
   float eps;
   int do_norm;
   uint8_t* frag0;
+  long long frag0_cta_stride;
   int gs0;
   int frag0_bytes;
   // shared-memory ring
@@ -91,13 +111,14 @@ struct EngineParams {
   int tile_stage_bytes;
   int aux_stage_bytes;
   // sync + errors
-  GridBar* bar;
+  unsigned long long* trace;  // optional [gridDim.x][kTraceEvents] globaltimer stamps
+  SyncState* sync;
   unsigned* err;
   unsigned long long timeout_ns;
 };
 
 struct TmapPack {
-  CUtensorMap map[3];
+  CUtensorMap map[6];  // per matrix: group-box map, step-box map
 };
 
 }  // namespace tk

@@ -57,6 +57,7 @@ struct ScratchBuf {
 struct TmapEntry {
   const void* base;
   uint64_t cols, rows;
+  uint32_t box_rows;
   CUtensorMap map;
 };
 
@@ -73,11 +74,13 @@ struct tk_device {
   int smem_optin = 0;
   unsigned long long timeout_ns = kDefaultTimeoutNs;
   int stages_override = 0;
-  GridBar* bar = nullptr;
+  SyncState* sync = nullptr;
   unsigned* err = nullptr;
   ScratchBuf frag[2];
   ScratchBuf partials[2];
   ScratchBuf counters[2];
+  ScratchBuf ready;  // per 128-column sub-tile flags of the FFN intermediate
+  unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   std::vector<TmapEntry> tmaps;
 };
 
@@ -120,11 +123,13 @@ int get_encoder() {
   return TK_OK;
 }
 
-// 2-D u8 tensor map over packed weights [rows = K/2][cols = N bytes], box 128 B x 8 rows,
-// 128-byte swizzle (bank-conflict-free 16 B fragment loads in the engine).
-int weight_tmap(tk_device* d, const void* base, uint64_t cols, uint64_t rows, CUtensorMap* out) {
+// 2-D tensor map over packed weights [rows = K/2][cols = N bytes] viewed as u64 elements;
+// box = 130 u64 (a 1040-byte row: one 1024-column wide tile + 16 bytes) x box_rows rows,
+// no swizzle (rows land 16 bytes apart modulo 128 in shared memory).  Cached per pointer.
+int weight_tmap(tk_device* d, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows,
+                CUtensorMap* out) {
   for (auto& e : d->tmaps)
-    if (e.base == base && e.cols == cols && e.rows == rows) {
+    if (e.base == base && e.cols == cols && e.rows == rows && e.box_rows == box_rows) {
       *out = e.map;
       return TK_OK;
     }
@@ -134,19 +139,28 @@ int weight_tmap(tk_device* d, const void* base, uint64_t cols, uint64_t rows, CU
   e.base = base;
   e.cols = cols;
   e.rows = rows;
-  cuuint64_t dims[2] = {cols, rows};
+  e.box_rows = box_rows;
+  cuuint64_t dims[2] = {cols / 8, rows};
   cuuint64_t strides[1] = {cols};
-  cuuint32_t box[2] = {(cuuint32_t)kTileCols, (cuuint32_t)kStepRows};
+  cuuint32_t box[2] = {(cuuint32_t)kRowElems, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode_tiled(&e.map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base),
+  CUresult r = g_encode_tiled(&e.map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base),
                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  if (d->tmaps.size() >= 256) d->tmaps.erase(d->tmaps.begin());
+  if (d->tmaps.size() >= 512) d->tmaps.erase(d->tmaps.begin());
   d->tmaps.push_back(e);
   *out = e.map;
   return TK_OK;
+}
+
+// Both tensor maps of one matrix (group box and k-step box) into maps[idx], maps[idx + 1].
+int matrix_tmaps(tk_device* d, const void* w, uint64_t n, uint64_t k, int gs, TmapPack& maps,
+                 int idx) {
+  int st = weight_tmap(d, w, n, k / 2, (uint32_t)(gs / 2), &maps.map[idx]);
+  if (st != TK_OK) return st;
+  return weight_tmap(d, w, n, k / 2, (uint32_t)kStepRows, &maps.map[idx + 1]);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -172,6 +186,7 @@ long long warp_of_unit_h(long long u, long long units, long long W) {
   return ((u + 1) * W - 1) / units;
 }
 
+// Largest number of CTA ranges that intersect one column unit (wide tile x matrix).
 int max_segments(const PhaseParams& P, long long Wtot) {
   const long long W = std::min<long long>(Wtot, P.units);
   const long long per = (long long)P.groups * P.spg;
@@ -192,7 +207,7 @@ void fill_phase(PhaseParams& P, int K, int N, int gs, int nmat, int mt) {
   P.nmat = nmat;
   P.spg = gs / 16;
   P.groups = K / gs;
-  P.tiles = N / kTileCols;
+  P.tiles = (N + kWideCols - 1) / kWideCols;
   P.units = (long long)P.tiles * nmat * P.groups * P.spg;
   P.frag_bytes = frag_record_bytes(P.spg, mt);
 }
@@ -200,10 +215,11 @@ void fill_phase(PhaseParams& P, int K, int N, int gs, int nmat, int mt) {
 // Sizes the split-K scratch of phase `idx` and points P at it.
 int bind_phase_scratch(tk_device* d, PhaseParams& P, int idx, int mt, long long Wtot) {
   P.maxseg = max_segments(P, Wtot);
-  const size_t pbytes = (size_t)P.tiles * P.nmat * P.maxseg * mt * kTileCols * sizeof(float);
+  const size_t pbytes =
+      (size_t)P.tiles * P.nmat * P.maxseg * kSlices * mt * kTileCols * sizeof(float);
   int st = scratch_ensure(d, d->partials[idx], pbytes);
   if (st != TK_OK) return st;
-  st = scratch_ensure(d, d->counters[idx], (size_t)P.tiles * sizeof(unsigned));
+  st = scratch_ensure(d, d->counters[idx], (size_t)(P.N / kTileCols) * sizeof(unsigned));
   if (st != TK_OK) return st;
   P.partials = static_cast<float*>(d->partials[idx].ptr);
   P.counters = static_cast<unsigned*>(d->counters[idx].ptr);
@@ -213,9 +229,9 @@ int bind_phase_scratch(tk_device* d, PhaseParams& P, int idx, int mt, long long 
 int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, cudaStream_t st) {
   const int spg_max = std::max(p.ph[0].spg, p.nphases > 1 ? p.ph[1].spg : 0);
   int fb_max = std::max(p.ph[0].frag_bytes, p.nphases > 1 ? p.ph[1].frag_bytes : 0);
-  p.tile_stage_bytes = spg_max * kStepBytes;
-  p.aux_stage_bytes = (kScaleBytes + kZeroBytes + fb_max + 15) & ~15;
-  int stages = d->stages_override > 0 ? d->stages_override : 4;
+  p.tile_stage_bytes = (spg_max * kStepRows * kRowBytes + 127) & ~127;
+  p.aux_stage_bytes = (kSlices * (kScaleBytes + kZeroBytes) + fb_max + 15) & ~15;
+  int stages = d->stages_override > 0 ? d->stages_override : 5;
   while (stages > 2 &&
          engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes) > (size_t)d->smem_optin - 2048)
     --stages;
@@ -223,7 +239,10 @@ int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, c
   if (smem > (size_t)d->smem_optin - 2048)
     return fail(TK_ERR_UNSUPPORTED, "engine ring does not fit in shared memory");
   p.stages = stages;
-  p.bar = d->bar;
+  p.trace = d->trace;
+  if (d->trace)
+    TK_CUDA_TRY(cudaMemsetAsync(d->trace, 0, (size_t)d->sm_count * kTraceEvents * 8, st));
+  p.sync = d->sync;
   p.err = d->err;
   p.timeout_ns = d->timeout_ns;
   int blocks = 0;
@@ -243,7 +262,7 @@ int qmatmul_engine_chunk(tk_device* d, const float* x, const uint8_t* w, const u
                          const uint8_t* z, float* out, int m, int k, int n, int gs,
                          cudaStream_t st) {
   const int mt = mt_for(m);
-  const long long Wtot = (long long)d->sm_count * engine_warps_per_cta();
+  const long long Wtot = d->sm_count;  // one CTA per SM; stream-K ranges are per CTA
   EngineParams p;
   std::memset(&p, 0, sizeof(p));
   p.m = m;
@@ -253,9 +272,11 @@ int qmatmul_engine_chunk(tk_device* d, const float* x, const uint8_t* w, const u
   P.map_base = 0;
   P.scales[0] = s;
   P.zeros[0] = z;
-  int stt = scratch_ensure(d, d->frag[0], (size_t)P.groups * P.frag_bytes);
+  const long long rec_stride = (long long)P.groups * P.frag_bytes;  // per-CTA records
+  int stt = scratch_ensure(d, d->frag[0], (size_t)Wtot * rec_stride);
   if (stt != TK_OK) return stt;
   P.frag_in = static_cast<const uint8_t*>(d->frag[0].ptr);
+  P.frag_cta_stride = rec_stride;
   stt = bind_phase_scratch(d, P, 0, mt, Wtot);
   if (stt != TK_OK) return stt;
   P.epi = kEpiStore;
@@ -266,11 +287,12 @@ int qmatmul_engine_chunk(tk_device* d, const float* x, const uint8_t* w, const u
   p.K0 = k;
   p.do_norm = 0;
   p.frag0 = static_cast<uint8_t*>(d->frag[0].ptr);
+  p.frag0_cta_stride = rec_stride;
   p.gs0 = gs;
   p.frag0_bytes = P.frag_bytes;
   TmapPack maps;
   std::memset(&maps, 0, sizeof(maps));
-  stt = weight_tmap(d, w, n, k / 2, &maps.map[0]);
+  stt = matrix_tmaps(d, w, n, k, gs, maps, 0);
   if (stt != TK_OK) return stt;
   return launch_engine(d, mt, maps, p, st);
 }
@@ -280,7 +302,7 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
                      float* h_out, int m, int hidden, int inter, int gs, float eps, bool residual,
                      cudaStream_t st) {
   const int mt = mt_for(m);
-  const long long Wtot = (long long)d->sm_count * engine_warps_per_cta();
+  const long long Wtot = d->sm_count;  // one CTA per SM; stream-K ranges are per CTA
   EngineParams p;
   std::memset(&p, 0, sizeof(p));
   p.m = m;
@@ -289,20 +311,25 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   PhaseParams& B = p.ph[1];
   fill_phase(A, hidden, inter, gs, 2, mt);
   fill_phase(B, inter, hidden, gs, 1, mt);
-  A.map_base = 0;
+  A.map_base = 0;  // gate: maps 0,1; up: maps 2,3
   A.scales[0] = gate->scales;
   A.scales[1] = up->scales;
   A.zeros[0] = gate->zeros;
   A.zeros[1] = up->zeros;
-  B.map_base = 2;
+  B.map_base = 4;  // down: maps 4,5
   B.scales[0] = down->scales;
   B.zeros[0] = down->zeros;
-  int stt = scratch_ensure(d, d->frag[0], (size_t)A.groups * A.frag_bytes);
+  const long long rec_stride = (long long)A.groups * A.frag_bytes;  // per-CTA records
+  int stt = scratch_ensure(d, d->frag[0], (size_t)Wtot * rec_stride);
   if (stt != TK_OK) return stt;
   stt = scratch_ensure(d, d->frag[1], (size_t)B.groups * B.frag_bytes);
   if (stt != TK_OK) return stt;
+  stt = scratch_ensure(d, d->ready, (size_t)(inter / kTileCols) * sizeof(unsigned));
+  if (stt != TK_OK) return stt;
   A.frag_in = static_cast<const uint8_t*>(d->frag[0].ptr);
+  A.frag_cta_stride = rec_stride;
   B.frag_in = static_cast<const uint8_t*>(d->frag[1].ptr);
+  B.ready_in = static_cast<const unsigned*>(d->ready.ptr);
   stt = bind_phase_scratch(d, A, 0, mt, Wtot);
   if (stt != TK_OK) return stt;
   stt = bind_phase_scratch(d, B, 1, mt, Wtot);
@@ -311,6 +338,7 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   A.out = h_out;
   A.ldo = inter;
   A.frag_out = static_cast<uint8_t*>(d->frag[1].ptr);
+  A.ready_out = static_cast<unsigned*>(d->ready.ptr);
   A.next_gs = gs;
   A.next_frag_bytes = B.frag_bytes;
   B.epi = kEpiStore;
@@ -325,15 +353,16 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   p.eps = eps;
   p.do_norm = 1;
   p.frag0 = static_cast<uint8_t*>(d->frag[0].ptr);
+  p.frag0_cta_stride = rec_stride;
   p.gs0 = gs;
   p.frag0_bytes = A.frag_bytes;
   TmapPack maps;
   std::memset(&maps, 0, sizeof(maps));
-  stt = weight_tmap(d, gate->w_packed, inter, hidden / 2, &maps.map[0]);
+  stt = matrix_tmaps(d, gate->w_packed, inter, hidden, gs, maps, 0);
   if (stt != TK_OK) return stt;
-  stt = weight_tmap(d, up->w_packed, inter, hidden / 2, &maps.map[1]);
+  stt = matrix_tmaps(d, up->w_packed, inter, hidden, gs, maps, 2);
   if (stt != TK_OK) return stt;
-  stt = weight_tmap(d, down->w_packed, hidden, inter / 2, &maps.map[2]);
+  stt = matrix_tmaps(d, down->w_packed, hidden, inter, gs, maps, 4);
   if (stt != TK_OK) return stt;
   return launch_engine(d, mt, maps, p, st);
 }
@@ -391,10 +420,10 @@ int tk_device_create(int ordinal, tk_device** out) {
     d->timeout_ns = (unsigned long long)std::atoll(env) * 1000000ull;
   if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
     return cleanup(fail(TK_ERR_CUDA, "cudaStreamCreate failed"));
-  if (cudaMalloc(&d->bar, sizeof(GridBar)) != cudaSuccess ||
+  if (cudaMalloc(&d->sync, sizeof(SyncState)) != cudaSuccess ||
       cudaMalloc(&d->err, 256) != cudaSuccess)
     return cleanup(fail(TK_ERR_NOMEM, "scratch allocation failed"));
-  if (cudaMemset(d->bar, 0, sizeof(GridBar)) != cudaSuccess || cudaMemset(d->err, 0, 256) != cudaSuccess)
+  if (cudaMemset(d->sync, 0, sizeof(SyncState)) != cudaSuccess || cudaMemset(d->err, 0, 256) != cudaSuccess)
     return cleanup(fail(TK_ERR_CUDA, "scratch init failed"));
   *out = d;
   return TK_OK;
@@ -405,10 +434,11 @@ void tk_device_destroy(tk_device* d) {
   cudaSetDevice(d->ordinal);
   if (d->stream) cudaStreamSynchronize(d->stream);
   for (auto* b : {&d->frag[0], &d->frag[1], &d->partials[0], &d->partials[1], &d->counters[0],
-                  &d->counters[1]})
+                  &d->counters[1], &d->ready})
     if (b->ptr) cudaFree(b->ptr);
-  if (d->bar) cudaFree(d->bar);
+  if (d->sync) cudaFree(d->sync);
   if (d->err) cudaFree(d->err);
+  if (d->trace) cudaFree(d->trace);
   if (d->stream) cudaStreamDestroy(d->stream);
   delete d;
 }
@@ -432,10 +462,38 @@ int tk_device_check_error(tk_device* d) {
   // Clear the error word and return the engine's scratch to its launch-ready state.
   TK_CUDA_TRY(cudaDeviceSynchronize());
   TK_CUDA_TRY(cudaMemset(d->err, 0, 256));
-  TK_CUDA_TRY(cudaMemset(d->bar, 0, sizeof(GridBar)));
-  for (auto* b : {&d->counters[0], &d->counters[1]})
+  TK_CUDA_TRY(cudaMemset(d->sync, 0, sizeof(SyncState)));
+  for (auto* b : {&d->counters[0], &d->counters[1], &d->ready})
     if (b->ptr) TK_CUDA_TRY(cudaMemset(b->ptr, 0, b->cap));
   return fail(TK_ERR_TIMEOUT, "device-side bounded wait gave up (error bits 0x%x)", h);
+}
+
+int tk_device_trace_enable(tk_device* d, int enable) {
+  if (!d) return fail(TK_ERR_ARG, "device is NULL");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  if (enable && !d->trace) {
+    TK_CUDA_TRY(cudaDeviceSynchronize());
+    TK_CUDA_TRY(cudaMalloc(&d->trace, (size_t)d->sm_count * kTraceEvents * 8));
+    TK_CUDA_TRY(cudaMemset(d->trace, 0, (size_t)d->sm_count * kTraceEvents * 8));
+  } else if (!enable && d->trace) {
+    TK_CUDA_TRY(cudaDeviceSynchronize());
+    TK_CUDA_TRY(cudaFree(d->trace));
+    d->trace = nullptr;
+  }
+  return TK_OK;
+}
+
+int tk_device_trace_read(tk_device* d, uint64_t* out, size_t max_values, size_t* n_values) {
+  if (!d || !out) return fail(TK_ERR_ARG, "NULL argument");
+  if (!d->trace) return fail(TK_ERR_ARG, "tracing is not enabled");
+  const size_t n = std::min(max_values, (size_t)d->sm_count * kTraceEvents);
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  TK_CUDA_TRY(cudaMemcpy(out, d->trace, n * 8, cudaMemcpyDeviceToHost));
+  if (n_values) *n_values = n;
+  return TK_OK;
 }
 
 int tk_buffer_alloc(tk_device* d, size_t bytes, int kind, void** ptr) {

@@ -69,6 +69,8 @@ SIGNATURES = {
                                 C.POINTER(Int4MatrixC), vp, vp, u32, u32, u32, u32, f32, u32,
                                 vp]),
     "tk_dequant_int4": (i32, [vp, vp, vp, vp, vp, u32, u32, u32]),
+    "tk_device_trace_enable": (i32, [vp, i32]),
+    "tk_device_trace_read": (i32, [vp, vp, C.c_size_t, C.POINTER(C.c_size_t)]),
 }
 
 
