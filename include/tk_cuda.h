@@ -177,6 +177,28 @@ int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *sca
 int tk_device_trace_enable(tk_device *dev, int enable);
 int tk_device_trace_read(tk_device *dev, uint64_t *out, size_t max_values, size_t *n_values);
 
+/* ---- allocation-free qmatmul_int4 ---------------------------------------------------
+ * No counterpart in the reference (its Metal buffers are always created by the caller
+ * through Device.createBuffer; nothing on its path allocates scratch).
+ *
+ * For callers that cannot call cudaMalloc: a process whose device memory is reserved up
+ * front by its own allocator, a latency-critical loop that must not take cudaMalloc's
+ * device-wide synchronisation, or a binding that cannot own a tk_device.  Same contract
+ * as tk_qmatmul_int4 (same layout, shapes, errors and results), on the calling thread's
+ * current CUDA device and on `stream` (NULL = the legacy default stream), synchronous.
+ * It allocates nothing: the engine's scratch is one static device array of
+ * TK_NOALLOC_SCRATCH_BYTES per GPU that loads the library, held until the process exits.
+ *  - A shape whose scratch would exceed that size fails with TK_ERR_ARG (config 0,
+ *    m=1 k=4096 n=14336 group 64, needs about 3.5 MB); use tk_qmatmul_int4 for those.
+ *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
+ *    make that first call before any stream capture.
+ *  - Every call shares the one array and clears its counters on entry: calls that overlap
+ *    on the GPU (other threads, other streams) race and must be serialised by the caller. */
+#define TK_NOALLOC_SCRATCH_BYTES (4u << 20)
+int tk_qmatmul_int4_noalloc(const float *x, const uint8_t *w_packed, const uint16_t *scales,
+                            const uint8_t *zeros, float *out, uint32_t m, uint32_t k,
+                            uint32_t n, uint32_t group_size, void *stream);
+
 /* Which path tk_qmatmul_int4 / tk_int4_ffn would take for a shape:
  * 1 = tensor-core engine, 0 = CUDA-core fallback, <0 = invalid shape. */
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t group_size);

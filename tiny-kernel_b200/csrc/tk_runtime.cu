@@ -706,3 +706,176 @@ int tk_int4_ffn(tk_device* d, const float* x, const float* norm_w, const tk_int4
 }
 
 }  // extern "C"
+
+// ---- qmatmul_int4 without any allocation ------------------------------------------------
+//
+// Some callers cannot call cudaMalloc: a host whose device memory is entirely reserved up
+// front by its own allocator (an inference server's memory pool, a framework arena), a
+// latency-critical loop where cudaMalloc's implicit device-wide synchronisation is not
+// acceptable, or a foreign-language binding that cannot own a tk_device and its arena.
+// tk_qmatmul_int4_noalloc serves them: the engine's scratch (split-K partials, tile
+// counters, activation records, launch state and error word) lives in the file-scope
+// array below instead of in buffers the device context allocates.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // TK_NOALLOC_SCRATCH_BYTES
+constexpr int kNoAllocMaxDevices = 64;
+
+// One copy per GPU that loads this library, held until the process exits.  In host code
+// `g_noalloc_scratch` is only a host-side stand-in for the symbol: its device address comes
+// from cudaGetSymbolAddress (noalloc_scratch below) and is what the kernel is given.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device (set up once per device).
+int noalloc_scratch(int ordinal, unsigned char** out) {
+  if (ordinal < 0 || ordinal >= kNoAllocMaxDevices)
+    return fail(TK_ERR_UNSUPPORTED, "device ordinal %d is beyond the %d devices supported", ordinal,
+                kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[ordinal]) {
+    void* p = nullptr;
+    TK_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[ordinal] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_ptr[ordinal];
+  return TK_OK;
+}
+
+// Tensor map of one matrix's packed weights, encoded on the stack (no cache, no heap).
+int noalloc_tmap(const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows,
+                 CUtensorMap* out) {
+  int st = get_encoder();
+  if (st != TK_OK) return st;
+  cuuint64_t dims[2] = {cols / 8, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {(cuuint32_t)kRowElems, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(out, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return TK_OK;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// One engine launch (<= 4 rows) with every scratch pointer carved from `scratch`.
+int noalloc_engine_chunk(unsigned char* scratch, int sm_count, int smem_optin, const float* x,
+                         const uint8_t* w, const uint16_t* s, const uint8_t* z, float* out, int m,
+                         int k, int n, int gs, cudaStream_t st) {
+  const int mt = mt_for(m);
+  const long long Wtot = sm_count;
+  EngineParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.m = m;
+  p.nphases = 1;
+  PhaseParams& P = p.ph[0];
+  fill_phase(P, k, n, gs, 1, mt);
+  P.maxseg = max_segments(P, Wtot);
+  // layout: launch state | error word | tile counters | partials | per-CTA records
+  const size_t off_err = align256(sizeof(SyncState));
+  const size_t off_cnt = off_err + 256;
+  const size_t off_part = off_cnt + align256((size_t)(n / kTileCols) * sizeof(unsigned));
+  const size_t part_bytes =
+      (size_t)P.tiles * P.nmat * P.maxseg * kSlices * mt * kTileCols * sizeof(float);
+  const size_t off_rec = off_part + align256(part_bytes);
+  const long long rec_stride = (long long)P.groups * P.frag_bytes;
+  const size_t need = off_rec + (size_t)Wtot * rec_stride;
+  if (need > kNoAllocScratchBytes)
+    return fail(TK_ERR_ARG,
+                "m=%d k=%d n=%d group_size=%d needs %zu bytes of scratch; the allocation-free "
+                "entry point has %zu (use tk_qmatmul_int4)",
+                m, k, n, gs, need, kNoAllocScratchBytes);
+  // the launch state, error word and tile counters must start at zero; the partials and
+  // records are written before they are read
+  TK_CUDA_TRY(cudaMemsetAsync(scratch, 0, off_part, st));
+  P.map_base = 0;
+  P.scales[0] = s;
+  P.zeros[0] = z;
+  P.frag_in = scratch + off_rec;
+  P.frag_cta_stride = rec_stride;
+  P.partials = reinterpret_cast<float*>(scratch + off_part);
+  P.counters = reinterpret_cast<unsigned*>(scratch + off_cnt);
+  P.epi = kEpiStore;
+  P.out = out;
+  P.ldo = n;
+  p.x = x;
+  p.ldx = k;
+  p.K0 = k;
+  p.do_norm = 0;
+  p.frag0 = scratch + off_rec;
+  p.frag0_cta_stride = rec_stride;
+  p.gs0 = gs;
+  p.frag0_bytes = P.frag_bytes;
+  TmapPack maps;
+  std::memset(&maps, 0, sizeof(maps));
+  int stt = noalloc_tmap(w, n, k / 2, (uint32_t)(gs / 2), &maps.map[0]);
+  if (stt != TK_OK) return stt;
+  stt = noalloc_tmap(w, n, k / 2, (uint32_t)kStepRows, &maps.map[1]);
+  if (stt != TK_OK) return stt;
+  p.tile_stage_bytes = (P.spg * kStepRows * kRowBytes + 127) & ~127;
+  p.aux_stage_bytes = (kSlices * (kScaleBytes + kZeroBytes) + P.frag_bytes + 15) & ~15;
+  int stages = 5;
+  while (stages > 2 &&
+         engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes) > (size_t)smem_optin - 2048)
+    --stages;
+  const size_t smem = engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes);
+  if (smem > (size_t)smem_optin - 2048)
+    return fail(TK_ERR_UNSUPPORTED, "engine ring does not fit in shared memory");
+  p.stages = stages;
+  p.trace = nullptr;
+  p.sync = reinterpret_cast<SyncState*>(scratch);
+  p.err = reinterpret_cast<unsigned*>(scratch + off_err);
+  p.timeout_ns = kDefaultTimeoutNs;
+  int blocks = 0;
+  TK_CUDA_TRY(engine_occupancy(mt, smem, &blocks));
+  if (blocks < 1) return fail(TK_ERR_UNSUPPORTED, "engine kernel cannot be resident");
+  TK_CUDA_TRY(engine_launch(mt, maps, p, sm_count, smem, st));
+  return TK_OK;
+}
+
+}  // namespace
+
+extern "C" int tk_qmatmul_int4_noalloc(const float* x, const uint8_t* w, const uint16_t* s,
+                                       const uint8_t* z, float* out, uint32_t m, uint32_t k,
+                                       uint32_t n, uint32_t gs, void* stream) {
+  if (!x || !w || !s || !z || !out) return fail(TK_ERR_ARG, "NULL argument");
+  int st = check_qshape(m, k, n, gs);
+  if (st != TK_OK) return st;
+  int ordinal = 0;
+  TK_CUDA_TRY(cudaGetDevice(&ordinal));
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  const bool fast = engine_shape(k, n, gs) && aligned16(x) && aligned16(w) && aligned16(s) &&
+                    aligned16(z) && aligned16(out);
+  if (!fast) {
+    // the CUDA-core kernel these shapes take uses no scratch at all
+    TK_CUDA_TRY(launch_qmatmul_int4_generic(x, w, s, z, out, (int)m, (int)k, (int)n, (int)gs, cs));
+    TK_CUDA_TRY(cudaStreamSynchronize(cs));
+    return TK_OK;
+  }
+  unsigned char* scratch = nullptr;
+  st = noalloc_scratch(ordinal, &scratch);
+  if (st != TK_OK) return st;
+  int sm_count = 0, smem_optin = 0, major = 0;
+  TK_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, ordinal));
+  if (major < 10) return fail(TK_ERR_UNSUPPORTED, "device %d is not sm_100a", ordinal);
+  TK_CUDA_TRY(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, ordinal));
+  TK_CUDA_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ordinal));
+  for (uint32_t r = 0; r < m; r += 4) {
+    const uint32_t mm = std::min<uint32_t>(4, m - r);
+    st = noalloc_engine_chunk(scratch, sm_count, smem_optin, x + (size_t)r * k, w, s, z,
+                              out + (size_t)r * n, (int)mm, (int)k, (int)n, (int)gs, cs);
+    if (st != TK_OK) return st;
+  }
+  TK_CUDA_TRY(cudaStreamSynchronize(cs));
+  // the error word sits right after the launch state (see noalloc_engine_chunk)
+  unsigned h = 0;
+  TK_CUDA_TRY(cudaMemcpy(&h, scratch + align256(sizeof(SyncState)), sizeof(h),
+                         cudaMemcpyDeviceToHost));
+  if (h != 0) return fail(TK_ERR_TIMEOUT, "device-side bounded wait gave up (error bits 0x%x)", h);
+  return TK_OK;
+}

@@ -57,6 +57,7 @@ SIGNATURES = {
     "tk_qmatmul_int4": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),
     "tk_qmatmul_int4_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
     "tk_qmatmul_int4_path": (i32, [u32, u32, u32, u32]),
+    "tk_qmatmul_int4_noalloc": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
     "tk_rmsnorm": (i32, [vp, vp, vp, vp, u32, u32, f32]),
     "tk_rmsnorm_async": (i32, [vp, vp, vp, vp, u32, u32, f32, vp]),
     "tk_fused_rmsnorm_rope": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, f32]),
