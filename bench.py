@@ -117,25 +117,6 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def shard_ffn(W, rank, world):
-    """TP shard: gate/up columns [r*I/tp, (r+1)*I/tp), down rows (K) of the same range."""
-    from tiny_kernel.data import FFNWeights, Int4Matrix
-    if world == 1:
-        return W
-    I, gs = W.inter, W.gs
-    c0, c1 = rank * I // world, (rank + 1) * I // world
-
-    def cols(M):
-        return Int4Matrix(np.ascontiguousarray(M.w[:, c0:c1]), np.ascontiguousarray(M.s[:, c0:c1]),
-                          np.ascontiguousarray(M.z[:, c0 // 2:c1 // 2]), M.K, c1 - c0, gs)
-
-    D = W.down
-    down = Int4Matrix(np.ascontiguousarray(D.w[c0 // 2:c1 // 2]),
-                      np.ascontiguousarray(D.s[c0 // gs:c1 // gs]),
-                      np.ascontiguousarray(D.z[c0 // gs:c1 // gs]), c1 - c0, D.N, gs)
-    return FFNWeights(W.norm_w, cols(W.gate), cols(W.up), down, W.hidden, c1 - c0, gs)
-
-
 def run_reference(args, world, rank):
     """CPU transcription of the reference shaders, all host threads (rank 0 only)."""
     if rank != 0:
@@ -219,6 +200,7 @@ def main():
     import torch
     import tiny_kernel as tk
     from tiny_kernel import data, ops
+    from tiny_kernel.tp import shard_ffn
 
     torch.cuda.set_device(local)
     pg = None
