@@ -14,7 +14,7 @@ from tiny_kernel import data, ops
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-3
-PRECISION = 2e-5
+PRECISION = 7e-4  # the int8 hi/lo activation split (about 2^-15 of each group's max |x|)
 EPS = 1e-5
 
 

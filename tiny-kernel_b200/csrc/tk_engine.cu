@@ -45,7 +45,7 @@ namespace tk {
 
 namespace {
 
-constexpr int kNC = kSlices;  // consumer warps per CTA (plus one producer warp)
+constexpr int kNC = kSlices;  // consumer warps: one per 128-column slice
 
 // CTA whose stream-K range holds unit u (ranges [U*b/W, U*(b+1)/W), all non-empty)
 __device__ __forceinline__ long long cta_of_unit(long long u, long long units, long long W) {
@@ -122,11 +122,11 @@ __device__ __forceinline__ void iter_next(ItemIter& it, const EngineParams& p, l
   iter_seek(it, p, w, Wtot);
 }
 
-// Total bytes a stage receives for item `it` (box rows, scales, zeros, record).
-__device__ __forceinline__ uint32_t item_bytes(const PhaseParams& P, const ItemIter& it) {
+// Bytes the weight warp's copies bring into a stage for item `it` (box rows, scales, zeros);
+// the record warp adds the activation record (P.frag_bytes).
+__device__ __forceinline__ uint32_t item_weight_bytes(const PhaseParams& P, const ItemIter& it) {
   const int ns = active_slices(P, it.cu >> (P.nmat - 1));
-  return (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes + ns * (kScaleBytes + kZeroBytes) +
-                    P.frag_bytes);
+  return (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes + ns * (kScaleBytes + kZeroBytes));
 }
 
 // Producer lane `lane` issues its share of item `it`'s weight-side copies: lane 0 the TMA
@@ -187,105 +187,177 @@ __device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity, unsig
   return all;
 }
 
-__device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
-  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+// Row (k pair within a 32-pair block) that MMA K index kappa = 16 h + 4 t + i reads:
+// 16 h + 2 t + (i & 1) + 8 (i >> 1).  For a fixed i the 4 t values land 2 rows apart, so the
+// 16-byte loads of a quarter warp (g in {0,1}, t in 0..3) hit 8 distinct 16-byte bank slots of
+// the 1040-byte-strided stage rows.
+__device__ __forceinline__ int kappa_row(int h, int t, int i) {
+  return 16 * h + 2 * t + (i & 1) + 8 * (i >> 1);
 }
 
-// Warp-collective: lane l holds v[0..3] = values 4l..4l+3 of a 128-value activation
-// chunk of token `tok`.  Writes the B fragments and metadata of the 128/gs groups of the
-// chunk into `rec` (record of the chunk's first group).  k order inside a k-step follows
-// the A-fragment construction: MMA k index (2t, 2t+1, 2t+8, 2t+9) <-> step-local k
-// (4t, 4t+2, 4t+1, 4t+3); odd k carry an extra 1/16.
+// Warp-collective: lane l holds v[0..3] = values 4l..4l+3 of a 128-value activation chunk of
+// token `tok`.  Writes the records of the chunk's 128/gs groups into `rec` (the record of the
+// chunk's first group, records `rec_bytes` apart).  Per k pair p the MMA sees x[2p+1] against
+// the high nibble and x[2p] against the low nibble of the packed byte.  The group's values are
+// scaled by 2^e (max |x| of the group in [32, 64)) and split into int8 hi + lo / 256 parts.
 template <int MT>
 __device__ __forceinline__ void build_records(const float (&v)[4], int tok, int gs,
                                               uint8_t* rec, int rec_bytes, int lane) {
   const int gl = gs >> 2;  // lanes per group
+  // k pairs 2l and 2l + 1 of the chunk: odd k (high nibble) and even k (low nibble)
+  const float b[4] = {v[1], v[0], v[3], v[2]};
   float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
   for (int off = 1; off < gl; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  int e = 0;
-  if (mx > 0.f && mx <= 3.0e38f) {
-    int E;
-    frexpf(mx, &E);
-    e = 14 - E;  // max |x * 2^e| in [2^13, 2^14)
-    e = e < -100 ? -100 : (e > 100 ? 100 : e);
+  // e with max |x| * 2^e in [32, 64): from the exponent field (subnormal or zero maxima and
+  // non-finite values are clamped to the range the scale stays a normal power of two in)
+  int e = 6 - ((int)((__float_as_uint(mx) >> 23) & 0xffu) - 126);
+  e = e < -100 ? -100 : (e > 100 ? 100 : e);
+  const float up = __uint_as_float((uint32_t)(127 + e) << 23);    // 2^e
+  const float down = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e
+  int hi[4], lo[4];
+  int sh = 0, sl = 0;  // sums of the hi and lo parts (zero-point term)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float w = b[i] * up;
+    hi[i] = __float2int_rn(w);
+    int l = __float2int_rn((w - (float)hi[i]) * 256.f);
+    lo[i] = l < -127 ? -127 : (l > 127 ? 127 : l);
+    sh += hi[i];
+    sl += lo[i];
   }
-  const float x0 = ldexpf(v[0], e), x1 = ldexpf(v[1], e);
-  const float x2 = ldexpf(v[2], e), x3 = ldexpf(v[3], e);
-  const float o1 = ldexpf(v[1], e - 4), o3 = ldexpf(v[3], e - 4);
-  const __half h0 = __float2half_rn(x0), h2 = __float2half_rn(x2);
-  const __half h1 = __float2half_rn(o1), h3 = __float2half_rn(o3);
-  const __half l0 = __float2half_rn(x0 - __half2float(h0));
-  const __half l2 = __float2half_rn(x2 - __half2float(h2));
-  const __half l1 = __float2half_rn(o1 - __half2float(h1));
-  const __half l3 = __float2half_rn(o3 - __half2float(h3));
-  const int gi = lane / gl, lg = lane - gi * gl;
-  const int s = lg >> 2, t = lg & 3;
-  const int spg = gs >> 4;
+  // this lane's two k pairs are bytes 2 j .. 2 j + 1 (j = (lambda >> 2) & 1) of word h of t:
+  // 16-bit pieces {odd hi, odd lo, even hi, even lo}, two per shuffle word
+  const uint32_t p_odd = (uint32_t)(hi[0] & 0xff) | ((uint32_t)(hi[2] & 0xff) << 8) |
+                         ((uint32_t)(lo[0] & 0xff) << 16) | ((uint32_t)(lo[2] & 0xff) << 24);
+  const uint32_t p_even = (uint32_t)(hi[1] & 0xff) | ((uint32_t)(hi[3] & 0xff) << 8) |
+                          ((uint32_t)(lo[1] & 0xff) << 16) | ((uint32_t)(lo[3] & 0xff) << 24);
+  const int gi = lane / gl, lg = lane - gi * gl;  // group within the chunk, lane within it
+  const int kbl = lg & 15;                        // lane within its 32-pair block
+  const int kb = lg >> 4;
+  const int t = kbl & 3, j = (kbl >> 2) & 1, h = kbl >> 3;
+  // the partner lane holds the other two bytes of the same words (none when gs == 16)
+  uint32_t q_odd = __shfl_xor_sync(0xffffffffu, p_odd, 4);
+  uint32_t q_even = __shfl_xor_sync(0xffffffffu, p_even, 4);
+  if (gl <= 4) q_odd = q_even = 0u;
   uint8_t* r = rec + (size_t)gi * rec_bytes;
-  uint2* b = reinterpret_cast<uint2*>(r);
-  b[(s * 4 + t) * 2 * MT + 2 * tok + 0] = make_uint2(pack_half2(h0, h2), pack_half2(h1, h3));
-  b[(s * 4 + t) * 2 * MT + 2 * tok + 1] = make_uint2(pack_half2(l0, l2), pack_half2(l1, l3));
-  float sum = (x0 + x1) + (x2 + x3);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-  if (t == 0) {
-    float2* meta = reinterpret_cast<float2*>(r + spg * 4 * 2 * MT * 8);
-    meta[s * MT + tok] = make_float2(sum * 0x1p-24f, ldexpf(1.0f, 24 - e));
+  if (j == 0) {
+    const uint32_t o1h = (p_odd & 0xffffu) | (q_odd << 16);
+    const uint32_t o1l = (p_odd >> 16) | (q_odd & 0xffff0000u);
+    const uint32_t o2h = (p_even & 0xffffu) | (q_even << 16);
+    const uint32_t o2l = (p_even >> 16) | (q_even & 0xffff0000u);
+    uint32_t* bh = reinterpret_cast<uint32_t*>(r) + ((kb * 4 + t) * 2 * MT + 2 * tok) * 4;
+    uint32_t* bl = bh + 4;  // the lo column of the same token
+    bh[h] = o1h;
+    bh[2 + h] = o2h;
+    bl[h] = o1l;
+    bl[2 + h] = o2l;
+    if (gs <= 32) {  // kappa half 1 is beyond the group: zero
+      bh[1] = 0u;
+      bh[3] = 0u;
+      bl[1] = 0u;
+      bl[3] = 0u;
+    }
   }
+  // per 16-k step (4 lanes): the sums of the quantised values' hi and lo parts, so the
+  // zero-point term -z * sum(x) is formed exactly from the same values the MMA sees
+  sh += __shfl_xor_sync(0xffffffffu, sh, 1);
+  sl += __shfl_xor_sync(0xffffffffu, sl, 1);
+  sh += __shfl_xor_sync(0xffffffffu, sh, 2);
+  sl += __shfl_xor_sync(0xffffffffu, sl, 2);
+  const int spg = gs >> 4;
+  const int kbg = spg >= 4 ? spg / 4 : 1;
+  int2* sums = reinterpret_cast<int2*>(r + 128 * MT * kbg);
+  if ((lg & 3) == 0) sums[(lg >> 2) * MT + tok] = make_int2(sh, sl);
+  if (lg == 0) reinterpret_cast<float*>(sums + spg * MT)[tok] = down;
 }
 
-// One k-step of one slice for this lane: 2 x 16 B smem loads, 8 MMAs.  `step` points at
-// the step's first box row plus the slice's byte offset; row r of the step is at
-// r * kRowBytes.
+// The 32 k pairs (rows) of block `kb` of one slice for this lane, 16 MMAs of m16n8k32 u8 x s8:
+// MMA j (0..7) covers columns 16 g + 2 j, 16 g + 2 j + 1 (A rows g, g + 8) for B-column class
+// j / (2 MT); each j gets the high-nibble MMA and the low-nibble MMA into its own accumulator.
+// Rows outside [r0, r1) (a partial item) or beyond `nrows` (groups of < 64 k) read as zero.
 template <int MT>
-__device__ __forceinline__ void compute_step(const uint8_t* step, const uint2* fragb, int g, int t,
-                                             const uint32_t (&cls_mask)[4 / MT], int cB,
-                                             float (&D)[2 * MT][4]) {
-  const uint4 U = *reinterpret_cast<const uint4*>(step + (2 * t) * kRowBytes + 16 * g);
-  const uint4 V = *reinterpret_cast<const uint4*>(step + (2 * t + 1) * kRowBytes + 16 * g);
-  const uint2 bf = fragb[t * 2 * MT + cB];
+__device__ __forceinline__ void compute_kblock(const uint8_t* blk, const uint4* recb, int kb0,
+                                               int nrows, int r0, int r1, int g, int t,
+                                               const uint32_t (&cls_mask)[4 / MT], int cB,
+                                               int (&D)[8][4]) {
+  uint4 R[2][4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = kappa_row(h, t, i);
+      const int ar = kb0 + rr;
+      R[h][i] = (rr < nrows && ar >= r0 && ar < r1)
+                    ? *reinterpret_cast<const uint4*>(blk + rr * kRowBytes + 16 * g)
+                    : make_uint4(0u, 0u, 0u, 0u);
+    }
+  const uint4 bf = recb[t * 2 * MT + cB];
   constexpr int NCL = 4 / MT;
-  uint32_t bx[NCL], by[NCL];
+  uint32_t b1x[NCL], b1y[NCL], b2x[NCL], b2y[NCL];
 #pragma unroll
   for (int c = 0; c < NCL; ++c) {
-    bx[c] = bf.x & cls_mask[c];
-    by[c] = bf.y & cls_mask[c];
+    b1x[c] = bf.x & cls_mask[c];
+    b1y[c] = bf.y & cls_mask[c];
+    b2x[c] = bf.z & cls_mask[c];
+    b2y[c] = bf.w & cls_mask[c];
   }
-  const uint32_t uw[4] = {U.x, U.y, U.z, U.w};
-  const uint32_t vw[4] = {V.x, V.y, V.z, V.w};
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int wd = j >> 1;
-    const uint32_t bA = (j & 1) * 2, bB = bA + 1;
-    const uint32_t pA = prmt(uw[wd], vw[wd], bA | (bA << 4) | ((bA + 4) << 8) | ((bA + 4) << 12));
-    const uint32_t pB = prmt(uw[wd], vw[wd], bB | (bB << 4) | ((bB + 4) << 8) | ((bB + 4) << 12));
-    mma_16816(D[j % (2 * MT)], pA & 0x000F000Fu, pB & 0x000F000Fu, pA & 0x00F000F0u,
-              pB & 0x00F000F0u, bx[j / (2 * MT)], by[j / (2 * MT)]);
+  for (int wd = 0; wd < 4; ++wd) {  // word wd: columns 16 g + 4 wd .. + 3
+    uint32_t C0[4], C1[4];
+    transpose4x4(word(R[0][0], wd), word(R[0][1], wd), word(R[0][2], wd), word(R[0][3], wd), C0);
+    transpose4x4(word(R[1][0], wd), word(R[1][1], wd), word(R[1][2], wd), word(R[1][3], wd), C1);
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+      const int j = 2 * wd + pr;
+      const uint32_t a0 = C0[2 * pr], a1 = C0[2 * pr + 1], a2 = C1[2 * pr], a3 = C1[2 * pr + 1];
+      mma_16832_u8s8(D[j], (a0 >> 4) & 0x0F0F0F0Fu, (a1 >> 4) & 0x0F0F0F0Fu,
+                     (a2 >> 4) & 0x0F0F0F0Fu, (a3 >> 4) & 0x0F0F0F0Fu, b1x[j / (2 * MT)],
+                     b1y[j / (2 * MT)]);
+      mma_16832_u8s8(D[j], a0 & 0x0F0F0F0Fu, a1 & 0x0F0F0F0Fu, a2 & 0x0F0F0F0Fu,
+                     a3 & 0x0F0F0F0Fu, b2x[j / (2 * MT)], b2y[j / (2 * MT)]);
+    }
   }
 }
 
-// Applies the group's scales and zero points to the MMA sums and resets them.
+// Applies the group's scales and zero points to the MMA sums and resets them.  The sums of
+// row pair r are spread over the classes c (accumulator c * 2 MT + r); the other classes hold
+// zeros in this lane's positions, so they are folded by addition.
 template <int MT>
 __device__ __forceinline__ void group_epilogue(const uint8_t* scales, const uint8_t* zeros,
-                                               const float2* meta, int s0, int s1, int tokE,
-                                               int colbase, float (&D)[2 * MT][4],
+                                               const int2* sums, const float* gscale, int s0,
+                                               int s1, int tokE, int colbase, int (&D)[8][4],
                                                float (&y)[4 * MT]) {
-  float sxs = 0.f;
-  for (int s = s0; s < s1; ++s) sxs += meta[s * MT + tokE].x;
-  const float gsc = meta[s0 * MT + tokE].y;
+  constexpr int NCL = 4 / MT;
+  int sbh = 0, sbl = 0;
+  for (int s = s0; s < s1; ++s) {
+    const int2 v = sums[s * MT + tokE];
+    sbh += v.x;
+    sbl += v.y;
+  }
+  const float esc = gscale[tokE];
   const __half* sc = reinterpret_cast<const __half*>(scales) + colbase;
   const uint8_t* zp = zeros + colbase / 2;
 #pragma unroll
   for (int r = 0; r < 2 * MT; ++r) {
+    int d0 = D[r][0], d1 = D[r][1], d2 = D[r][2], d3 = D[r][3];
+#pragma unroll
+    for (int c = 1; c < NCL; ++c) {
+      d0 += D[c * 2 * MT + r][0];
+      d1 += D[c * 2 * MT + r][1];
+      d2 += D[c * 2 * MT + r][2];
+      d3 += D[c * 2 * MT + r][3];
+    }
     const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(sc + 2 * r));
-    const uint32_t zz = zp[r];
-    const float za = (float)(zz & 15u), zb = (float)(zz >> 4);
-    const float va = D[r][0] + D[r][1];
-    const float vb = D[r][2] + D[r][3];
-    y[2 * r] = fmaf(sf.x * gsc, fmaf(-za, sxs, va), y[2 * r]);
-    y[2 * r + 1] = fmaf(sf.y * gsc, fmaf(-zb, sxs, vb), y[2 * r + 1]);
-    D[r][0] = D[r][1] = D[r][2] = D[r][3] = 0.f;
+    const int zz = zp[r];
+    const int za = zz & 15, zb = zz >> 4;
+    // sum_k xq_k * (q_k - z), exact in int32 per part, then one rounding each
+    const float va = fmaf((float)(d1 - za * sbl), 0x1p-8f, (float)(d0 - za * sbh)) * esc;
+    const float vb = fmaf((float)(d3 - zb * sbl), 0x1p-8f, (float)(d2 - zb * sbh)) * esc;
+    y[2 * r] = fmaf(sf.x, va, y[2 * r]);
+    y[2 * r + 1] = fmaf(sf.y, vb, y[2 * r + 1]);
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) D[j][0] = D[j][1] = D[j][2] = D[j][3] = 0;
 }
 
 // The last warp to finish a tile: deterministic reduction of the partials + epilogue.
@@ -353,6 +425,26 @@ __device__ void fixup_tile(const PhaseParams& P, int m, int wt, int slice, long 
   }
 }
 
+// Global address of this lane's partial sums for segment `b` of column unit `cu`.
+template <int MT>
+__device__ __forceinline__ float* segment_partials(const PhaseParams& P, int cu, long long b,
+                                                   long long Wtot, int slice, int tokE, int colbase) {
+  const long long W = phase_ctas(P, Wtot);
+  const long long a = (long long)cu * P.groups * P.spg;
+  const int seg = (int)(b - cta_of_unit(a, P.units, W));
+  return P.partials + ((((size_t)cu * P.maxseg + seg) * kSlices + slice) * MT + tokE) * 128 + colbase;
+}
+
+// Counts one finished segment of sub-tile (wt, slice); returns true to the last of them.
+__device__ __forceinline__ bool count_segment(const PhaseParams& P, int wt, int slice,
+                                              long long Wtot) {
+  unsigned total = 0;
+  for (int mi = 0; mi < P.nmat; ++mi)
+    total += (unsigned)nseg_of_cu(P, (long long)wt * P.nmat + mi, Wtot);
+  const unsigned prev = atomicAdd(&P.counters[wt * kSlices + slice], 1u);
+  return prev == total - 1;
+}
+
 template <int MT>
 __device__ __forceinline__ void flush_segment(const PhaseParams& P, int m, int cu, long long b,
                                               long long Wtot, int slice, float (&y)[4 * MT],
@@ -389,64 +481,136 @@ __device__ __forceinline__ void flush_segment(const PhaseParams& P, int m, int c
 }
 
 // Consumer warps: x (optionally rmsnorm'ed, src/kernels/shaders.zig:16-56) -> records.
+// x and the norm weight are read first and the weight producer is held at named barrier 2
+// until every consumer has them in registers: reads issued after the weight stream starts
+// queue behind megabytes of TMA traffic.
 template <int MT>
-__device__ void prologue(const EngineParams& p, int warp, int lane, float* s_red, float* s_rms) {
-  if (p.do_norm) {
-    for (int tok = 0; tok < p.m; ++tok) {
-      const float* xr = p.x + (size_t)tok * p.ldx;
-      float ss = 0.f;
-      for (int i = threadIdx.x; i < p.K0; i += kNC * 32) {
-        const float v = xr[i];
-        ss = fmaf(v, v, ss);
-      }
-      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if (lane == 0) s_red[warp] = ss;
-      named_barrier(1, kNC * 32);
-      if (threadIdx.x == 0) {
-        float tot = 0.f;
-        for (int i = 0; i < kNC; ++i) tot += s_red[i];
-        s_rms[tok] = rsqrtf(tot / (float)p.K0 + p.eps);
-      }
-      named_barrier(1, kNC * 32);
-    }
-  }
+__device__ void prologue(const EngineParams& p, int warp, int lane, float* s_red, float* s_rms,
+                         uint8_t* rec0s) {
   const int nchunks = p.K0 / kTileCols;
-  uint8_t* recs = p.frag0 + (long long)blockIdx.x * p.frag0_cta_stride;
-  for (int c = warp; c < MT * nchunks; c += kNC) {
-    const int tok = (int)(c / nchunks), ch = (int)(c - (long long)tok * nchunks);
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (tok < p.m) {
-      const float4 xv =
-          *reinterpret_cast<const float4*>(p.x + (size_t)tok * p.ldx + ch * kTileCols + 4 * lane);
-      v[0] = xv.x;
-      v[1] = xv.y;
-      v[2] = xv.z;
-      v[3] = xv.w;
-      if (p.do_norm) {
-        const float4 wv = *reinterpret_cast<const float4*>(p.norm_w + ch * kTileCols + 4 * lane);
-        const float rms = s_rms[tok];
-        v[0] = v[0] * rms * wv.x;
-        v[1] = v[1] * rms * wv.y;
-        v[2] = v[2] * rms * wv.z;
-        v[3] = v[3] * rms * wv.w;
+  constexpr int kLocal = 4;  // 128-value chunks held in registers per consumer warp and token
+  float4 xv[MT][kLocal], wv[kLocal];
+  float ss[MT];
+#pragma unroll
+  for (int i = 0; i < kLocal; ++i) {
+    const int ch = warp + i * kNC;
+    const bool in = ch < nchunks;
+    wv[i] = (in && p.do_norm) ? *reinterpret_cast<const float4*>(p.norm_w + ch * kTileCols + 4 * lane)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok)
+      xv[tok][i] = (in && tok < p.m) ? *reinterpret_cast<const float4*>(
+                                           p.x + (size_t)tok * p.ldx + ch * kTileCols + 4 * lane)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int tok = 0; tok < MT; ++tok) {
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLocal; ++i) {
+      const float4 a = xv[tok][i];
+      v = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, v))));
+    }
+    // chunks beyond the register window (K0 > kLocal * kNC * 128) are read again later
+    if (tok < p.m)
+      for (int ch = warp + kLocal * kNC; ch < nchunks; ch += kNC) {
+        const float4 a =
+            *reinterpret_cast<const float4*>(p.x + (size_t)tok * p.ldx + ch * kTileCols + 4 * lane);
+        v = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, v))));
       }
+    ss[tok] = v;
+  }
+  // every consumer thread has its x values: release the weight producer
+  named_barrier_arrive(2, (kNC + 1) * 32);
+  float rms[MT];
+#pragma unroll
+  for (int tok = 0; tok < MT; ++tok) rms[tok] = 1.f;
+  if (p.do_norm) {
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok) {
+      float v = ss[tok];
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) s_red[tok * kNC + warp] = v;
+    }
+    named_barrier(1, kNC * 32);
+    if (threadIdx.x < MT) {
+      float tot = 0.f;
+      for (int i = 0; i < kNC; ++i) tot += s_red[threadIdx.x * kNC + i];
+      s_rms[threadIdx.x] = rsqrtf(tot / (float)p.K0 + p.eps);
+    }
+    named_barrier(1, kNC * 32);
+#pragma unroll
+    for (int tok = 0; tok < MT; ++tok) rms[tok] = s_rms[tok];
+  }
+  uint8_t* recs = p.rec0_smem ? rec0s : p.frag0 + (long long)blockIdx.x * p.frag0_cta_stride;
+  auto emit = [&](float4 a, float4 w, int tok, int ch) {
+    float v[4] = {a.x, a.y, a.z, a.w};
+    if (p.do_norm) {
+      v[0] = v[0] * rms[tok] * w.x;
+      v[1] = v[1] * rms[tok] * w.y;
+      v[2] = v[2] * rms[tok] * w.z;
+      v[3] = v[3] * rms[tok] * w.w;
     }
     build_records<MT>(v, tok, p.gs0, recs + (size_t)(ch * kTileCols / p.gs0) * p.frag0_bytes,
                       p.frag0_bytes, lane);
+  };
+#pragma unroll
+  for (int tok = 0; tok < MT; ++tok) {
+#pragma unroll
+    for (int i = 0; i < kLocal; ++i) {
+      const int ch = warp + i * kNC;
+      if (ch < nchunks) emit(xv[tok][i], wv[i], tok, ch);
+    }
+    for (int ch = warp + kLocal * kNC; ch < nchunks; ch += kNC) {
+      const float4 a = tok < p.m ? *reinterpret_cast<const float4*>(p.x + (size_t)tok * p.ldx +
+                                                                     ch * kTileCols + 4 * lane)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 w = p.do_norm
+                           ? *reinterpret_cast<const float4*>(p.norm_w + ch * kTileCols + 4 * lane)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      emit(a, w, tok, ch);
+    }
   }
-  fence_proxy_async();  // read back by this CTA's producer through TMA
+  // records in global memory are read back by this CTA's record warp through the async proxy
+  if (!p.rec0_smem) fence_proxy_async();
 }
 
+// Bounded warp-collective wait for an mbarrier phase that also gives up when the CTA aborts.
+__device__ __forceinline__ bool wait_slot(uint64_t* bar, uint32_t parity, const volatile int* abort,
+                                          unsigned* err, unsigned long long timeout_ns) {
+  bool done = mbar_try_wait(bar, parity);
+  if (!done) {
+    const uint64_t t0 = global_timer_ns();
+    while (!(done = mbar_try_wait(bar, parity))) {
+      if (*abort) break;
+      if (global_timer_ns() - t0 > timeout_ns) {
+        if ((threadIdx.x & 31) == 0) atomicOr(err, kErrTmaWait);
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, done);
+}
+
+// Warp roles: warps 0..kNC-1 consume stages, warp kNC (weight warp) streams the packed weights,
+// scales and zero points of every item, warp kNC+1 (record warp) copies each item's activation
+// record once it is ready.  Each stage's full barrier takes one arrival from each producer warp.
+constexpr int kWeightWarp = kNC;
+constexpr int kRecordWarp = kNC + 1;
+constexpr int kThreads = (kNC + 2) * 32;
+
 template <int MT>
-__global__ void __launch_bounds__((kNC + 1) * 32, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     int4_engine_kernel(const __grid_constant__ TmapPack maps, const __grid_constant__ EngineParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ float s_red[kNC];
+  __shared__ float s_red[MT * kNC];
   __shared__ float s_rms[MT];
-  __shared__ long long s_issued;
   __shared__ unsigned s_epoch;
-  __shared__ volatile int s_records;  // this CTA's phase-0 records are written
+  __shared__ volatile long long s_armed;   // items whose weights the weight warp has armed
+  __shared__ volatile int s_wdone;         // weight warp has left its loop (s_armed final)
+  __shared__ volatile int s_records;       // this CTA's phase-0 records are written
   __shared__ volatile int s_abort;
+  __shared__ volatile int s_never;         // stays 0: a wait that must not be cut short
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.stages;
@@ -454,15 +618,18 @@ __global__ void __launch_bounds__((kNC + 1) * 32, 1)
   uint8_t* auxs = smem + (size_t)S * p.tile_stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(auxs + (size_t)S * p.aux_stage_bytes);
   uint64_t* empty = full + S;
+  uint8_t* rec0s = reinterpret_cast<uint8_t*>(empty + S) + 16 - (smem_addr(empty + S) & 15u);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], 2);
       mbar_init(&empty[i], kNC);
     }
     fence_mbar_init();
     s_records = 0;
     s_abort = 0;
-    s_issued = 0;
+    s_never = 0;
+    s_armed = 0;
+    s_wdone = 0;
     s_epoch = ld_acquire_u32(&p.sync->epoch);
     trace_event(p, 0);
   }
@@ -475,96 +642,117 @@ __global__ void __launch_bounds__((kNC + 1) * 32, 1)
   uint32_t parity = 0;
   long long consumed = 0;
 
-  if (warp == kNC) {
-    // ------------------------------- producer warp -------------------------------------
+  if (warp == kWeightWarp) {
+    // ---------------------------- weight producer warp ---------------------------------
     const uint64_t pol_stream = l2_evict_first();
-    const uint64_t pol_keep = l2_evict_last();
-    ItemIter wi, fi;  // next item whose weights / whose activation record to issue
+    ItemIter wi;
     iter_start(wi, p, b, Ptot);
-    fi = wi;
-    long long G = 0, F = 0;  // items with weights issued / with records issued
-    int wslot = 0, fslot = 0;
+    long long G = 0;
+    int wslot = 0;
     uint32_t wround = 0;
+    named_barrier(2, (kNC + 1) * 32);  // the consumers have read x
+    while (wi.ph < p.nphases) {
+      if (wround > 0 && !wait_slot(&empty[wslot], (wround - 1) & 1, &s_abort, p.err, p.timeout_ns)) {
+        s_abort = 1;
+        break;
+      }
+      if (s_abort) break;
+      const PhaseParams& P = p.ph[wi.ph];
+      if (lane == 0) {
+        if (G == 0) trace_event(p, 7);
+        mbar_arrive_expect_tx(&full[wslot], item_weight_bytes(P, wi));
+      }
+      __syncwarp();
+      issue_weights(maps, P, wi, tiles + (size_t)wslot * p.tile_stage_bytes,
+                    auxs + (size_t)wslot * p.aux_stage_bytes, &full[wslot], pol_stream, lane);
+      __syncwarp();
+      ++G;
+      if (lane == 0) s_armed = G;
+      iter_next(wi, p, b, Ptot);
+      if (++wslot == S) {
+        wslot = 0;
+        ++wround;
+      }
+    }
+    if (lane == 0) {
+      s_armed = G;
+      __threadfence_block();
+      s_wdone = 1;
+      trace_event(p, 8);
+    }
+  } else if (warp == kRecordWarp) {
+    // ---------------------------- record producer warp ---------------------------------
+    const uint64_t pol_keep = l2_evict_last();
+    ItemIter fi;
+    iter_start(fi, p, b, Ptot);
+    long long F = 0;
+    int fslot = 0;
     bool aborted = false;
-    uint64_t t_idle = 0;
-    uint32_t spins = 0;
-    while (wi.ph < p.nphases || F < G) {
+    uint64_t t_wait = 0;
+    while (fi.ph < p.nphases) {
       if (s_abort) {
         aborted = true;
         break;
       }
-      bool progress = false;
-      if (wi.ph < p.nphases) {
-        bool free_slot = wround == 0;
-        if (!free_slot) free_slot = mbar_test_wait(&empty[wslot], (wround - 1) & 1);
-        free_slot = __shfl_sync(0xffffffffu, free_slot, 0);
-        if (free_slot) {
-          const PhaseParams& P = p.ph[wi.ph];
-          uint8_t* aux = auxs + (size_t)wslot * p.aux_stage_bytes;
-          if (lane == 0) {
-            if (G == 0) trace_event(p, 7);
-            mbar_arrive_expect_tx(&full[wslot], item_bytes(P, wi));
-          }
-          __syncwarp();
-          issue_weights(maps, P, wi, tiles + (size_t)wslot * p.tile_stage_bytes, aux, &full[wslot],
-                        pol_stream, lane);
-          ++G;
-          iter_next(wi, p, b, Ptot);
-          if (++wslot == S) {
-            wslot = 0;
-            ++wround;
-          }
-          progress = true;
-        }
-      }
-      if (F < G) {
-        const PhaseParams& P = p.ph[fi.ph];
-        bool ready;
-        if (P.ready_in == nullptr) {
-          ready = s_records != 0;
-        } else {
-          ready = ld_acquire_u32(&P.ready_in[fi.grp * P.gs / kTileCols]) == epoch + 1;
-        }
-        ready = __shfl_sync(0xffffffffu, ready, 0);
-        if (ready) {
-          fence_proxy_async();  // records were written by generic stores
-          if (lane == 10)
-            issue_frag(P, fi, b, auxs + (size_t)fslot * p.aux_stage_bytes, &full[fslot], pol_keep);
-          ++F;
-          iter_next(fi, p, b, Ptot);
-          fslot = fslot + 1 == S ? 0 : fslot + 1;
-          progress = true;
-        }
-      }
-      if (progress) {
-        t_idle = 0;
-        spins = 0;
-      } else if ((++spins & 63u) == 0) {
-        const uint64_t now = __shfl_sync(0xffffffffu, global_timer_ns(), 0);
-        if (t_idle == 0) {
-          t_idle = now;
-        } else if (now - t_idle > p.timeout_ns) {
-          if (lane == 0) atomicOr(p.err, kErrFlagWait);
-          aborted = true;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    if (aborted) {
-      // complete the armed stages so every issued copy lands before the CTA exits
-      while (F < G) {
-        if (lane == 10)
-          issue_frag(p.ph[fi.ph], fi, b, auxs + (size_t)fslot * p.aux_stage_bytes, &full[fslot],
-                     pol_keep);
+      // only items whose weights are armed (their slot is free and the full barrier is in
+      // the phase this arrival belongs to)
+      bool go = F < s_armed;
+      if (go && fi.ph == 0 && p.rec0_smem) {
+        // the consumers read this item's record from shared memory: complete the arrival
+        if (lane == 0) mbar_arrive(&full[fslot]);
+        __syncwarp();
         ++F;
         iter_next(fi, p, b, Ptot);
         fslot = fslot + 1 == S ? 0 : fslot + 1;
+        t_wait = 0;
+        continue;
+      }
+      if (go) {
+        const PhaseParams& P = p.ph[fi.ph];
+        if (P.ready_in == nullptr) {
+          go = s_records != 0;
+        } else {
+          unsigned v = 0;
+          if (lane == 0) v = ld_acquire_u32(&P.ready_in[fi.grp * P.gs / kTileCols]);
+          go = __shfl_sync(0xffffffffu, v, 0) == epoch + 1;
+        }
+      }
+      if (go) {
+        const PhaseParams& P = p.ph[fi.ph];
+        fence_proxy_async();  // records were written by generic stores
+        if (lane == 0) {
+          uint8_t* aux = auxs + (size_t)fslot * p.aux_stage_bytes;
+          mbar_arrive_expect_tx(&full[fslot], (uint32_t)P.frag_bytes);
+          issue_frag(P, fi, b, aux, &full[fslot], pol_keep);
+        }
+        __syncwarp();
+        ++F;
+        iter_next(fi, p, b, Ptot);
+        fslot = fslot + 1 == S ? 0 : fslot + 1;
+        t_wait = 0;
+      } else {
+        const uint64_t now = global_timer_ns();
+        if (t_wait == 0) {
+          t_wait = now;
+        } else if (now - t_wait > p.timeout_ns) {
+          if (lane == 0) atomicOr(p.err, kErrFlagWait);
+          s_abort = 1;
+          aborted = true;
+          break;
+        }
+        __nanosleep(32);
       }
     }
-    if (lane == 0) {
-      s_issued = G;
-      trace_event(p, 8);
+    if (aborted) {
+      // Complete every stage the weight warp armed (a plain arrival in place of the record) so
+      // that every copy in flight lands before the CTA exits.
+      const uint64_t t0 = global_timer_ns();
+      while (!s_wdone && global_timer_ns() - t0 < p.timeout_ns) __nanosleep(64);
+      const long long G = s_armed;
+      for (; F < G; ++F) {
+        if (lane == 0) mbar_arrive(&full[fslot]);
+        fslot = fslot + 1 == S ? 0 : fslot + 1;
+      }
     }
   } else {
     // ------------------------------- consumer warps ------------------------------------
@@ -581,7 +769,7 @@ __global__ void __launch_bounds__((kNC + 1) * 32, 1)
     iter_start(it, p, b, Ptot);
     bool ok = true;
 
-    prologue<MT>(p, warp, lane, s_red, s_rms);
+    prologue<MT>(p, warp, lane, s_red, s_rms, rec0s);
     named_barrier(1, kNC * 32);
     if (threadIdx.x == 0) {
       __threadfence_block();
@@ -591,14 +779,16 @@ __global__ void __launch_bounds__((kNC + 1) * 32, 1)
 
     for (int ph = 0; ph < p.nphases && ok; ++ph) {
       const PhaseParams& P = p.ph[ph];
-      float D[2 * MT][4];
+      int D[8][4];
       float y[4 * MT];
 #pragma unroll
-      for (int r = 0; r < 2 * MT; ++r) D[r][0] = D[r][1] = D[r][2] = D[r][3] = 0.f;
+      for (int r = 0; r < 8; ++r) D[r][0] = D[r][1] = D[r][2] = D[r][3] = 0;
 #pragma unroll
       for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+      const int kbg = P.spg >= 4 ? P.spg / 4 : 1;    // 32-pair blocks per group
+      const int nrows = P.spg >= 4 ? 32 : 8 * P.spg;  // valid rows per block
       while (it.ph == ph) {
-        if (!wait_stage(&full[slot], parity, p.err, p.timeout_ns)) {
+        if (!wait_slot(&full[slot], parity, &s_abort, p.err, p.timeout_ns)) {
           ok = false;
           s_abort = 1;
           break;
@@ -609,13 +799,20 @@ __global__ void __launch_bounds__((kNC + 1) * 32, 1)
         const uint8_t* ax = auxs + (size_t)slot * p.aux_stage_bytes;
         if (active) {
           const uint8_t* tl = tiles + (size_t)slot * p.tile_stage_bytes + slice * kTileCols;
-          const uint2* fb = reinterpret_cast<const uint2*>(frag_slot(const_cast<uint8_t*>(ax)));
-          for (int s = it.s0; s < it.s1; ++s)
-            compute_step<MT>(tl + s * kStepRows * kRowBytes, fb + s * 4 * 2 * MT, g, t, cls_mask,
-                             cB, D);
-          const float2* meta = reinterpret_cast<const float2*>(fb + P.spg * 4 * 2 * MT);
+          const uint8_t* rec = (ph == 0 && p.rec0_smem)
+                                   ? rec0s + (size_t)it.grp * P.frag_bytes
+                                   : frag_slot(const_cast<uint8_t*>(ax));
+          const uint4* rb = reinterpret_cast<const uint4*>(rec);
+          const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
+          for (int kb = 0; kb < kbg; ++kb) {
+            if (kb * 32 >= r1 || kb * 32 + 32 <= r0) continue;
+            compute_kblock<MT>(tl + (size_t)kb * 32 * kRowBytes, rb + kb * 4 * 2 * MT, kb * 32,
+                               nrows, r0, r1, g, t, cls_mask, cB, D);
+          }
+          const int2* sums = reinterpret_cast<const int2*>(rec + 128 * MT * kbg);
           group_epilogue<MT>(ax + slice * kScaleBytes,
-                             ax + kSlices * kScaleBytes + slice * kZeroBytes, meta, it.s0, it.s1,
+                             ax + kSlices * kScaleBytes + slice * kZeroBytes, sums,
+                             reinterpret_cast<const float*>(sums + P.spg * MT), it.s0, it.s1,
                              tokE, colbase, D, y);
         }
         __syncwarp();
@@ -636,11 +833,10 @@ __global__ void __launch_bounds__((kNC + 1) * 32, 1)
   }
   __syncthreads();
   if (warp < kNC) {
-    // Only after an error: wait for the stages the producer armed but the consumers did
-    // not take (the producer completed their records before leaving), so no copy is in
-    // flight when the CTA exits.
-    for (long long G = consumed; G < s_issued; ++G) {
-      wait_stage(&full[slot], parity, p.err, p.timeout_ns);
+    // Only after an error: wait for the stages that were armed but not consumed, so no copy
+    // is in flight when the CTA exits.
+    for (long long G = consumed; G < s_armed; ++G) {
+      wait_slot(&full[slot], parity, &s_never, p.err, p.timeout_ns);
       if (++slot == S) {
         slot = 0;
         parity ^= 1u;
@@ -665,7 +861,7 @@ cudaError_t launch_mt(const TmapPack& maps, const EngineParams& p, int grid, siz
   auto kern = int4_engine_kernel<MT>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3((kNC + 1) * 32);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -681,15 +877,39 @@ cudaError_t prepare_mt(size_t smem, int* blocks) {
   auto kern = int4_engine_kernel<MT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kern, (kNC + 1) * 32, smem);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kern, kThreads, smem);
 }
 
 }  // namespace
 
 int engine_warps_per_cta() { return kNC; }
 
-size_t engine_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes) {
-  return 1024 + (size_t)stages * ((size_t)tile_stage_bytes + aux_stage_bytes + 16);
+size_t engine_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes) {
+  return 1024 + (size_t)stages * ((size_t)tile_stage_bytes + aux_stage_bytes + 16) + 16 +
+         (size_t)rec0_bytes;
+}
+
+bool engine_plan_smem(int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes, int smem_limit,
+                      int* stages, int* rec0_smem, size_t* smem) {
+  for (int s = 5; s >= 4; --s) {
+    const size_t need = engine_smem_bytes(s, tile_stage_bytes, aux_stage_bytes, rec0_bytes);
+    if (need <= (size_t)smem_limit) {
+      *stages = s;
+      *rec0_smem = 1;
+      *smem = need;
+      return true;
+    }
+  }
+  for (int s = 5; s >= 2; --s) {
+    const size_t need = engine_smem_bytes(s, tile_stage_bytes, aux_stage_bytes, 0);
+    if (need <= (size_t)smem_limit) {
+      *stages = s;
+      *rec0_smem = 0;
+      *smem = need;
+      return true;
+    }
+  }
+  return false;
 }
 
 cudaError_t engine_occupancy(int mt, size_t smem, int* blocks) {

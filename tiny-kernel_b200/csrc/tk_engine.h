@@ -41,13 +41,15 @@ constexpr int kTraceEvents = 10;
 constexpr unsigned kErrTmaWait = 1u;
 constexpr unsigned kErrFlagWait = 2u;
 
-// One group's activation record: the B-operand fragments of the m16n8k16 MMA for every
-// k-step of the group, followed by per-step metadata:
-//   uint2  b[spg][4 (t)][2*MT (token, hi/lo)]
-//   float2 meta[spg][MT]  = {sum_k xs_k * 2^-24 over the step, 2^(24 - e) for the group}
+// One group's activation record (the B operand of the int8 tensor-core MMA):
+//   uint4 b[kbg][4 (t)][2*MT (token, hi/lo)]   kbg = max(1, gs / 64) blocks of 32 k pairs;
+//         .x/.y = high-nibble B (odd k) for kappa halves 0/1, .z/.w = low-nibble B (even k),
+//         each an int8 hi or lo part, 4 k pairs per word
+//   int2  sums[spg][MT]   sums of the int8 hi and lo parts over each 16-k step (zero points)
+//   float scale[MT]       2^-e of the group's int8 split
 // padded to 16 bytes.
 __host__ __device__ constexpr int frag_record_bytes(int spg, int mt) {
-  return (spg * 72 * mt + 15) & ~15;
+  return (128 * mt * (spg >= 4 ? spg / 4 : 1) + 8 * mt * spg + 4 * mt + 15) & ~15;
 }
 
 enum EpilogueKind : int {
@@ -106,6 +108,9 @@ struct EngineParams {
   long long frag0_cta_stride;
   int gs0;
   int frag0_bytes;
+  // phase-0 records in shared memory (built by the consumers, read with plain loads) when
+  // rec0_smem, else in frag0 (global, one copy per CTA) and copied per stage by TMA
+  int rec0_smem;
   // shared-memory ring
   int stages;
   int tile_stage_bytes;

@@ -61,6 +61,11 @@ __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Arrives at a named barrier without waiting (the waiting side uses named_barrier).
+__device__ __forceinline__ void named_barrier_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ---- proxies / fences -------------------------------------------------------------
 // Orders this thread's generic-proxy accesses before later async-proxy (TMA) accesses.
 __device__ __forceinline__ void fence_proxy_async() {
@@ -122,8 +127,34 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// m16n8k32 integer MMA, A unsigned 8-bit (row), B signed 8-bit (col), s32 accumulate.
+__device__ __forceinline__ void mma_16832_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return __byte_perm(a, b, sel);
 }
 
+}  // namespace tk
+
+namespace tk {
+// Word w (0..3) of a 16-byte vector.
+__device__ __forceinline__ uint32_t word(const uint4& v, int w) {
+  return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
+}
+// 4x4 byte transpose: r_i holds row i (byte j = column j); c_j receives column j (byte i = row i).
+__device__ __forceinline__ void transpose4x4(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3,
+                                             uint32_t (&c)[4]) {
+  const uint32_t t0 = prmt(r0, r1, 0x5140), t1 = prmt(r0, r1, 0x7362);
+  const uint32_t t2 = prmt(r2, r3, 0x5140), t3 = prmt(r2, r3, 0x7362);
+  c[0] = prmt(t0, t2, 0x5410);
+  c[1] = prmt(t0, t2, 0x7632);
+  c[2] = prmt(t1, t3, 0x5410);
+  c[3] = prmt(t1, t3, 0x7632);
+}
 }  // namespace tk

@@ -231,14 +231,19 @@ int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, c
   int fb_max = std::max(p.ph[0].frag_bytes, p.nphases > 1 ? p.ph[1].frag_bytes : 0);
   p.tile_stage_bytes = (spg_max * kStepRows * kRowBytes + 127) & ~127;
   p.aux_stage_bytes = (kSlices * (kScaleBytes + kZeroBytes) + fb_max + 15) & ~15;
-  int stages = d->stages_override > 0 ? d->stages_override : 5;
-  while (stages > 2 &&
-         engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes) > (size_t)d->smem_optin - 2048)
-    --stages;
-  size_t smem = engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes);
-  if (smem > (size_t)d->smem_optin - 2048)
+  int stages = 0, rec0_smem = 0;
+  size_t smem = 0;
+  const int rec0_bytes = (p.K0 / p.gs0) * p.frag0_bytes;
+  if (!engine_plan_smem(p.tile_stage_bytes, p.aux_stage_bytes, rec0_bytes, d->smem_optin - 2048,
+                        &stages, &rec0_smem, &smem))
     return fail(TK_ERR_UNSUPPORTED, "engine ring does not fit in shared memory");
+  if (d->stages_override > 0 && d->stages_override < stages) {
+    stages = d->stages_override;
+    smem = engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes,
+                             rec0_smem ? rec0_bytes : 0);
+  }
   p.stages = stages;
+  p.rec0_smem = rec0_smem;
   p.trace = d->trace;
   if (d->trace)
     TK_CUDA_TRY(cudaMemsetAsync(d->trace, 0, (size_t)d->sm_count * kTraceEvents * 8, st));
@@ -819,14 +824,13 @@ int noalloc_engine_chunk(unsigned char* scratch, int sm_count, int smem_optin, c
   if (stt != TK_OK) return stt;
   p.tile_stage_bytes = (P.spg * kStepRows * kRowBytes + 127) & ~127;
   p.aux_stage_bytes = (kSlices * (kScaleBytes + kZeroBytes) + P.frag_bytes + 15) & ~15;
-  int stages = 5;
-  while (stages > 2 &&
-         engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes) > (size_t)smem_optin - 2048)
-    --stages;
-  const size_t smem = engine_smem_bytes(stages, p.tile_stage_bytes, p.aux_stage_bytes);
-  if (smem > (size_t)smem_optin - 2048)
+  int stages = 0, rec0_smem = 0;
+  size_t smem = 0;
+  if (!engine_plan_smem(p.tile_stage_bytes, p.aux_stage_bytes, P.groups * P.frag_bytes,
+                        smem_optin - 2048, &stages, &rec0_smem, &smem))
     return fail(TK_ERR_UNSUPPORTED, "engine ring does not fit in shared memory");
   p.stages = stages;
+  p.rec0_smem = rec0_smem;
   p.trace = nullptr;
   p.sync = reinterpret_cast<SyncState*>(scratch);
   p.err = reinterpret_cast<unsigned*>(scratch + off_err);
