@@ -594,10 +594,21 @@ __device__ __forceinline__ bool wait_slot(uint64_t* bar, uint32_t parity, const 
 
 // Warp roles: warps 0..kNC-1 consume stages, warp kNC (weight warp) streams the packed weights,
 // scales and zero points of every item, warp kNC+1 (record warp) copies each item's activation
-// record once it is ready.  Each stage's full barrier takes one arrival from each producer warp.
+// record once it is ready, warp kNC+2 (flush warp) completes the split-K segments that end in
+// the middle of a CTA's range (the consumers only store their partial sums and move on; the
+// flush warp makes them visible, counts them and runs the tile epilogue when it is last).  Each
+// stage's full barrier takes one arrival from each producer warp.
 constexpr int kWeightWarp = kNC;
 constexpr int kRecordWarp = kNC + 1;
-constexpr int kThreads = (kNC + 2) * 32;
+constexpr int kFlushWarp = kNC + 2;
+constexpr int kThreads = (kNC + 3) * 32;
+constexpr int kFlushSlots = 4;  // flush events in flight between the consumers and the flush warp
+
+// An item ends its column unit in the middle of the CTA's range of the phase (its split-K
+// segment is handed to the flush warp) rather than at the end of the range.
+__device__ __forceinline__ bool mid_range_flush(const PhaseParams& P, const ItemIter& it) {
+  return it.grp == P.groups - 1 && it.i != it.n - 1;
+}
 
 template <int MT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -611,6 +622,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ volatile int s_records;       // this CTA's phase-0 records are written
   __shared__ volatile int s_abort;
   __shared__ volatile int s_never;         // stays 0: a wait that must not be cut short
+  __shared__ uint64_t s_fbar[kFlushSlots];  // mid-range flush events (kNC consumer arrivals)
+  __shared__ volatile int s_fdone;         // flush events the flush warp has completed
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.stages;
@@ -624,6 +637,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[i], 2);
       mbar_init(&empty[i], kNC);
     }
+    for (int i = 0; i < kFlushSlots; ++i) mbar_init(&s_fbar[i], kNC);
+    s_fdone = 0;
     fence_mbar_init();
     s_records = 0;
     s_abort = 0;
@@ -754,6 +769,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         fslot = fslot + 1 == S ? 0 : fslot + 1;
       }
     }
+  } else if (warp == kFlushWarp) {
+    // ------------------------------- flush warp ----------------------------------------
+    ItemIter hi;
+    iter_start(hi, p, b, Ptot);
+    int k = 0;
+    while (hi.ph < p.nphases) {
+      const PhaseParams& P = p.ph[hi.ph];
+      if (mid_range_flush(P, hi)) {
+        if (!wait_slot(&s_fbar[k % kFlushSlots], (uint32_t)(k / kFlushSlots) & 1u, &s_abort, p.err,
+                       p.timeout_ns)) {
+          s_abort = 1;
+          break;
+        }
+        __threadfence();  // the consumers' partial sums (acquired through the barrier)
+        const int wt = hi.cu >> (P.nmat - 1);
+        const int ns = active_slices(P, wt);
+        const bool last = lane < ns && count_segment(P, wt, lane, Ptot);
+        unsigned won = __ballot_sync(0xffffffffu, last);
+        if (won) __threadfence();
+        while (won) {
+          const int sl = __ffs(won) - 1;
+          won &= won - 1;
+          fixup_tile<MT>(P, p.m, wt, sl, Ptot, lane, epoch);
+          __syncwarp();
+          if (lane == 0) atomicExch(&P.counters[wt * kSlices + sl], 0u);
+        }
+        __syncwarp();
+        if (lane == 0) s_fdone = k + 1;
+        ++k;
+      }
+      iter_next(hi, p, b, Ptot);
+    }
   } else {
     // ------------------------------- consumer warps ------------------------------------
     const int slice = warp;
@@ -768,6 +815,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ItemIter it;
     iter_start(it, p, b, Ptot);
     bool ok = true;
+    int fk = 0;  // mid-range flush events handed to the flush warp
 
     prologue<MT>(p, warp, lane, s_red, s_rms, rec0s);
     named_barrier(1, kNC * 32);
@@ -823,10 +871,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           parity ^= 1u;
         }
         const int cu = it.cu;
-        const bool last_of_cu = (it.i == it.n - 1) || (it.grp == P.groups - 1);
+        const bool mid = mid_range_flush(P, it);
+        const bool last_of_range = it.i == it.n - 1;
         iter_next(it, p, b, Ptot);
-        if (last_of_cu && active)
+        if (mid) {
+          // store the partial sums and hand the segment to the flush warp
+          if (active) {
+            float* dst = segment_partials<MT>(P, cu, b, Ptot, slice, tokE, colbase);
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+              *reinterpret_cast<float4*>(dst + 4 * i) =
+                  make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+          __syncwarp();
+          if (lane == 0) {
+            // the event slot is free once the flush warp has completed event fk - kFlushSlots
+            const uint64_t t0 = global_timer_ns();
+            while (s_fdone < fk - kFlushSlots + 1 && !s_abort) {
+              if (global_timer_ns() - t0 > p.timeout_ns) {
+                atomicOr(p.err, kErrFlagWait);
+                s_abort = 1;
+                break;
+              }
+            }
+            mbar_arrive(&s_fbar[fk % kFlushSlots]);
+          }
+          ++fk;
+        } else if (last_of_range && active) {
           flush_segment<MT>(P, p.m, cu, b, Ptot, slice, y, lane, tokE, colbase, epoch);
+        }
       }
       if (threadIdx.x == 0) trace_event(p, 3 + 2 * ph);
     }
