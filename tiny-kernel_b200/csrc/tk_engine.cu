@@ -6,34 +6,39 @@
 // on the reference's packed layout, and the INT4 Llama FFN built from it
 // (src/bench.zig:266-341 gate/up composition plus the down projection).
 //
-// Design (one CTA per SM: 8 consumer warps + 1 producer warp):
+// Design (one CTA per SM: 8 consumer warps + weight, record and flush warps):
 //  * A work unit is one k-step (8 packed rows = 16 k) of a 1024-column wide tile of one
-//    matrix.  Units are ordered tile-major, matrix, group, step; CTA b of P owns units
-//    [U*b/P, U*(b+1)/P) (stream-K), so every SM streams the same number of bytes.  Units
-//    are visited group by group ("items"); the iteration is incremental (no divisions).
+//    matrix.  Within a phase, units are ordered tile-major, matrix, group, step; CTA b of P
+//    owns units [U*b/P, U*(b+1)/P) (stream-K), so every SM streams the same number of bytes.
+//    Units are visited group by group ("items"); the iteration is incremental.
 //  * The CTA has one ring of S stages (full + empty mbarrier each).  A stage holds one
 //    item: the packed rows of the group as 1040-byte TMA box rows (u64 tensor map; one
 //    box for a whole group, or one per k-step for a partial group) -- long rows are what
 //    lets TMA stream near the HBM read limit -- plus the group's f16 scales (2 KB), zero
-//    points (512 B) and activation record.  Producer lane 0 issues the boxes, lanes 8-10
-//    the rest.  Consecutive 1040-byte rows sit 16 bytes apart modulo 128, which makes the
-//    fragment loads bank-conflict free without a swizzle.
-//  * Consumer warp j computes slice j of every stage.  The weight nibbles become m16n8k16
-//    A fragments with one PRMT and two LOPs per 4 nibbles: each nibble lands in the
-//    mantissa of an f16 subnormal, so the MMA sees q * 2^-24 exactly (even k) or
-//    16 q * 2^-24 (odd k; the activations carry the 1/16).  Zero points are applied per
-//    group in f32 as  - z * sum_k x_k.
-//  * Activations arrive as precomputed B fragments: x is scaled by a power of two per
-//    group and split x = hi + lo into two f16 values (B columns 2c, 2c+1), so the
-//    products keep ~22 significant bits and accumulate in f32 in the tensor core.
+//    points (512 B) and activation record.  Weight-warp lane 0 issues the boxes, lanes 8-9
+//    the scales and zero points; the record warp adds the record.
+//  * Consumer warp j computes slice j (128 columns) of every stage.
+//    - m <= 2 (the dp2a path): lane l owns columns 4l..4l+3 of the slice.  It copies its
+//      packed bytes of every row, the scales, zero points and the activation record into
+//      registers and releases the stage at once (a held stage is a stage not streaming),
+//      then computes.  Two rows' bytes are interleaved with one PRMT per column pair so a
+//      column's two k pairs sit in adjacent bytes; masking gives the low nibbles (even k)
+//      and 16 x the high nibbles (odd k); dp2a multiplies them by the activations
+//      quantised to int16 per group (scale 2^-e, max |x| * 2^e in [2^14, 2^15)), two k per
+//      instruction, into exact int32 sums.  Per group:
+//        v = 2^-e * (sum_even + (sum_odd16 >> 4) - z * sum_k xq_k)     (exact integers)
+//        y += scale * v.
+//    - m = 3, 4 (the int8 tensor-core path): m16n8k32 u8 x s8 MMAs on nibble planes
+//      against activations split into int8 hi + lo / 256 parts.
 //  * Split-K partial sums go to a scratch buffer; the last warp to finish a 128-column
-//    sub-tile (an atomic counter per sub-tile) adds the partials in CTA order
+//    sub-tile (an atomic counter per sub-tile) adds the partials in phase and CTA order
 //    (deterministic) and runs the epilogue: store (+ residual), or silu(gate) * up -> the
 //    next phase's records plus a ready flag for that sub-tile.
-//  * No grid-wide barrier: every CTA builds its own phase-0 records in a private scratch
-//    slice; the producer issues a phase-1 record copy only once the flag of the h
-//    sub-tile it reads equals epoch + 1 (epoch = launches completed, advanced by the last
-//    CTA to finish), so weights of both phases stream without a pause.
+//  * No grid-wide barrier: every CTA builds its own prologue records; the record warp
+//    issues a record copy for an h group only once the flag of its h sub-tile equals
+//    epoch + 1 (epoch = launches completed, advanced by the last CTA to finish).  The FFN
+//    splits gate/up into tile ranges so the down projection of an early range overlaps
+//    the reduction of the last one.
 // Every spin-wait is bounded by a global-timer timeout and reports through p.err.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -47,6 +52,8 @@ namespace {
 
 constexpr int kNC = kSlices;  // consumer warps: one per 128-column slice
 
+// ---- stream-K bookkeeping --------------------------------------------------------------
+
 // CTA whose stream-K range holds unit u (ranges [U*b/W, U*(b+1)/W), all non-empty)
 __device__ __forceinline__ long long cta_of_unit(long long u, long long units, long long W) {
   return ((u + 1) * W - 1) / units;
@@ -56,12 +63,36 @@ __device__ __forceinline__ long long phase_ctas(const PhaseParams& P, long long 
   return P.units < Wtot ? P.units : Wtot;
 }
 
-// Number of CTAs whose ranges intersect column unit cu (= wide tile * nmat + mat).
+// Number of CTA ranges of phase P holding units of (global) column unit cu = wide tile *
+// nmat + matrix; 0 when the phase does not cover cu.
 __device__ __forceinline__ int nseg_of_cu(const PhaseParams& P, long long cu, long long Wtot) {
+  const long long c = cu - (long long)P.wt0 * P.nmat;
+  if (c < 0 || c >= (long long)P.tiles * P.nmat) return 0;
   const long long W = phase_ctas(P, Wtot);
   const long long per = (long long)P.groups * P.spg;
-  const long long a = cu * per;
+  const long long a = c * per;
   return (int)(cta_of_unit(a + per - 1, P.units, W) - cta_of_unit(a, P.units, W) + 1);
+}
+
+// Segments of column unit cu summed over the phases that reduce together with phase ph.
+__device__ __forceinline__ int red_segments(const EngineParams& p, int ph, long long cu,
+                                            long long Wtot) {
+  const PhaseParams& P = p.ph[ph];
+  int n = 0;
+  for (int q = P.red_first; q < P.red_first + P.red_count; ++q) n += nseg_of_cu(p.ph[q], cu, Wtot);
+  return n;
+}
+
+// Index within its reduction of CTA b's segment of column unit cu in phase ph (earlier
+// phases of the reduction first, then CTA order).
+__device__ __forceinline__ int segment_index(const EngineParams& p, int ph, long long cu,
+                                             long long b, long long Wtot) {
+  const PhaseParams& P = p.ph[ph];
+  int off = 0;
+  for (int q = P.red_first; q < ph; ++q) off += nseg_of_cu(p.ph[q], cu, Wtot);
+  const long long W = phase_ctas(P, Wtot);
+  const long long a = (cu - (long long)P.wt0 * P.nmat) * P.groups * P.spg;
+  return off + (int)(b - cta_of_unit(a, P.units, W));
 }
 
 __device__ __forceinline__ int active_slices(const PhaseParams& P, int wtile) {
@@ -69,11 +100,18 @@ __device__ __forceinline__ int active_slices(const PhaseParams& P, int wtile) {
   return rem < kSlices ? rem : kSlices;
 }
 
+// Partial sums of segment `seg` of column unit cu, slice `slice`: [MT][128] floats.
+template <int MT>
+__device__ __forceinline__ float* partial_slot(const PhaseParams& P, long long cu, int seg,
+                                               int slice) {
+  return P.partials + (((size_t)cu * P.maxseg + seg) * kSlices + slice) * MT * kTileCols;
+}
+
 // Walks one CTA's items (one group of one wide tile each) through all phases.
 struct ItemIter {
   int ph;       // phase of the current item; == nphases when exhausted
   int i, n;     // index within the phase, items in the phase
-  int cu, grp;  // column unit (tile * nmat + mat) and group of the current item
+  int cu, grp;  // global column unit (tile * nmat + mat) and global group of the item
   int s0, s1;   // k-step range of the current item within its group
   int last_s1;  // s1 of the phase's last item
 };
@@ -86,10 +124,11 @@ __device__ __forceinline__ void iter_seek(ItemIter& it, const EngineParams& p, l
     if (w < W) {
       const long long beg = P.units * w / W, end = P.units * (w + 1) / W;
       const long long fg0 = beg / P.spg, fgl = (end - 1) / P.spg;
+      const long long cl = fg0 / P.groups;
       it.i = 0;
       it.n = (int)(fgl - fg0 + 1);
-      it.cu = (int)(fg0 / P.groups);
-      it.grp = (int)(fg0 - (long long)it.cu * P.groups);
+      it.cu = (int)(cl + (long long)P.wt0 * P.nmat);
+      it.grp = P.g0 + (int)(fg0 - cl * P.groups);
       it.s0 = (int)(beg - fg0 * P.spg);
       it.last_s1 = (int)(end - fgl * P.spg);
       it.s1 = it.n == 1 ? it.last_s1 : P.spg;
@@ -110,8 +149,8 @@ __device__ __forceinline__ void iter_next(ItemIter& it, const EngineParams& p, l
                                           long long Wtot) {
   const PhaseParams& P = p.ph[it.ph];
   if (++it.i < it.n) {
-    if (++it.grp == P.groups) {
-      it.grp = 0;
+    if (++it.grp == P.g1) {
+      it.grp = P.g0;
       ++it.cu;
     }
     it.s0 = 0;
@@ -129,7 +168,7 @@ __device__ __forceinline__ uint32_t item_weight_bytes(const PhaseParams& P, cons
   return (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes + ns * (kScaleBytes + kZeroBytes));
 }
 
-// Producer lane `lane` issues its share of item `it`'s weight-side copies: lane 0 the TMA
+// Weight-warp lane `lane` issues its share of item `it`'s weight-side copies: lane 0 the TMA
 // box(es), lane 8 the scales, lane 9 the zero points.
 __device__ __forceinline__ void issue_weights(const TmapPack& maps, const PhaseParams& P,
                                               const ItemIter& it, uint8_t* tile, uint8_t* aux,
@@ -172,37 +211,17 @@ __device__ __forceinline__ void trace_event(const EngineParams& p, int ev) {
   if (p.trace) p.trace[(size_t)blockIdx.x * kTraceEvents + ev] = global_timer_ns();
 }
 
-// Warp-collective bounded wait on a stage barrier.
-__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity, unsigned* err,
-                                           unsigned long long timeout_ns) {
-  bool done = mbar_try_wait(bar, parity);
-  if (!done) {
-    const uint64_t t0 = global_timer_ns();
-    while (!(done = mbar_try_wait(bar, parity))) {
-      if (global_timer_ns() - t0 > timeout_ns) break;
-    }
-  }
-  const bool all = __all_sync(0xffffffffu, done);
-  if (!all && (threadIdx.x & 31) == 0) atomicOr(err, kErrTmaWait);
-  return all;
-}
+// ---- activation records ------------------------------------------------------------------
 
-// Row (k pair within a 32-pair block) that MMA K index kappa = 16 h + 4 t + i reads:
-// 16 h + 2 t + (i & 1) + 8 (i >> 1).  For a fixed i the 4 t values land 2 rows apart, so the
-// 16-byte loads of a quarter warp (g in {0,1}, t in 0..3) hit 8 distinct 16-byte bank slots of
-// the 1040-byte-strided stage rows.
-__device__ __forceinline__ int kappa_row(int h, int t, int i) {
-  return 16 * h + 2 * t + (i & 1) + 8 * (i >> 1);
-}
-
-// Warp-collective: lane l holds v[0..3] = values 4l..4l+3 of a 128-value activation chunk of
-// token `tok`.  Writes the records of the chunk's 128/gs groups into `rec` (the record of the
-// chunk's first group, records `rec_bytes` apart).  Per k pair p the MMA sees x[2p+1] against
-// the high nibble and x[2p] against the low nibble of the packed byte.  The group's values are
-// scaled by 2^e (max |x| of the group in [32, 64)) and split into int8 hi + lo / 256 parts.
+// int8 tensor-core path.  Warp-collective: lane l holds v[0..3] = values 4l..4l+3 of a
+// 128-value activation chunk of token `tok`.  Writes the records of the chunk's 128/gs
+// groups into `rec` (the record of the chunk's first group, records `rec_bytes` apart).  Per
+// k pair p the MMA sees x[2p+1] against the high nibble and x[2p] against the low nibble of
+// the packed byte.  The group's values are scaled by 2^e (max |x| of the group in [32, 64))
+// and split into int8 hi + lo / 256 parts.
 template <int MT>
-__device__ __forceinline__ void build_records(const float (&v)[4], int tok, int gs,
-                                              uint8_t* rec, int rec_bytes, int lane) {
+__device__ __forceinline__ void build_records_mma(const float (&v)[4], int tok, int gs,
+                                                  uint8_t* rec, int rec_bytes, int lane) {
   const int gl = gs >> 2;  // lanes per group
   // k pairs 2l and 2l + 1 of the chunk: odd k (high nibble) and even k (low nibble)
   const float b[4] = {v[1], v[0], v[3], v[2]};
@@ -269,6 +288,57 @@ __device__ __forceinline__ void build_records(const float (&v)[4], int tok, int 
   int2* sums = reinterpret_cast<int2*>(r + 128 * MT * kbg);
   if ((lg & 3) == 0) sums[(lg >> 2) * MT + tok] = make_int2(sh, sl);
   if (lg == 0) reinterpret_cast<float*>(sums + spg * MT)[tok] = down;
+}
+
+// dp2a path.  Warp-collective, same lane contract as build_records_mma: lane l holds values
+// 4l..4l+3 of a 128-value chunk of token `tok`.  A group's lane lg writes X[lg] of the
+// group's record (its four values are k = 4lg..4lg+3 of the group: packed rows 2lg, 2lg+1).
+template <int MT>
+__device__ __forceinline__ void build_records_dp(const float (&v)[4], int tok, int gs,
+                                                 uint8_t* rec, int rec_bytes, int lane) {
+  const int gl = gs >> 2;  // lanes per group
+  float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  for (int off = 1; off < gl; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  // e with max |x| * 2^e in [2^14, 2^15) from the exponent field (zero, subnormal and
+  // non-finite maxima are clamped to the range the scale stays a normal power of two in)
+  int e = 141 - (int)((__float_as_uint(mx) >> 23) & 0xffu);
+  e = e < -100 ? -100 : (e > 100 ? 100 : e);
+  const float up = __uint_as_float((uint32_t)(127 + e) << 23);    // 2^e
+  const float down = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e
+  int q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = __float2int_rn(v[i] * up);
+    q[i] = t < -32767 ? -32767 : (t > 32767 ? 32767 : t);
+  }
+  const int gi = lane / gl, lg = lane - gi * gl;
+  uint8_t* r = rec + (size_t)gi * rec_bytes + (size_t)tok * dp_tok_stride(gs);
+  reinterpret_cast<uint2*>(r)[lg] =
+      make_uint2(((uint32_t)q[0] & 0xffffu) | ((uint32_t)q[2] << 16),
+                 ((uint32_t)q[1] & 0xffffu) | ((uint32_t)q[3] << 16));
+  // per 16-k step (4 lanes): the sum of the quantised values, for the zero-point term
+  int s = q[0] + q[1] + q[2] + q[3];
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  if ((lg & 3) == 0) reinterpret_cast<int*>(r + 2 * gs)[lg >> 2] = s;
+  if (lg == 0) *reinterpret_cast<float*>(r + 2 * gs + gs / 4) = down;
+}
+
+template <int MT>
+__device__ __forceinline__ void build_records(const float (&v)[4], int tok, int gs, uint8_t* rec,
+                                              int rec_bytes, int lane) {
+  if constexpr (MT <= 2) build_records_dp<MT>(v, tok, gs, rec, rec_bytes, lane);
+  else build_records_mma<MT>(v, tok, gs, rec, rec_bytes, lane);
+}
+
+// ---- int8 tensor-core path (m = 3, 4) ------------------------------------------------------
+
+// Row (k pair within a 32-pair block) that MMA K index kappa = 16 h + 4 t + i reads:
+// 16 h + 2 t + (i & 1) + 8 (i >> 1).  For a fixed i the 4 t values land 2 rows apart, so the
+// 16-byte loads of a quarter warp (g in {0,1}, t in 0..3) hit 8 distinct 16-byte bank slots of
+// the 1040-byte-strided stage rows.
+__device__ __forceinline__ int kappa_row(int h, int t, int i) {
+  return 16 * h + 2 * t + (i & 1) + 8 * (i >> 1);
 }
 
 // The 32 k pairs (rows) of block `kb` of one slice for this lane, 16 MMAs of m16n8k32 u8 x s8:
@@ -360,27 +430,182 @@ __device__ __forceinline__ void group_epilogue(const uint8_t* scales, const uint
   for (int j = 0; j < 8; ++j) D[j][0] = D[j][1] = D[j][2] = D[j][3] = 0;
 }
 
-// The last warp to finish a tile: deterministic reduction of the partials + epilogue.
+// ---- dp2a path (m = 1, 2) ---------------------------------------------------------------------
+
+// Packed bytes of rows [rb, rb + RB) of this lane's 4 columns; rows outside [r0, r1) are 0.
+template <int RB>
+__device__ __forceinline__ void dp_load_rows(const uint8_t* tl, int rb, int r0, int r1, int lane,
+                                             uint32_t (&w)[RB]) {
+  if (r0 <= rb && r1 >= rb + RB) {
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+      w[r] = *reinterpret_cast<const uint32_t*>(tl + (size_t)(rb + r) * kRowBytes + 4 * lane);
+  } else {
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      const int rr = rb + r;
+      w[r] = (rr >= r0 && rr < r1)
+                 ? *reinterpret_cast<const uint32_t*>(tl + (size_t)rr * kRowBytes + 4 * lane)
+                 : 0u;
+    }
+  }
+}
+
+// Activation pairs of row pairs [rb/2, rb/2 + RB/2) of every token (two row pairs per uint4).
+template <int MT, int RB>
+__device__ __forceinline__ void dp_load_x(const uint8_t* rec, int tok_stride, int rb,
+                                          uint4 (&X)[MT][RB / 4]) {
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const uint4* xp = reinterpret_cast<const uint4*>(rec + (size_t)m * tok_stride) + rb / 4;
+#pragma unroll
+    for (int q = 0; q < RB / 4; ++q) X[m][q] = xp[q];
+  }
+}
+
+// Row pair j = (2j, 2j+1): p0 = {r c0, r+1 c0, r c1, r+1 c1}, p1 the same for c2, c3.  The low
+// nibbles (even k) meet x[4j], x[4j+2]; 16 x the high nibbles (odd k) meet x[4j+1], x[4j+3].
+template <int MT, int RB>
+__device__ __forceinline__ void dp_compute(const uint32_t (&w)[RB], const uint4 (&X)[MT][RB / 4],
+                                           int (&aL)[MT][4], int (&aH)[MT][4]) {
+#pragma unroll
+  for (int j = 0; j < RB / 2; ++j) {
+    const uint32_t p0 = prmt(w[2 * j], w[2 * j + 1], 0x5140);
+    const uint32_t p1 = prmt(w[2 * j], w[2 * j + 1], 0x7362);
+    const uint32_t l0 = p0 & 0x0F0F0F0Fu, h0 = p0 & 0xF0F0F0F0u;
+    const uint32_t l1 = p1 & 0x0F0F0F0Fu, h1 = p1 & 0xF0F0F0F0u;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const uint32_t xe = (j & 1) ? X[m][j >> 1].z : X[m][j >> 1].x;
+      const uint32_t xo = (j & 1) ? X[m][j >> 1].w : X[m][j >> 1].y;
+      aL[m][0] = dp2a_lo(xe, l0, aL[m][0]);
+      aL[m][1] = dp2a_hi(xe, l0, aL[m][1]);
+      aL[m][2] = dp2a_lo(xe, l1, aL[m][2]);
+      aL[m][3] = dp2a_hi(xe, l1, aL[m][3]);
+      aH[m][0] = dp2a_lo(xo, h0, aH[m][0]);
+      aH[m][1] = dp2a_hi(xo, h0, aH[m][1]);
+      aH[m][2] = dp2a_lo(xo, h1, aH[m][2]);
+      aH[m][3] = dp2a_hi(xo, h1, aH[m][3]);
+    }
+  }
+}
+
+// One item of one slice on the dp2a path: R = packed rows per group (gs / 2).  Loads every
+// stage byte it needs, releases the stage (empty barrier), then computes; groups of 128 k
+// (R = 64) are computed in two 32-row blocks before the release.  y[4 m + i] accumulates
+// column 4 lane + i of token m.
+template <int MT, int R>
+__device__ __forceinline__ void dp_item(const uint8_t* tl, const uint8_t* rec, const uint8_t* scp,
+                                        const uint8_t* zpp, int s0, int s1, int lane,
+                                        uint64_t* empty_bar, float (&y)[4 * MT]) {
+  constexpr int gs = 2 * R;
+  constexpr int RB = R < 32 ? R : 32;
+  constexpr int tok_stride = dp_tok_stride(gs);
+  const int r0 = s0 * kStepRows, r1 = s1 * kStepRows;
+  const uint2 sc = *reinterpret_cast<const uint2*>(scp + 8 * lane);
+  const uint32_t zz = *reinterpret_cast<const uint16_t*>(zpp + 2 * lane);
+  int sx[MT];
+  float esc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const uint8_t* rt = rec + (size_t)m * tok_stride;
+    const int* sums = reinterpret_cast<const int*>(rt + 2 * gs);
+    int a = 0;
+    for (int s = s0; s < s1; ++s) a += sums[s];
+    sx[m] = a;
+    esc[m] = *reinterpret_cast<const float*>(rt + 2 * gs + gs / 4);
+  }
+  int aL[MT][4], aH[MT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) aL[m][i] = aH[m][i] = 0;
+  if constexpr (R <= 32) {
+    uint32_t w[RB];
+    uint4 X[MT][RB / 4];
+    dp_load_rows<RB>(tl, 0, r0, r1, lane, w);
+    dp_load_x<MT, RB>(rec, tok_stride, 0, X);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);
+    dp_compute<MT, RB>(w, X, aL, aH);
+  } else {
+    for (int rb = 0; rb < R; rb += 32) {
+      if (rb >= r1 || rb + 32 <= r0) continue;
+      uint32_t w[32];
+      uint4 X[MT][8];
+      dp_load_rows<32>(tl, rb, r0, r1, lane, w);
+      dp_load_x<MT, 32>(rec, tok_stride, rb, X);
+      dp_compute<MT, 32>(w, X, aL, aH);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);
+  }
+  const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&sc.x));
+  const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&sc.y));
+  const float s[4] = {s01.x, s01.y, s23.x, s23.y};
+  const int z[4] = {(int)(zz & 15u), (int)((zz >> 4) & 15u), (int)((zz >> 8) & 15u),
+                    (int)((zz >> 12) & 15u)};
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      // sum_k xq_k * (q_k - z): exact in int32, then one rounding
+      const int t = aL[m][i] + (aH[m][i] >> 4) - z[i] * sx[m];
+      y[4 * m + i] = fmaf(s[i] * esc[m], (float)t, y[4 * m + i]);
+    }
+}
+
+// ---- split-K reduction -----------------------------------------------------------------------
+
+// Stores this lane's partial sums of a slice: dp2a path y[4 m + i] -> [m][4 lane + i];
+// tensor-core path y[4 i + c] -> [tokE][colbase + 4 i + c].
 template <int MT>
-__device__ void fixup_tile(const PhaseParams& P, int m, int wt, int slice, long long Wtot,
+__device__ __forceinline__ void store_partials(float* slot, const float (&y)[4 * MT], int lane,
+                                               int tokE, int colbase) {
+  if constexpr (MT <= 2) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      *reinterpret_cast<float4*>(slot + m * kTileCols + 4 * lane) =
+          make_float4(y[4 * m], y[4 * m + 1], y[4 * m + 2], y[4 * m + 3]);
+  } else {
+    float* dst = slot + tokE * kTileCols + colbase;
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+      *reinterpret_cast<float4*>(dst + 4 * i) =
+          make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+  }
+}
+
+// The last warp to finish a sub-tile: deterministic reduction of the partials + epilogue.
+template <int MT>
+__device__ void fixup_tile(const EngineParams& p, int ph, int wt, int slice, long long Wtot,
                            int lane, unsigned epoch) {
+  const PhaseParams& P = p.ph[ph];
+  const int m = p.m;
   for (int tok = 0; tok < MT; ++tok) {
     float acc[kMaxMats][4];
 #pragma unroll
     for (int mi = 0; mi < kMaxMats; ++mi) acc[mi][0] = acc[mi][1] = acc[mi][2] = acc[mi][3] = 0.f;
     for (int mi = 0; mi < P.nmat; ++mi) {
       const long long cu = (long long)wt * P.nmat + mi;
-      const int ns = nseg_of_cu(P, cu, Wtot);
-      const float* base =
-          P.partials + (((size_t)cu * P.maxseg * kSlices + slice) * MT + tok) * 128 + 4 * lane;
+      const int ns = red_segments(p, ph, cu, Wtot);
+      const float* base = partial_slot<MT>(P, cu, 0, slice) + tok * kTileCols + 4 * lane;
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      for (int s = 0; s < ns; ++s) {
-        const float4 v =
-            __ldcg(reinterpret_cast<const float4*>(base + (size_t)s * kSlices * MT * 128));
-        a0 += v.x;
-        a1 += v.y;
-        a2 += v.z;
-        a3 += v.w;
+      // eight segments' loads in flight at a time; the sum stays in segment order
+      for (int s0 = 0; s0 < ns; s0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          v[i] = s0 + i < ns ? __ldcg(reinterpret_cast<const float4*>(
+                                   base + (size_t)(s0 + i) * kSlices * MT * kTileCols))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          a0 += v[i].x;
+          a1 += v[i].y;
+          a2 += v[i].z;
+          a3 += v[i].w;
+        }
       }
       acc[mi][0] = a0;
       acc[mi][1] = a1;
@@ -425,54 +650,36 @@ __device__ void fixup_tile(const PhaseParams& P, int m, int wt, int slice, long 
   }
 }
 
-// Global address of this lane's partial sums for segment `b` of column unit `cu`.
-template <int MT>
-__device__ __forceinline__ float* segment_partials(const PhaseParams& P, int cu, long long b,
-                                                   long long Wtot, int slice, int tokE, int colbase) {
-  const long long W = phase_ctas(P, Wtot);
-  const long long a = (long long)cu * P.groups * P.spg;
-  const int seg = (int)(b - cta_of_unit(a, P.units, W));
-  return P.partials + ((((size_t)cu * P.maxseg + seg) * kSlices + slice) * MT + tokE) * 128 + colbase;
-}
-
-// Counts one finished segment of sub-tile (wt, slice); returns true to the last of them.
-__device__ __forceinline__ bool count_segment(const PhaseParams& P, int wt, int slice,
+// Counts one finished segment of sub-tile (wt, slice) of phase ph's reduction; returns true
+// to the last of them.
+__device__ __forceinline__ bool count_segment(const EngineParams& p, int ph, int wt, int slice,
                                               long long Wtot) {
+  const PhaseParams& P = p.ph[ph];
   unsigned total = 0;
   for (int mi = 0; mi < P.nmat; ++mi)
-    total += (unsigned)nseg_of_cu(P, (long long)wt * P.nmat + mi, Wtot);
+    total += (unsigned)red_segments(p, ph, (long long)wt * P.nmat + mi, Wtot);
   const unsigned prev = atomicAdd(&P.counters[wt * kSlices + slice], 1u);
   return prev == total - 1;
 }
 
+// End of a CTA's range in phase ph: store the segment, count it, reduce if last.
 template <int MT>
-__device__ __forceinline__ void flush_segment(const PhaseParams& P, int m, int cu, long long b,
+__device__ __forceinline__ void flush_segment(const EngineParams& p, int ph, int cu, long long b,
                                               long long Wtot, int slice, float (&y)[4 * MT],
                                               int lane, int tokE, int colbase, unsigned epoch) {
-  const long long W = phase_ctas(P, Wtot);
-  const long long a = (long long)cu * P.groups * P.spg;
-  const int seg = (int)(b - cta_of_unit(a, P.units, W));
+  const PhaseParams& P = p.ph[ph];
+  const int seg = segment_index(p, ph, cu, b, Wtot);
   const int wt = cu >> (P.nmat - 1);
   const int sub = wt * kSlices + slice;
-  float* dst =
-      P.partials + ((((size_t)cu * P.maxseg + seg) * kSlices + slice) * MT + tokE) * 128 + colbase;
-#pragma unroll
-  for (int i = 0; i < MT; ++i)
-    *reinterpret_cast<float4*>(dst + 4 * i) = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+  store_partials<MT>(partial_slot<MT>(P, cu, seg, slice), y, lane, tokE, colbase);
   __threadfence();
   __syncwarp();
   unsigned last = 0;
-  if (lane == 0) {
-    unsigned total = 0;
-    for (int mi = 0; mi < P.nmat; ++mi)
-      total += (unsigned)nseg_of_cu(P, (long long)wt * P.nmat + mi, Wtot);
-    const unsigned prev = atomicAdd(&P.counters[sub], 1u);
-    last = (prev == total - 1) ? 1u : 0u;
-  }
+  if (lane == 0) last = count_segment(p, ph, wt, slice, Wtot) ? 1u : 0u;
   last = __shfl_sync(0xffffffffu, last, 0);
   if (last) {
     __threadfence();
-    fixup_tile<MT>(P, m, wt, slice, Wtot, lane, epoch);
+    fixup_tile<MT>(p, ph, wt, slice, Wtot, lane, epoch);
     __syncwarp();
     if (lane == 0) atomicExch(&P.counters[sub], 0u);
   }
@@ -607,7 +814,7 @@ constexpr int kFlushSlots = 4;  // flush events in flight between the consumers 
 // An item ends its column unit in the middle of the CTA's range of the phase (its split-K
 // segment is handed to the flush warp) rather than at the end of the range.
 __device__ __forceinline__ bool mid_range_flush(const PhaseParams& P, const ItemIter& it) {
-  return it.grp == P.groups - 1 && it.i != it.n - 1;
+  return it.grp == P.g1 - 1 && it.i != it.n - 1;
 }
 
 template <int MT>
@@ -619,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ unsigned s_epoch;
   __shared__ volatile long long s_armed;   // items whose weights the weight warp has armed
   __shared__ volatile int s_wdone;         // weight warp has left its loop (s_armed final)
-  __shared__ volatile int s_records;       // this CTA's phase-0 records are written
+  __shared__ volatile int s_records;       // this CTA's prologue records are written
   __shared__ volatile int s_abort;
   __shared__ volatile int s_never;         // stays 0: a wait that must not be cut short
   __shared__ uint64_t s_fbar[kFlushSlots];  // mid-range flush events (kNC consumer arrivals)
@@ -712,7 +919,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // only items whose weights are armed (their slot is free and the full barrier is in
       // the phase this arrival belongs to)
       bool go = F < s_armed;
-      if (go && fi.ph == 0 && p.rec0_smem) {
+      const PhaseParams& P = p.ph[fi.ph];
+      if (go && P.ready_in == nullptr && p.rec0_smem) {
         // the consumers read this item's record from shared memory: complete the arrival
         if (lane == 0) mbar_arrive(&full[fslot]);
         __syncwarp();
@@ -723,7 +931,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       if (go) {
-        const PhaseParams& P = p.ph[fi.ph];
         if (P.ready_in == nullptr) {
           go = s_records != 0;
         } else {
@@ -733,7 +940,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (go) {
-        const PhaseParams& P = p.ph[fi.ph];
         fence_proxy_async();  // records were written by generic stores
         if (lane == 0) {
           uint8_t* aux = auxs + (size_t)fslot * p.aux_stage_bytes;
@@ -785,13 +991,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();  // the consumers' partial sums (acquired through the barrier)
         const int wt = hi.cu >> (P.nmat - 1);
         const int ns = active_slices(P, wt);
-        const bool last = lane < ns && count_segment(P, wt, lane, Ptot);
+        const bool last = lane < ns && count_segment(p, hi.ph, wt, lane, Ptot);
         unsigned won = __ballot_sync(0xffffffffu, last);
         if (won) __threadfence();
         while (won) {
           const int sl = __ffs(won) - 1;
           won &= won - 1;
-          fixup_tile<MT>(P, p.m, wt, sl, Ptot, lane, epoch);
+          fixup_tile<MT>(p, hi.ph, wt, sl, Ptot, lane, epoch);
           __syncwarp();
           if (lane == 0) atomicExch(&P.counters[wt * kSlices + sl], 0u);
         }
@@ -804,6 +1010,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------- consumer warps ------------------------------------
     const int slice = warp;
+    // tensor-core path lane roles
     const int g = lane >> 2, t = lane & 3, q = g >> 1;
     const int cB = 2 * (q % MT) + (g & 1);
     const int tokE = t % MT;
@@ -825,31 +1032,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       trace_event(p, 1);
     }
 
-    for (int ph = 0; ph < p.nphases && ok; ++ph) {
+    float y[4 * MT];
+#pragma unroll
+    for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+    int D[8][4];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) D[r][0] = D[r][1] = D[r][2] = D[r][3] = 0;
+    int cur_ph = -1;
+    while (ok && it.ph < p.nphases) {
+      const int ph = it.ph;
       const PhaseParams& P = p.ph[ph];
-      int D[8][4];
-      float y[4 * MT];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) D[r][0] = D[r][1] = D[r][2] = D[r][3] = 0;
-#pragma unroll
-      for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
-      const int kbg = P.spg >= 4 ? P.spg / 4 : 1;    // 32-pair blocks per group
-      const int nrows = P.spg >= 4 ? 32 : 8 * P.spg;  // valid rows per block
-      while (it.ph == ph) {
-        if (!wait_slot(&full[slot], parity, &s_abort, p.err, p.timeout_ns)) {
-          ok = false;
-          s_abort = 1;
-          break;
-        }
-        if (consumed == 0 && threadIdx.x == 0) trace_event(p, 9);
-        const int wt = it.cu >> (P.nmat - 1);
-        const bool active = slice < active_slices(P, wt);
-        const uint8_t* ax = auxs + (size_t)slot * p.aux_stage_bytes;
+      if (ph != cur_ph) {
+        if (cur_ph >= 0 && threadIdx.x == 0) trace_event(p, 3 + (cur_ph ? 2 : 0));
+        cur_ph = ph;
+      }
+      if (!wait_slot(&full[slot], parity, &s_abort, p.err, p.timeout_ns)) {
+        ok = false;
+        s_abort = 1;
+        break;
+      }
+      if (consumed == 0 && threadIdx.x == 0) trace_event(p, 9);
+      const int wt = it.cu >> (P.nmat - 1);
+      const bool active = slice < active_slices(P, wt);
+      const uint8_t* ax = auxs + (size_t)slot * p.aux_stage_bytes;
+      const uint8_t* tl = tiles + (size_t)slot * p.tile_stage_bytes + slice * kTileCols;
+      const uint8_t* rec = (P.ready_in == nullptr && p.rec0_smem)
+                               ? rec0s + (size_t)it.grp * P.frag_bytes
+                               : frag_slot(const_cast<uint8_t*>(ax));
+      if constexpr (MT <= 2) {
         if (active) {
-          const uint8_t* tl = tiles + (size_t)slot * p.tile_stage_bytes + slice * kTileCols;
-          const uint8_t* rec = (ph == 0 && p.rec0_smem)
-                                   ? rec0s + (size_t)it.grp * P.frag_bytes
-                                   : frag_slot(const_cast<uint8_t*>(ax));
+          const uint8_t* scp = ax + slice * kScaleBytes;
+          const uint8_t* zpp = ax + kSlices * kScaleBytes + slice * kZeroBytes;
+          switch (P.gs) {
+            case 16: dp_item<MT, 8>(tl, rec, scp, zpp, it.s0, it.s1, lane, &empty[slot], y); break;
+            case 32: dp_item<MT, 16>(tl, rec, scp, zpp, it.s0, it.s1, lane, &empty[slot], y); break;
+            case 64: dp_item<MT, 32>(tl, rec, scp, zpp, it.s0, it.s1, lane, &empty[slot], y); break;
+            default: dp_item<MT, 64>(tl, rec, scp, zpp, it.s0, it.s1, lane, &empty[slot], y); break;
+          }
+        } else {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+      } else {
+        if (active) {
+          const int kbg = P.spg >= 4 ? P.spg / 4 : 1;    // 32-pair blocks per group
+          const int nrows = P.spg >= 4 ? 32 : 8 * P.spg;  // valid rows per block
           const uint4* rb = reinterpret_cast<const uint4*>(rec);
           const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
           for (int kb = 0; kb < kbg; ++kb) {
@@ -865,46 +1092,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
-        ++consumed;
-        if (++slot == S) {
-          slot = 0;
-          parity ^= 1u;
-        }
-        const int cu = it.cu;
-        const bool mid = mid_range_flush(P, it);
-        const bool last_of_range = it.i == it.n - 1;
-        iter_next(it, p, b, Ptot);
-        if (mid) {
-          // store the partial sums and hand the segment to the flush warp
-          if (active) {
-            float* dst = segment_partials<MT>(P, cu, b, Ptot, slice, tokE, colbase);
-#pragma unroll
-            for (int i = 0; i < MT; ++i)
-              *reinterpret_cast<float4*>(dst + 4 * i) =
-                  make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
-          }
-#pragma unroll
-          for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
-          __syncwarp();
-          if (lane == 0) {
-            // the event slot is free once the flush warp has completed event fk - kFlushSlots
-            const uint64_t t0 = global_timer_ns();
-            while (s_fdone < fk - kFlushSlots + 1 && !s_abort) {
-              if (global_timer_ns() - t0 > p.timeout_ns) {
-                atomicOr(p.err, kErrFlagWait);
-                s_abort = 1;
-                break;
-              }
-            }
-            mbar_arrive(&s_fbar[fk % kFlushSlots]);
-          }
-          ++fk;
-        } else if (last_of_range && active) {
-          flush_segment<MT>(P, p.m, cu, b, Ptot, slice, y, lane, tokE, colbase, epoch);
-        }
       }
-      if (threadIdx.x == 0) trace_event(p, 3 + 2 * ph);
+      ++consumed;
+      if (++slot == S) {
+        slot = 0;
+        parity ^= 1u;
+      }
+      const int cu = it.cu;
+      const bool mid = mid_range_flush(P, it);
+      const bool last_of_range = it.i == it.n - 1;
+      iter_next(it, p, b, Ptot);
+      if (mid) {
+        // store the partial sums and hand the segment to the flush warp
+        if (active)
+          store_partials<MT>(partial_slot<MT>(P, cu, segment_index(p, ph, cu, b, Ptot), slice), y,
+                             lane, tokE, colbase);
+#pragma unroll
+        for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+        __syncwarp();
+        if (lane == 0) {
+          // the event slot is free once the flush warp has completed event fk - kFlushSlots
+          const uint64_t t0 = global_timer_ns();
+          while (s_fdone < fk - kFlushSlots + 1 && !s_abort) {
+            if (global_timer_ns() - t0 > p.timeout_ns) {
+              atomicOr(p.err, kErrFlagWait);
+              s_abort = 1;
+              break;
+            }
+          }
+          mbar_arrive(&s_fbar[fk % kFlushSlots]);
+        }
+        ++fk;
+      } else if (last_of_range) {
+        if (active)
+          flush_segment<MT>(p, ph, cu, b, Ptot, slice, y, lane, tokE, colbase, epoch);
+#pragma unroll
+        for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+      }
     }
+    if (threadIdx.x == 0) trace_event(p, 5);
   }
   __syncthreads();
   if (warp < kNC) {
@@ -964,23 +1190,23 @@ size_t engine_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes, 
          (size_t)rec0_bytes;
 }
 
+// Deepest ring that fits (bytes in flight are what keeps HBM busy), with the prologue
+// records in shared memory when they fit beside it.
 bool engine_plan_smem(int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes, int smem_limit,
                       int* stages, int* rec0_smem, size_t* smem) {
-  for (int s = 5; s >= 4; --s) {
-    const size_t need = engine_smem_bytes(s, tile_stage_bytes, aux_stage_bytes, rec0_bytes);
-    if (need <= (size_t)smem_limit) {
+  for (int s = kMaxStages; s >= 2; --s) {
+    const size_t with = engine_smem_bytes(s, tile_stage_bytes, aux_stage_bytes, rec0_bytes);
+    if (with <= (size_t)smem_limit) {
       *stages = s;
       *rec0_smem = 1;
-      *smem = need;
+      *smem = with;
       return true;
     }
-  }
-  for (int s = 5; s >= 2; --s) {
-    const size_t need = engine_smem_bytes(s, tile_stage_bytes, aux_stage_bytes, 0);
-    if (need <= (size_t)smem_limit) {
+    const size_t without = engine_smem_bytes(s, tile_stage_bytes, aux_stage_bytes, 0);
+    if (without <= (size_t)smem_limit) {
       *stages = s;
       *rec0_smem = 0;
-      *smem = need;
+      *smem = without;
       return true;
     }
   }

@@ -1,17 +1,23 @@
 // tk_engine.h -- parameters shared by the host launcher and the persistent INT4 engine.
 //
-// The engine runs one or two "phases" of INT4 fused-dequant GEMV in one persistent,
+// The engine runs a list of "phases" of INT4 fused-dequant GEMV in one persistent,
 // cooperative launch (one CTA per SM):
 //   qmatmul_int4 (src/kernels/shaders.zig:442-501):   prologue(x -> records) | phase 0
 //   INT4 FFN (src/bench.zig:266-341 + down proj):     prologue(rmsnorm(x) -> records) |
-//                                                     phase 0 gate+up -> silu*up -> h |
-//                                                     phase 1 down (+ residual)
+//                                                     gate+up over tile range 0 -> silu*up -> h |
+//                                                     ... | gate+up over tile range P-1 |
+//                                                     down over the h groups of range 0 | ... |
+//                                                     down over the h groups of range P-1
+// A phase covers the wide tiles [wt0, wt1) of N and the groups [g0, g1) of K of its matrices.
 // Work unit = one k-step (16 k values = 8 packed rows) of a 1024-column wide tile of one
-// matrix; each CTA owns a contiguous range of units (stream-K) and its 8 consumer warps
-// take one 128-column slice each.  Partial sums of a 128-column sub-tile are reduced
-// deterministically (in CTA order) by the last warp to finish it.  There is no grid-wide
-// barrier: every CTA builds its own phase-0 activation records, and a phase-1 record is
-// consumed only after its producer sub-tile has published a ready flag for this launch.
+// matrix; each CTA owns a contiguous range of every phase's units (stream-K) and its 8
+// consumer warps take one 128-column slice each.  Partial sums of a 128-column sub-tile are
+// reduced deterministically (in phase and CTA order) by the last warp to finish it; the
+// phases [red_first, red_first + red_count) add into the same outputs.  There is no
+// grid-wide barrier: every CTA builds its own prologue records, and a record of h is consumed
+// only after its producer sub-tile has published a ready flag for this launch.  Splitting the
+// gate/up tiles into P ranges lets the down projection of range j run while later ranges are
+// still being reduced.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -27,7 +33,8 @@ constexpr int kStepRows = 8;     // packed rows (k pairs) per k-step
 // 128 in shared memory and the fragment loads are bank-conflict free.
 constexpr int kRowBytes = 1040;
 constexpr int kRowElems = kRowBytes / 8;  // u64 elements per box row
-constexpr int kMaxPhases = 2;
+constexpr int kMaxPhases = 8;
+constexpr int kMaxStages = 16;  // ring stages per CTA (the deepest that fits is taken)
 constexpr int kMaxMats = 2;
 constexpr int kScaleBytes = kTileCols * 2;  // f16 scales of one slice, one group
 constexpr int kZeroBytes = kTileCols / 2;   // packed zero points of one slice, one group
@@ -41,7 +48,7 @@ constexpr int kTraceEvents = 10;
 constexpr unsigned kErrTmaWait = 1u;
 constexpr unsigned kErrFlagWait = 2u;
 
-// One group's activation record (the B operand of the int8 tensor-core MMA):
+// One group's activation record for the int8 tensor-core path (MT = 4):
 //   uint4 b[kbg][4 (t)][2*MT (token, hi/lo)]   kbg = max(1, gs / 64) blocks of 32 k pairs;
 //         .x/.y = high-nibble B (odd k) for kappa halves 0/1, .z/.w = low-nibble B (even k),
 //         each an int8 hi or lo part, 4 k pairs per word
@@ -50,6 +57,20 @@ constexpr unsigned kErrFlagWait = 2u;
 // padded to 16 bytes.
 __host__ __device__ constexpr int frag_record_bytes(int spg, int mt) {
   return (128 * mt * (spg >= 4 ? spg / 4 : 1) + 8 * mt * spg + 4 * mt + 15) & ~15;
+}
+
+// One group's activation record for the dp2a path (MT = 1, 2), per token (token stride
+// dp_tok_stride(gs)): the group's gs values quantised to int16 with one power-of-two scale
+// (max |x| * 2^e in [2^14, 2^15)),
+//   uint2 X[gs / 4]   X[j] = {x[4j] | x[4j+2] << 16, x[4j+1] | x[4j+3] << 16}: the even-k and
+//                     odd-k halves of packed rows 2j, 2j+1 as dp2a's two 16-bit lanes
+//   int   sums[spg]   sum of the quantised values over each 16-k step (zero points)
+//   float esc         2^-e
+__host__ __device__ constexpr int dp_tok_stride(int gs) { return (2 * gs + gs / 4 + 4 + 15) & ~15; }
+
+// Record bytes per group for MT tokens on the path the engine takes for MT.
+__host__ __device__ constexpr int record_bytes(int gs, int mt) {
+  return mt <= 2 ? mt * dp_tok_stride(gs) : frag_record_bytes(gs / 16, mt);
 }
 
 enum EpilogueKind : int {
@@ -67,20 +88,25 @@ struct SyncState {
 
 struct PhaseParams {
   int K, N, gs, nmat;
-  int spg;      // k-steps per group = gs / 16
-  int groups;   // K / gs
-  int tiles;    // wide tiles: ceil(N / 1024); the last may have fewer than 8 slices
+  int spg;          // k-steps per group = gs / 16
+  int wt0, wt1;     // wide tiles [wt0, wt1) of N
+  int g0, g1;       // groups [g0, g1) of K
+  int tiles;        // wt1 - wt0; the last tile of N may have fewer than 8 slices
+  int groups;       // g1 - g0
   long long units;  // tiles * nmat * groups * spg
+  int red_first;    // phases [red_first, red_first + red_count) reduce into the same outputs
+  int red_count;
   int map_base;     // tensor maps of matrix i: map[map_base + 2i] (group box), +1 (step box)
   const uint16_t* scales[kMaxMats];
   const uint8_t* zeros[kMaxMats];
-  const uint8_t* frag_in;     // activation records, one per group of K
+  const uint8_t* frag_in;     // activation records, one per group of K (global group index)
   long long frag_cta_stride;  // bytes between CTAs' private copies (0: one shared copy)
   int frag_bytes;
-  const unsigned* ready_in;   // per 128-value sub-tile of K: record ready when == epoch + 1
-  float* partials;         // [tiles*nmat][maxseg][kSlices][MT][128]
-  unsigned* counters;      // [N / 128] per sub-tile, zero between launches
-  int maxseg;
+  const unsigned* ready_in;   // per 128-value sub-tile of K: record ready when == epoch + 1;
+                              // null: the records are the prologue's
+  float* partials;         // [N/1024 * nmat][maxseg][kSlices][MT][128], shared by the reduction
+  unsigned* counters;      // [N / 128] per sub-tile, zero between launches, shared likewise
+  int maxseg;              // segments per column unit summed over the reduction's phases
   int epi;
   float* out;              // kEpiStore: y; kEpiSiluMul: optional h
   int ldo;

@@ -1,7 +1,7 @@
 // tk_ptx.cuh -- thin inline-PTX wrappers used by the sm_100a kernels.
 //
 // mbarrier transaction barriers, TMA (cp.async.bulk / cp.async.bulk.tensor) loads
-// into shared memory, L2 eviction hints, the m16n8k16 f16 tensor-core MMA, and a
+// into shared memory, L2 eviction hints, the m16n8k32 int8 tensor-core MMA, dp2a, and a
 // bounded wait helper.  No cluster multicast is used anywhere in this project.
 #pragma once
 #include <cstdint>
@@ -138,6 +138,18 @@ __device__ __forceinline__ void mma_16832_u8s8(int (&d)[4], uint32_t a0, uint32_
 }
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return __byte_perm(a, b, sel);
+}
+// Two-way dot product: c + a.h0 * b.byte0 + a.h1 * b.byte1, a = two signed 16-bit lanes,
+// b = four unsigned bytes (dp2a_hi uses bytes 2 and 3).
+__device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 }  // namespace tk

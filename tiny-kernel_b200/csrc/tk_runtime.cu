@@ -74,6 +74,7 @@ struct tk_device {
   int smem_optin = 0;
   unsigned long long timeout_ns = kDefaultTimeoutNs;
   int stages_override = 0;
+  int ffn_split = 1;  // gate/up tile ranges of the FFN (TK_FFN_SPLIT, 1..4)
   SyncState* sync = nullptr;
   unsigned* err = nullptr;
   ScratchBuf frag[2];
@@ -199,36 +200,62 @@ int max_segments(const PhaseParams& P, long long Wtot) {
   return mx;
 }
 
-void fill_phase(PhaseParams& P, int K, int N, int gs, int nmat, int mt) {
+// One phase over the wide tiles [wt0, wt1) of N and the groups [g0, g1) of K (all of them
+// when wt1 / g1 are negative); a reduction of its own until bind_partials says otherwise.
+void fill_phase(PhaseParams& P, int K, int N, int gs, int nmat, int mt, int wt0 = 0, int wt1 = -1,
+                int g0 = 0, int g1 = -1) {
   std::memset(&P, 0, sizeof(P));
   P.K = K;
   P.N = N;
   P.gs = gs;
   P.nmat = nmat;
   P.spg = gs / 16;
-  P.groups = K / gs;
-  P.tiles = (N + kWideCols - 1) / kWideCols;
+  P.wt0 = wt0;
+  P.wt1 = wt1 < 0 ? (N + kWideCols - 1) / kWideCols : wt1;
+  P.g0 = g0;
+  P.g1 = g1 < 0 ? K / gs : g1;
+  P.tiles = P.wt1 - P.wt0;
+  P.groups = P.g1 - P.g0;
   P.units = (long long)P.tiles * nmat * P.groups * P.spg;
-  P.frag_bytes = frag_record_bytes(P.spg, mt);
+  P.frag_bytes = record_bytes(gs, mt);
 }
 
-// Sizes the split-K scratch of phase `idx` and points P at it.
-int bind_phase_scratch(tk_device* d, PhaseParams& P, int idx, int mt, long long Wtot) {
-  P.maxseg = max_segments(P, Wtot);
-  const size_t pbytes =
-      (size_t)P.tiles * P.nmat * P.maxseg * kSlices * mt * kTileCols * sizeof(float);
+// Split-K scratch of phases [first, first + count) of p, which run over the same matrices:
+// one partials buffer indexed by global column unit and one counter per 128-column sub-tile.
+// combined: the phases cover disjoint groups of the same outputs and form one reduction (its
+// segments are the phases' segments in phase order); otherwise each phase covers its own
+// tiles and is a reduction of its own.
+int bind_partials(tk_device* d, EngineParams& p, int first, int count, int idx, int mt,
+                  long long Wtot, bool combined) {
+  int maxseg = 0;
+  for (int q = first; q < first + count; ++q) {
+    const int ms = max_segments(p.ph[q], Wtot);
+    maxseg = combined ? maxseg + ms : std::max(maxseg, ms);
+  }
+  const PhaseParams& F = p.ph[first];
+  const size_t tiles_all = (size_t)(F.N + kWideCols - 1) / kWideCols;
+  const size_t pbytes = tiles_all * F.nmat * maxseg * kSlices * mt * kTileCols * sizeof(float);
   int st = scratch_ensure(d, d->partials[idx], pbytes);
   if (st != TK_OK) return st;
-  st = scratch_ensure(d, d->counters[idx], (size_t)(P.N / kTileCols) * sizeof(unsigned));
+  st = scratch_ensure(d, d->counters[idx], (size_t)(F.N / kTileCols) * sizeof(unsigned));
   if (st != TK_OK) return st;
-  P.partials = static_cast<float*>(d->partials[idx].ptr);
-  P.counters = static_cast<unsigned*>(d->counters[idx].ptr);
+  for (int q = first; q < first + count; ++q) {
+    PhaseParams& P = p.ph[q];
+    P.maxseg = maxseg;
+    P.partials = static_cast<float*>(d->partials[idx].ptr);
+    P.counters = static_cast<unsigned*>(d->counters[idx].ptr);
+    P.red_first = combined ? first : q;
+    P.red_count = combined ? count : 1;
+  }
   return TK_OK;
 }
 
 int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, cudaStream_t st) {
-  const int spg_max = std::max(p.ph[0].spg, p.nphases > 1 ? p.ph[1].spg : 0);
-  int fb_max = std::max(p.ph[0].frag_bytes, p.nphases > 1 ? p.ph[1].frag_bytes : 0);
+  int spg_max = 0, fb_max = 0;
+  for (int q = 0; q < p.nphases; ++q) {
+    spg_max = std::max(spg_max, p.ph[q].spg);
+    fb_max = std::max(fb_max, p.ph[q].frag_bytes);
+  }
   p.tile_stage_bytes = (spg_max * kStepRows * kRowBytes + 127) & ~127;
   p.aux_stage_bytes = (kSlices * (kScaleBytes + kZeroBytes) + fb_max + 15) & ~15;
   int stages = 0, rec0_smem = 0;
@@ -277,12 +304,12 @@ int qmatmul_engine_chunk(tk_device* d, const float* x, const uint8_t* w, const u
   P.map_base = 0;
   P.scales[0] = s;
   P.zeros[0] = z;
-  const long long rec_stride = (long long)P.groups * P.frag_bytes;  // per-CTA records
+  const long long rec_stride = (long long)(k / gs) * P.frag_bytes;  // per-CTA records
   int stt = scratch_ensure(d, d->frag[0], (size_t)Wtot * rec_stride);
   if (stt != TK_OK) return stt;
   P.frag_in = static_cast<const uint8_t*>(d->frag[0].ptr);
   P.frag_cta_stride = rec_stride;
-  stt = bind_phase_scratch(d, P, 0, mt, Wtot);
+  stt = bind_partials(d, p, 0, 1, 0, mt, Wtot, false);
   if (stt != TK_OK) return stt;
   P.epi = kEpiStore;
   P.out = out;
@@ -311,46 +338,57 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   EngineParams p;
   std::memset(&p, 0, sizeof(p));
   p.m = m;
-  p.nphases = 2;
-  PhaseParams& A = p.ph[0];
-  PhaseParams& B = p.ph[1];
-  fill_phase(A, hidden, inter, gs, 2, mt);
-  fill_phase(B, inter, hidden, gs, 1, mt);
-  A.map_base = 0;  // gate: maps 0,1; up: maps 2,3
-  A.scales[0] = gate->scales;
-  A.scales[1] = up->scales;
-  A.zeros[0] = gate->zeros;
-  A.zeros[1] = up->zeros;
-  B.map_base = 4;  // down: maps 4,5
-  B.scales[0] = down->scales;
-  B.zeros[0] = down->zeros;
-  const long long rec_stride = (long long)A.groups * A.frag_bytes;  // per-CTA records
+  // gate/up over nsplit tile ranges, then the down projection over the h groups of each
+  // range in the same order: the down work of early ranges runs while the last range's
+  // sub-tiles are still being reduced
+  const int tiles_i = (inter + kWideCols - 1) / kWideCols;
+  const int nsplit = std::max(1, std::min({d->ffn_split, tiles_i, kMaxPhases / 2}));
+  p.nphases = 2 * nsplit;
+  const int groups_h = inter / gs;
+  const long long rec_stride = (long long)(hidden / gs) * record_bytes(gs, mt);  // per-CTA records
   int stt = scratch_ensure(d, d->frag[0], (size_t)Wtot * rec_stride);
   if (stt != TK_OK) return stt;
-  stt = scratch_ensure(d, d->frag[1], (size_t)B.groups * B.frag_bytes);
+  stt = scratch_ensure(d, d->frag[1], (size_t)groups_h * record_bytes(gs, mt));
   if (stt != TK_OK) return stt;
   stt = scratch_ensure(d, d->ready, (size_t)(inter / kTileCols) * sizeof(unsigned));
   if (stt != TK_OK) return stt;
-  A.frag_in = static_cast<const uint8_t*>(d->frag[0].ptr);
-  A.frag_cta_stride = rec_stride;
-  B.frag_in = static_cast<const uint8_t*>(d->frag[1].ptr);
-  B.ready_in = static_cast<const unsigned*>(d->ready.ptr);
-  stt = bind_phase_scratch(d, A, 0, mt, Wtot);
+  for (int j = 0; j < nsplit; ++j) {
+    const int t0 = tiles_i * j / nsplit, t1 = tiles_i * (j + 1) / nsplit;
+    PhaseParams& A = p.ph[j];
+    fill_phase(A, hidden, inter, gs, 2, mt, t0, t1);
+    A.map_base = 0;  // gate: maps 0,1; up: maps 2,3
+    A.scales[0] = gate->scales;
+    A.scales[1] = up->scales;
+    A.zeros[0] = gate->zeros;
+    A.zeros[1] = up->zeros;
+    A.frag_in = static_cast<const uint8_t*>(d->frag[0].ptr);
+    A.frag_cta_stride = rec_stride;
+    A.epi = kEpiSiluMul;
+    A.out = h_out;
+    A.ldo = inter;
+    A.frag_out = static_cast<uint8_t*>(d->frag[1].ptr);
+    A.ready_out = static_cast<unsigned*>(d->ready.ptr);
+    A.next_gs = gs;
+    A.next_frag_bytes = record_bytes(gs, mt);
+    const int g0 = std::min(groups_h, t0 * kWideCols / gs);
+    const int g1 = j == nsplit - 1 ? groups_h : std::min(groups_h, t1 * kWideCols / gs);
+    PhaseParams& B = p.ph[nsplit + j];
+    fill_phase(B, inter, hidden, gs, 1, mt, 0, -1, g0, g1);
+    B.map_base = 4;  // down: maps 4,5
+    B.scales[0] = down->scales;
+    B.zeros[0] = down->zeros;
+    B.frag_in = static_cast<const uint8_t*>(d->frag[1].ptr);
+    B.ready_in = static_cast<const unsigned*>(d->ready.ptr);
+    B.epi = kEpiStore;
+    B.out = out;
+    B.ldo = hidden;
+    B.residual = residual ? x : nullptr;
+    B.ldr = hidden;
+  }
+  stt = bind_partials(d, p, 0, nsplit, 0, mt, Wtot, false);
   if (stt != TK_OK) return stt;
-  stt = bind_phase_scratch(d, B, 1, mt, Wtot);
+  stt = bind_partials(d, p, nsplit, nsplit, 1, mt, Wtot, true);
   if (stt != TK_OK) return stt;
-  A.epi = kEpiSiluMul;
-  A.out = h_out;
-  A.ldo = inter;
-  A.frag_out = static_cast<uint8_t*>(d->frag[1].ptr);
-  A.ready_out = static_cast<unsigned*>(d->ready.ptr);
-  A.next_gs = gs;
-  A.next_frag_bytes = B.frag_bytes;
-  B.epi = kEpiStore;
-  B.out = out;
-  B.ldo = hidden;
-  B.residual = residual ? x : nullptr;
-  B.ldr = hidden;
   p.x = x;
   p.ldx = hidden;
   p.K0 = hidden;
@@ -360,7 +398,7 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   p.frag0 = static_cast<uint8_t*>(d->frag[0].ptr);
   p.frag0_cta_stride = rec_stride;
   p.gs0 = gs;
-  p.frag0_bytes = A.frag_bytes;
+  p.frag0_bytes = record_bytes(gs, mt);
   TmapPack maps;
   std::memset(&maps, 0, sizeof(maps));
   stt = matrix_tmaps(d, gate->w_packed, inter, hidden, gs, maps, 0);
@@ -421,6 +459,7 @@ int tk_device_create(int ordinal, tk_device** out) {
   d->sm_count = d->prop.multiProcessorCount;
   d->smem_optin = (int)d->prop.sharedMemPerBlockOptin;
   if (const char* env = std::getenv("TK_ENGINE_STAGES")) d->stages_override = std::atoi(env);
+  if (const char* env = std::getenv("TK_FFN_SPLIT")) d->ffn_split = std::atoi(env);
   if (const char* env = std::getenv("TK_WAIT_TIMEOUT_MS"))
     d->timeout_ns = (unsigned long long)std::atoll(env) * 1000000ull;
   if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -781,6 +820,8 @@ int noalloc_engine_chunk(unsigned char* scratch, int sm_count, int smem_optin, c
   PhaseParams& P = p.ph[0];
   fill_phase(P, k, n, gs, 1, mt);
   P.maxseg = max_segments(P, Wtot);
+  P.red_first = 0;
+  P.red_count = 1;
   // layout: launch state | error word | tile counters | partials | per-CTA records
   const size_t off_err = align256(sizeof(SyncState));
   const size_t off_cnt = off_err + 256;
