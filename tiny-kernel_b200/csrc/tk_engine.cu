@@ -30,15 +30,17 @@
 //        y += scale * v.
 //    - m = 3, 4 (the int8 tensor-core path): m16n8k32 u8 x s8 MMAs on nibble planes
 //      against activations split into int8 hi + lo / 256 parts.
-//  * Split-K partial sums go to a scratch buffer; the last warp to finish a 128-column
-//    sub-tile (an atomic counter per sub-tile) adds the partials in phase and CTA order
-//    (deterministic) and runs the epilogue: store (+ residual), or silu(gate) * up -> the
-//    next phase's records plus a ready flag for that sub-tile.
-//  * No grid-wide barrier: every CTA builds its own prologue records; the record warp
-//    issues a record copy for an h group only once the flag of its h sub-tile equals
-//    epoch + 1 (epoch = launches completed, advanced by the last CTA to finish).  The FFN
-//    splits gate/up into tile ranges so the down projection of an early range overlaps
-//    the reduction of the last one.
+//  * Split-K partial sums go to a scratch buffer and each finished segment bumps a counter
+//    per 128-column sub-tile.  An output sub-tile is reduced (in phase and CTA order, so
+//    deterministically) by the warp that counts its last segment, which stores y
+//    (+ residual).  The gate/up sub-tiles are not reduced by their producers: the record warp
+//    of every CTA that needs an h sub-tile waits for its counter to be complete, reduces it
+//    in the same fixed order, applies silu(gate) * up and writes its items' records straight
+//    into their stages -- two L2 round trips between the last gate/up segment and the down
+//    projection.  The last CTA to finish returns those counters to zero.
+//  * No grid-wide barrier: every CTA builds its own prologue records.  The FFN splits
+//    gate/up into tile ranges so the down projection of an early range overlaps the
+//    production of the last one.
 // Every spin-wait is bounded by a global-timer timeout and reports through p.err.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -52,47 +54,56 @@ namespace {
 
 constexpr int kNC = kSlices;  // consumer warps: one per 128-column slice
 
+// The phase list as the kernel reads it: a copy in shared memory (dynamic indexing into the
+// kernel parameters would go through the constant cache on every access).
+struct PhaseTable {
+  const PhaseParams* ph;
+  int n;
+};
+
 // ---- stream-K bookkeeping --------------------------------------------------------------
 
+// Stream-K arithmetic is 32-bit: the host admits a phase only when units * CTAs < 2^31, so
+// every product below fits (64-bit division is a long software sequence on the GPU).
+
 // CTA whose stream-K range holds unit u (ranges [U*b/W, U*(b+1)/W), all non-empty)
-__device__ __forceinline__ long long cta_of_unit(long long u, long long units, long long W) {
-  return ((u + 1) * W - 1) / units;
+__device__ __forceinline__ int cta_of_unit(unsigned u, unsigned units, unsigned W) {
+  return (int)(((u + 1) * W - 1) / units);
 }
 
-__device__ __forceinline__ long long phase_ctas(const PhaseParams& P, long long Wtot) {
-  return P.units < Wtot ? P.units : Wtot;
+__device__ __forceinline__ unsigned phase_ctas(const PhaseParams& P, unsigned Wtot) {
+  return (unsigned)P.units < Wtot ? (unsigned)P.units : Wtot;
 }
 
 // Number of CTA ranges of phase P holding units of (global) column unit cu = wide tile *
 // nmat + matrix; 0 when the phase does not cover cu.
-__device__ __forceinline__ int nseg_of_cu(const PhaseParams& P, long long cu, long long Wtot) {
-  const long long c = cu - (long long)P.wt0 * P.nmat;
-  if (c < 0 || c >= (long long)P.tiles * P.nmat) return 0;
-  const long long W = phase_ctas(P, Wtot);
-  const long long per = (long long)P.groups * P.spg;
-  const long long a = c * per;
-  return (int)(cta_of_unit(a + per - 1, P.units, W) - cta_of_unit(a, P.units, W) + 1);
+__device__ __forceinline__ int nseg_of_cu(const PhaseParams& P, int cu, unsigned Wtot) {
+  const int c = cu - P.wt0 * P.nmat;
+  if (c < 0 || c >= P.tiles * P.nmat) return 0;
+  const unsigned W = phase_ctas(P, Wtot), U = (unsigned)P.units;
+  const unsigned per = (unsigned)(P.groups * P.spg);
+  const unsigned a = (unsigned)c * per;
+  return cta_of_unit(a + per - 1, U, W) - cta_of_unit(a, U, W) + 1;
 }
 
 // Segments of column unit cu summed over the phases that reduce together with phase ph.
-__device__ __forceinline__ int red_segments(const EngineParams& p, int ph, long long cu,
-                                            long long Wtot) {
-  const PhaseParams& P = p.ph[ph];
+__device__ __forceinline__ int red_segments(const PhaseTable& T, int ph, int cu, unsigned Wtot) {
+  const PhaseParams& P = T.ph[ph];
   int n = 0;
-  for (int q = P.red_first; q < P.red_first + P.red_count; ++q) n += nseg_of_cu(p.ph[q], cu, Wtot);
+  for (int q = P.red_first; q < P.red_first + P.red_count; ++q) n += nseg_of_cu(T.ph[q], cu, Wtot);
   return n;
 }
 
 // Index within its reduction of CTA b's segment of column unit cu in phase ph (earlier
 // phases of the reduction first, then CTA order).
-__device__ __forceinline__ int segment_index(const EngineParams& p, int ph, long long cu,
-                                             long long b, long long Wtot) {
-  const PhaseParams& P = p.ph[ph];
+__device__ __forceinline__ int segment_index(const PhaseTable& T, int ph, int cu, int b,
+                                             unsigned Wtot) {
+  const PhaseParams& P = T.ph[ph];
   int off = 0;
-  for (int q = P.red_first; q < ph; ++q) off += nseg_of_cu(p.ph[q], cu, Wtot);
-  const long long W = phase_ctas(P, Wtot);
-  const long long a = (cu - (long long)P.wt0 * P.nmat) * P.groups * P.spg;
-  return off + (int)(b - cta_of_unit(a, P.units, W));
+  for (int q = P.red_first; q < ph; ++q) off += nseg_of_cu(T.ph[q], cu, Wtot);
+  const unsigned W = phase_ctas(P, Wtot);
+  const unsigned a = (unsigned)(cu - P.wt0 * P.nmat) * (unsigned)(P.groups * P.spg);
+  return off + b - cta_of_unit(a, (unsigned)P.units, W);
 }
 
 __device__ __forceinline__ int active_slices(const PhaseParams& P, int wtile) {
@@ -102,35 +113,51 @@ __device__ __forceinline__ int active_slices(const PhaseParams& P, int wtile) {
 
 // Partial sums of segment `seg` of column unit cu, slice `slice`: [MT][128] floats.
 template <int MT>
-__device__ __forceinline__ float* partial_slot(const PhaseParams& P, long long cu, int seg,
-                                               int slice) {
+__device__ __forceinline__ float* partial_slot(const PhaseParams& P, int cu, int seg, int slice) {
   return P.partials + (((size_t)cu * P.maxseg + seg) * kSlices + slice) * MT * kTileCols;
 }
 
-// Walks one CTA's items (one group of one wide tile each) through all phases.
+// Walks one CTA's items (one group of one wide tile each) through all phases.  The fields of
+// the current phase that per-item paths read are copied in at the phase switch: a shared-memory
+// read on a per-item path waits behind the consumers' bulk of stage reads.
 struct ItemIter {
   int ph;       // phase of the current item; == nphases when exhausted
   int i, n;     // index within the phase, items in the phase
   int cu, grp;  // global column unit (tile * nmat + mat) and global group of the item
   int s0, s1;   // k-step range of the current item within its group
   int last_s1;  // s1 of the phase's last item
+  int nmat, g0, g1, spg, N, frag_bytes, epi;
+  bool rec_pro;  // the phase's records are the prologue's (else built from partial sums)
 };
 
-__device__ __forceinline__ void iter_seek(ItemIter& it, const EngineParams& p, long long w,
-                                          long long Wtot) {
-  while (it.ph < p.nphases) {
-    const PhaseParams& P = p.ph[it.ph];
-    const long long W = phase_ctas(P, Wtot);
-    if (w < W) {
-      const long long beg = P.units * w / W, end = P.units * (w + 1) / W;
-      const long long fg0 = beg / P.spg, fgl = (end - 1) / P.spg;
-      const long long cl = fg0 / P.groups;
+// Slices of the current item's wide tile that hold columns (8 except in a ragged last tile).
+__device__ __forceinline__ int item_slices(const ItemIter& it) {
+  const int rem = (it.N - (it.cu >> (it.nmat - 1)) * kWideCols) / kTileCols;
+  return rem < kSlices ? rem : kSlices;
+}
+
+__device__ __forceinline__ void iter_seek(ItemIter& it, const PhaseTable& T, int w, unsigned Wtot) {
+  while (it.ph < T.n) {
+    const PhaseParams& P = T.ph[it.ph];
+    const unsigned W = phase_ctas(P, Wtot), U = (unsigned)P.units;
+    if ((unsigned)w < W) {
+      const unsigned beg = U * (unsigned)w / W, end = U * (unsigned)(w + 1) / W;
+      const unsigned fg0 = beg / (unsigned)P.spg, fgl = (end - 1) / (unsigned)P.spg;
+      const unsigned cl = fg0 / (unsigned)P.groups;
+      it.nmat = P.nmat;
+      it.g0 = P.g0;
+      it.g1 = P.g1;
+      it.spg = P.spg;
+      it.N = P.N;
+      it.frag_bytes = P.frag_bytes;
+      it.epi = P.epi;
+      it.rec_pro = P.src_count == 0;
       it.i = 0;
       it.n = (int)(fgl - fg0 + 1);
-      it.cu = (int)(cl + (long long)P.wt0 * P.nmat);
-      it.grp = P.g0 + (int)(fg0 - cl * P.groups);
-      it.s0 = (int)(beg - fg0 * P.spg);
-      it.last_s1 = (int)(end - fgl * P.spg);
+      it.cu = (int)cl + P.wt0 * P.nmat;
+      it.grp = P.g0 + (int)(fg0 - cl * (unsigned)P.groups);
+      it.s0 = (int)(beg - fg0 * (unsigned)P.spg);
+      it.last_s1 = (int)(end - fgl * (unsigned)P.spg);
       it.s1 = it.n == 1 ? it.last_s1 : P.spg;
       return;
     }
@@ -138,62 +165,67 @@ __device__ __forceinline__ void iter_seek(ItemIter& it, const EngineParams& p, l
   }
 }
 
-__device__ __forceinline__ void iter_start(ItemIter& it, const EngineParams& p, long long w,
-                                           long long Wtot) {
+__device__ __forceinline__ void iter_start(ItemIter& it, const PhaseTable& T, int w, unsigned Wtot) {
   it.ph = 0;
   it.i = it.n = it.cu = it.grp = it.s0 = it.s1 = it.last_s1 = 0;
-  iter_seek(it, p, w, Wtot);
+  it.nmat = 1;
+  it.g0 = it.g1 = it.spg = it.N = it.frag_bytes = it.epi = 0;
+  it.rec_pro = true;
+  iter_seek(it, T, w, Wtot);
 }
 
-__device__ __forceinline__ void iter_next(ItemIter& it, const EngineParams& p, long long w,
-                                          long long Wtot) {
-  const PhaseParams& P = p.ph[it.ph];
+__device__ __forceinline__ void iter_next(ItemIter& it, const PhaseTable& T, int w, unsigned Wtot) {
   if (++it.i < it.n) {
-    if (++it.grp == P.g1) {
-      it.grp = P.g0;
+    if (++it.grp == it.g1) {
+      it.grp = it.g0;
       ++it.cu;
     }
     it.s0 = 0;
-    it.s1 = it.i == it.n - 1 ? it.last_s1 : P.spg;
+    it.s1 = it.i == it.n - 1 ? it.last_s1 : it.spg;
     return;
   }
   ++it.ph;
-  iter_seek(it, p, w, Wtot);
+  iter_seek(it, T, w, Wtot);
 }
 
 // Bytes the weight warp's copies bring into a stage for item `it` (box rows, scales, zeros);
 // the record warp adds the activation record (P.frag_bytes).
-__device__ __forceinline__ uint32_t item_weight_bytes(const PhaseParams& P, const ItemIter& it) {
-  const int ns = active_slices(P, it.cu >> (P.nmat - 1));
-  return (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes + ns * (kScaleBytes + kZeroBytes));
+__device__ __forceinline__ uint32_t item_weight_bytes(const ItemIter& it) {
+  return (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes +
+                    item_slices(it) * (kScaleBytes + kZeroBytes));
 }
+
+// The weight warp's copy of its current phase's pointers.
+struct WeightPhase {
+  int map_base;
+  const uint16_t* scales[kMaxMats];
+  const uint8_t* zeros[kMaxMats];
+};
 
 // Weight-warp lane `lane` issues its share of item `it`'s weight-side copies: lane 0 the TMA
 // box(es), lane 8 the scales, lane 9 the zero points.
-__device__ __forceinline__ void issue_weights(const TmapPack& maps, const PhaseParams& P,
+__device__ __forceinline__ void issue_weights(const TmapPack& maps, const WeightPhase& W,
                                               const ItemIter& it, uint8_t* tile, uint8_t* aux,
                                               uint64_t* bar, uint64_t pol, int lane) {
-  const int mat = it.cu & (P.nmat - 1);
-  const int wt = it.cu >> (P.nmat - 1);
+  const int mat = it.cu & (it.nmat - 1);
+  const int wt = it.cu >> (it.nmat - 1);
   const int col0 = wt * kWideCols;
   if (lane == 0) {
-    const int row0 = it.grp * P.spg * kStepRows;
+    const int row0 = it.grp * it.spg * kStepRows;
     const int x = wt * (kWideCols / 8);  // u64 element of the tile's first byte
-    if (it.s0 == 0 && it.s1 == P.spg) {
-      tma_load_2d(tile, &maps.map[P.map_base + 2 * mat], bar, x, row0, pol);
+    if (it.s0 == 0 && it.s1 == it.spg) {
+      tma_load_2d(tile, &maps.map[W.map_base + 2 * mat], bar, x, row0, pol);
     } else {
       for (int s = it.s0; s < it.s1; ++s)
-        tma_load_2d(tile + s * kStepRows * kRowBytes, &maps.map[P.map_base + 2 * mat + 1], bar, x,
+        tma_load_2d(tile + s * kStepRows * kRowBytes, &maps.map[W.map_base + 2 * mat + 1], bar, x,
                     row0 + s * kStepRows, pol);
     }
   } else if (lane == 8) {
-    const int ns = active_slices(P, wt);
-    bulk_load(aux, P.scales[mat] + (size_t)it.grp * P.N + col0, (uint32_t)(ns * kScaleBytes), bar,
-              pol);
+    bulk_load(aux, W.scales[mat] + (size_t)it.grp * it.N + col0,
+              (uint32_t)(item_slices(it) * kScaleBytes), bar, pol);
   } else if (lane == 9) {
-    const int ns = active_slices(P, wt);
-    bulk_load(aux + kSlices * kScaleBytes, P.zeros[mat] + (size_t)it.grp * (P.N / 2) + col0 / 2,
-              (uint32_t)(ns * kZeroBytes), bar, pol);
+    bulk_load(aux + kSlices * kScaleBytes, W.zeros[mat] + (size_t)it.grp * (it.N / 2) + col0 / 2,
+              (uint32_t)(item_slices(it) * kZeroBytes), bar, pol);
   }
 }
 
@@ -201,10 +233,17 @@ __device__ __forceinline__ uint8_t* frag_slot(uint8_t* aux) {
   return aux + kSlices * (kScaleBytes + kZeroBytes);
 }
 
-__device__ __forceinline__ void issue_frag(const PhaseParams& P, const ItemIter& it, long long b,
+// The record warp's copy of its current phase's record source.
+struct RecordPhase {
+  const uint8_t* frag_in;
+  long long frag_cta_stride;
+  int src_first, src_count;
+};
+
+__device__ __forceinline__ void issue_frag(const RecordPhase& R, const ItemIter& it, int b,
                                            uint8_t* aux, uint64_t* bar, uint64_t pol) {
-  bulk_load(frag_slot(aux), P.frag_in + b * P.frag_cta_stride + (size_t)it.grp * P.frag_bytes,
-            (uint32_t)P.frag_bytes, bar, pol);
+  bulk_load(frag_slot(aux), R.frag_in + b * R.frag_cta_stride + (size_t)it.grp * it.frag_bytes,
+            (uint32_t)it.frag_bytes, bar, pol);
 }
 
 __device__ __forceinline__ void trace_event(const EngineParams& p, int ev) {
@@ -221,7 +260,8 @@ __device__ __forceinline__ void trace_event(const EngineParams& p, int ev) {
 // and split into int8 hi + lo / 256 parts.
 template <int MT>
 __device__ __forceinline__ void build_records_mma(const float (&v)[4], int tok, int gs,
-                                                  uint8_t* rec, int rec_bytes, int lane) {
+                                                  uint8_t* rec, int rec_bytes, int lane,
+                                                  int gi_only) {
   const int gl = gs >> 2;  // lanes per group
   // k pairs 2l and 2l + 1 of the chunk: odd k (high nibble) and even k (low nibble)
   const float b[4] = {v[1], v[0], v[3], v[2]};
@@ -259,7 +299,8 @@ __device__ __forceinline__ void build_records_mma(const float (&v)[4], int tok, 
   uint32_t q_even = __shfl_xor_sync(0xffffffffu, p_even, 4);
   if (gl <= 4) q_odd = q_even = 0u;
   uint8_t* r = rec + (size_t)gi * rec_bytes;
-  if (j == 0) {
+  const bool store = gi_only < 0 || gi == gi_only;
+  if (j == 0 && store) {
     const uint32_t o1h = (p_odd & 0xffffu) | (q_odd << 16);
     const uint32_t o1l = (p_odd >> 16) | (q_odd & 0xffff0000u);
     const uint32_t o2h = (p_even & 0xffffu) | (q_even << 16);
@@ -286,8 +327,8 @@ __device__ __forceinline__ void build_records_mma(const float (&v)[4], int tok, 
   const int spg = gs >> 4;
   const int kbg = spg >= 4 ? spg / 4 : 1;
   int2* sums = reinterpret_cast<int2*>(r + 128 * MT * kbg);
-  if ((lg & 3) == 0) sums[(lg >> 2) * MT + tok] = make_int2(sh, sl);
-  if (lg == 0) reinterpret_cast<float*>(sums + spg * MT)[tok] = down;
+  if ((lg & 3) == 0 && store) sums[(lg >> 2) * MT + tok] = make_int2(sh, sl);
+  if (lg == 0 && store) reinterpret_cast<float*>(sums + spg * MT)[tok] = down;
 }
 
 // dp2a path.  Warp-collective, same lane contract as build_records_mma: lane l holds values
@@ -295,7 +336,8 @@ __device__ __forceinline__ void build_records_mma(const float (&v)[4], int tok, 
 // group's record (its four values are k = 4lg..4lg+3 of the group: packed rows 2lg, 2lg+1).
 template <int MT>
 __device__ __forceinline__ void build_records_dp(const float (&v)[4], int tok, int gs,
-                                                 uint8_t* rec, int rec_bytes, int lane) {
+                                                 uint8_t* rec, int rec_bytes, int lane,
+                                                 int gi_only) {
   const int gl = gs >> 2;  // lanes per group
   float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
   for (int off = 1; off < gl; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -312,23 +354,27 @@ __device__ __forceinline__ void build_records_dp(const float (&v)[4], int tok, i
     q[i] = t < -32767 ? -32767 : (t > 32767 ? 32767 : t);
   }
   const int gi = lane / gl, lg = lane - gi * gl;
+  const bool store = gi_only < 0 || gi == gi_only;
   uint8_t* r = rec + (size_t)gi * rec_bytes + (size_t)tok * dp_tok_stride(gs);
-  reinterpret_cast<uint2*>(r)[lg] =
-      make_uint2(((uint32_t)q[0] & 0xffffu) | ((uint32_t)q[2] << 16),
-                 ((uint32_t)q[1] & 0xffffu) | ((uint32_t)q[3] << 16));
+  if (store)
+    reinterpret_cast<uint2*>(r)[lg] =
+        make_uint2(((uint32_t)q[0] & 0xffffu) | ((uint32_t)q[2] << 16),
+                   ((uint32_t)q[1] & 0xffffu) | ((uint32_t)q[3] << 16));
   // per 16-k step (4 lanes): the sum of the quantised values, for the zero-point term
   int s = q[0] + q[1] + q[2] + q[3];
   s += __shfl_xor_sync(0xffffffffu, s, 1);
   s += __shfl_xor_sync(0xffffffffu, s, 2);
-  if ((lg & 3) == 0) reinterpret_cast<int*>(r + 2 * gs)[lg >> 2] = s;
-  if (lg == 0) *reinterpret_cast<float*>(r + 2 * gs + gs / 4) = down;
+  if ((lg & 3) == 0 && store) reinterpret_cast<int*>(r + 2 * gs)[lg >> 2] = s;
+  if (lg == 0 && store) *reinterpret_cast<float*>(r + 2 * gs + gs / 4) = down;
 }
 
+// Records of the groups of a 128-value chunk (all of them, or only group gi_only: the other
+// lanes still take part in the shuffles but store nothing).
 template <int MT>
 __device__ __forceinline__ void build_records(const float (&v)[4], int tok, int gs, uint8_t* rec,
-                                              int rec_bytes, int lane) {
-  if constexpr (MT <= 2) build_records_dp<MT>(v, tok, gs, rec, rec_bytes, lane);
-  else build_records_mma<MT>(v, tok, gs, rec, rec_bytes, lane);
+                                              int rec_bytes, int lane, int gi_only = -1) {
+  if constexpr (MT <= 2) build_records_dp<MT>(v, tok, gs, rec, rec_bytes, lane, gi_only);
+  else build_records_mma<MT>(v, tok, gs, rec, rec_bytes, lane, gi_only);
 }
 
 // ---- int8 tensor-core path (m = 3, 4) ------------------------------------------------------
@@ -490,68 +536,55 @@ __device__ __forceinline__ void dp_compute(const uint32_t (&w)[RB], const uint4 
   }
 }
 
-// One item of one slice on the dp2a path: R = packed rows per group (gs / 2).  Loads every
-// stage byte it needs, releases the stage (empty barrier), then computes; groups of 128 k
-// (R = 64) are computed in two 32-row blocks before the release.  y[4 m + i] accumulates
-// column 4 lane + i of token m.
-template <int MT, int R>
-__device__ __forceinline__ void dp_item(const uint8_t* tl, const uint8_t* rec, const uint8_t* scp,
-                                        const uint8_t* zpp, int s0, int s1, int lane,
-                                        uint64_t* empty_bar, float (&y)[4 * MT]) {
-  constexpr int gs = 2 * R;
-  constexpr int RB = R < 32 ? R : 32;
-  constexpr int tok_stride = dp_tok_stride(gs);
-  const int r0 = s0 * kStepRows, r1 = s1 * kStepRows;
-  const uint2 sc = *reinterpret_cast<const uint2*>(scp + 8 * lane);
-  const uint32_t zz = *reinterpret_cast<const uint16_t*>(zpp + 2 * lane);
+// Per-item values of the dp2a path that stay in registers from the item's first loads to its
+// epilogue: this lane's 4 scales and 4 zero points, and per token the sum of the quantised
+// activations over the item's k-steps and 2^-e.
+template <int MT>
+struct DpMeta {
+  uint2 sc;
+  uint32_t zz;
   int sx[MT];
   float esc[MT];
+};
+
+template <int MT, int GS>
+__device__ __forceinline__ void dp_load_meta(const uint8_t* ax, const uint8_t* rec, int slice,
+                                             int lane, int s0, int s1, DpMeta<MT>& M) {
+  constexpr int tok_stride = dp_tok_stride(GS);
+  constexpr int spg = GS / 16;
+  M.sc = *reinterpret_cast<const uint2*>(ax + slice * kScaleBytes + 8 * lane);
+  M.zz = *reinterpret_cast<const uint16_t*>(ax + kSlices * kScaleBytes + slice * kZeroBytes + 2 * lane);
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     const uint8_t* rt = rec + (size_t)m * tok_stride;
-    const int* sums = reinterpret_cast<const int*>(rt + 2 * gs);
+    const int* sums = reinterpret_cast<const int*>(rt + 2 * GS);
     int a = 0;
-    for (int s = s0; s < s1; ++s) a += sums[s];
-    sx[m] = a;
-    esc[m] = *reinterpret_cast<const float*>(rt + 2 * gs + gs / 4);
-  }
-  int aL[MT][4], aH[MT][4];
 #pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) aL[m][i] = aH[m][i] = 0;
-  if constexpr (R <= 32) {
-    uint32_t w[RB];
-    uint4 X[MT][RB / 4];
-    dp_load_rows<RB>(tl, 0, r0, r1, lane, w);
-    dp_load_x<MT, RB>(rec, tok_stride, 0, X);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty_bar);
-    dp_compute<MT, RB>(w, X, aL, aH);
-  } else {
-    for (int rb = 0; rb < R; rb += 32) {
-      if (rb >= r1 || rb + 32 <= r0) continue;
-      uint32_t w[32];
-      uint4 X[MT][8];
-      dp_load_rows<32>(tl, rb, r0, r1, lane, w);
-      dp_load_x<MT, 32>(rec, tok_stride, rb, X);
-      dp_compute<MT, 32>(w, X, aL, aH);
+    for (int s = 0; s < spg; ++s) {
+      const int v = sums[s];
+      a += (s >= s0 && s < s1) ? v : 0;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty_bar);
+    M.sx[m] = a;
+    M.esc[m] = *reinterpret_cast<const float*>(rt + 2 * GS + GS / 4);
   }
-  const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&sc.x));
-  const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&sc.y));
+}
+
+// y[4 m + i] (column 4 lane + i of token m) += scale * 2^-e * sum_k xq_k * (q_k - z)
+template <int MT>
+__device__ __forceinline__ void dp_epilogue(const DpMeta<MT>& M, const int (&aL)[MT][4],
+                                            const int (&aH)[MT][4], float (&y)[4 * MT]) {
+  const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&M.sc.x));
+  const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&M.sc.y));
   const float s[4] = {s01.x, s01.y, s23.x, s23.y};
-  const int z[4] = {(int)(zz & 15u), (int)((zz >> 4) & 15u), (int)((zz >> 8) & 15u),
-                    (int)((zz >> 12) & 15u)};
+  const int z[4] = {(int)(M.zz & 15u), (int)((M.zz >> 4) & 15u), (int)((M.zz >> 8) & 15u),
+                    (int)((M.zz >> 12) & 15u)};
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      // sum_k xq_k * (q_k - z): exact in int32, then one rounding
-      const int t = aL[m][i] + (aH[m][i] >> 4) - z[i] * sx[m];
-      y[4 * m + i] = fmaf(s[i] * esc[m], (float)t, y[4 * m + i]);
+      // exact in int32, then one rounding
+      const int t = aL[m][i] + (aH[m][i] >> 4) - z[i] * M.sx[m];
+      y[4 * m + i] = fmaf(s[i] * M.esc[m], (float)t, y[4 * m + i]);
     }
 }
 
@@ -576,122 +609,125 @@ __device__ __forceinline__ void store_partials(float* slot, const float (&y)[4 *
   }
 }
 
-// The last warp to finish a sub-tile: deterministic reduction of the partials + epilogue.
+// Sums this lane's 4 columns of token `tok` over the segments of one sub-tile of a reduction:
+// ns0 segments of column unit cu0 into a0 and, when two_mats, ns1 segments of cu0 + 1 into a1
+// (a single matrix takes 16 segments per batch into a0).  16 loads in flight per batch; the
+// sums run in a fixed order, so every warp that reduces a sub-tile gets the same bits.
 template <int MT>
-__device__ void fixup_tile(const EngineParams& p, int ph, int wt, int slice, long long Wtot,
-                           int lane, unsigned epoch) {
-  const PhaseParams& P = p.ph[ph];
-  const int m = p.m;
-  for (int tok = 0; tok < MT; ++tok) {
-    float acc[kMaxMats][4];
+__device__ __forceinline__ void sum_partials(const PhaseParams& P, int cu0, int ns0,
+                                             int ns1, bool two_mats, int slice, int tok, int lane,
+                                             float4& a0, float4& a1) {
+  constexpr size_t kSegStride = (size_t)kSlices * MT * kTileCols;
+  constexpr int kB = 8;
+  const float* base0 = partial_slot<MT>(P, cu0, 0, slice) + tok * kTileCols + 4 * lane;
+  const float* base1 =
+      two_mats ? partial_slot<MT>(P, cu0 + 1, 0, slice) + tok * kTileCols + 4 * lane : base0;
+  if (!two_mats) ns1 = ns0;
+  const int step = two_mats ? kB : 2 * kB;
+  a0 = make_float4(0.f, 0.f, 0.f, 0.f);
+  a1 = a0;
+  for (int s0 = 0; s0 < ns0 || s0 < ns1; s0 += step) {
+    const int s1 = two_mats ? s0 : s0 + kB;  // first segment of the batch's second half
+    float4 v0[kB], v1[kB];
 #pragma unroll
-    for (int mi = 0; mi < kMaxMats; ++mi) acc[mi][0] = acc[mi][1] = acc[mi][2] = acc[mi][3] = 0.f;
-    for (int mi = 0; mi < P.nmat; ++mi) {
-      const long long cu = (long long)wt * P.nmat + mi;
-      const int ns = red_segments(p, ph, cu, Wtot);
-      const float* base = partial_slot<MT>(P, cu, 0, slice) + tok * kTileCols + 4 * lane;
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      // eight segments' loads in flight at a time; the sum stays in segment order
-      for (int s0 = 0; s0 < ns; s0 += 8) {
-        float4 v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          v[i] = s0 + i < ns ? __ldcg(reinterpret_cast<const float4*>(
-                                   base + (size_t)(s0 + i) * kSlices * MT * kTileCols))
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          a0 += v[i].x;
-          a1 += v[i].y;
-          a2 += v[i].z;
-          a3 += v[i].w;
-        }
-      }
-      acc[mi][0] = a0;
-      acc[mi][1] = a1;
-      acc[mi][2] = a2;
-      acc[mi][3] = a3;
+    for (int i = 0; i < kB; ++i) {
+      v0[i] = s0 + i < ns0 ? __ldcg(reinterpret_cast<const float4*>(base0 + (s0 + i) * kSegStride))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      v1[i] = s1 + i < ns1 ? __ldcg(reinterpret_cast<const float4*>(base1 + (s1 + i) * kSegStride))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    const int sub0 = wt * kWideCols + slice * kTileCols;  // first column of the sub-tile
-    const int col = sub0 + 4 * lane;
-    if (P.epi == kEpiStore) {
-      if (tok < m) {
-        float4 o = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-        if (P.residual) {
-          const float4 r = *reinterpret_cast<const float4*>(P.residual + (size_t)tok * P.ldr + col);
-          o.x = r.x + o.x;
-          o.y = r.y + o.y;
-          o.z = r.z + o.z;
-          o.w = r.w + o.w;
-        }
-        *reinterpret_cast<float4*>(P.out + (size_t)tok * P.ldo + col) = o;
-      }
-    } else {
-      float h[4];
+    float4 t0 = make_float4(0.f, 0.f, 0.f, 0.f), t1 = t0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float gv = acc[0][i];
-        h[i] = (tok < m) ? gv / (1.0f + expf(-gv)) * acc[1][i] : 0.f;
-      }
-      if (P.out && tok < m)
-        *reinterpret_cast<float4*>(P.out + (size_t)tok * P.ldo + col) = make_float4(h[0], h[1], h[2], h[3]);
-      build_records<MT>(h, tok, P.next_gs,
-                        P.frag_out + (size_t)(sub0 / P.next_gs) * P.next_frag_bytes,
-                        P.next_frag_bytes, lane);
+    for (int i = 0; i < kB; ++i) {
+      t0.x += v0[i].x;
+      t0.y += v0[i].y;
+      t0.z += v0[i].z;
+      t0.w += v0[i].w;
+      t1.x += v1[i].x;
+      t1.y += v1[i].y;
+      t1.z += v1[i].z;
+      t1.w += v1[i].w;
+    }
+    a0.x += t0.x;
+    a0.y += t0.y;
+    a0.z += t0.z;
+    a0.w += t0.w;
+    if (two_mats) {
+      a1.x += t1.x;
+      a1.y += t1.y;
+      a1.z += t1.z;
+      a1.w += t1.w;
+    } else {
+      a0.x += t1.x;
+      a0.y += t1.y;
+      a0.z += t1.z;
+      a0.w += t1.w;
     }
   }
-  if (P.epi == kEpiSiluMul) {
-    fence_proxy_async();  // the records are read by other CTAs through TMA
-    __syncwarp();
-    if (lane == 0) {
-      __threadfence();
-      atomicExch(&P.ready_out[wt * kSlices + slice], epoch + 1);
+}
+
+// The last warp to finish an output sub-tile (kEpiStore): reduction of the partials + store.
+template <int MT, int GS>
+__device__ void fixup_tile(const EngineParams& p, const PhaseTable& T, int ph, int wt, int slice,
+                           unsigned Wtot, int lane) {
+  const PhaseParams& P = T.ph[ph];
+  const int cu0 = wt * P.nmat;
+  const int ns0 = red_segments(T, ph, cu0, Wtot);
+  const int ns1 = P.nmat > 1 ? red_segments(T, ph, cu0 + 1, Wtot) : 0;
+  const int col = wt * kWideCols + slice * kTileCols + 4 * lane;
+  for (int tok = 0; tok < MT; ++tok) {
+    float4 a0, a1;
+    sum_partials<MT>(P, cu0, ns0, ns1, P.nmat > 1, slice, tok, lane, a0, a1);
+    if (tok < p.m) {
+      if (P.residual) {
+        const float4 r = *reinterpret_cast<const float4*>(P.residual + (size_t)tok * P.ldr + col);
+        a0.x = r.x + a0.x;
+        a0.y = r.y + a0.y;
+        a0.z = r.z + a0.z;
+        a0.w = r.w + a0.w;
+      }
+      *reinterpret_cast<float4*>(P.out + (size_t)tok * P.ldo + col) = a0;
     }
+  }
+}
+
+// h = silu(gate) * up for this lane's 4 columns of sub-tile (wt, slice) of the kEpiSiluMul
+// phase `a` (gate/up column units 2 wt, 2 wt + 1), every token (0 beyond the live ones).
+template <int MT>
+__device__ __forceinline__ void reduce_silu_mul(const PhaseTable& T, int a, int wt, int slice,
+                                                unsigned Wtot, int lane, int m,
+                                                float (&h)[MT][4]) {
+  const PhaseParams& A = T.ph[a];
+  const int cu0 = 2 * wt;
+  const int ns0 = red_segments(T, a, cu0, Wtot);
+  const int ns1 = red_segments(T, a, cu0 + 1, Wtot);
+#pragma unroll
+  for (int tok = 0; tok < MT; ++tok) {
+    float4 g, u;
+    sum_partials<MT>(A, cu0, ns0, ns1, true, slice, tok, lane, g, u);
+    const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[tok][i] = tok < m ? gv[i] / (1.0f + expf(-gv[i])) * uv[i] : 0.f;
   }
 }
 
 // Counts one finished segment of sub-tile (wt, slice) of phase ph's reduction; returns true
 // to the last of them.
-__device__ __forceinline__ bool count_segment(const EngineParams& p, int ph, int wt, int slice,
-                                              long long Wtot) {
-  const PhaseParams& P = p.ph[ph];
+__device__ __forceinline__ bool count_segment(const PhaseTable& T, int ph, int wt, int slice,
+                                              unsigned Wtot) {
+  const PhaseParams& P = T.ph[ph];
   unsigned total = 0;
   for (int mi = 0; mi < P.nmat; ++mi)
-    total += (unsigned)red_segments(p, ph, (long long)wt * P.nmat + mi, Wtot);
+    total += (unsigned)red_segments(T, ph, wt * P.nmat + mi, Wtot);
   const unsigned prev = atomicAdd(&P.counters[wt * kSlices + slice], 1u);
   return prev == total - 1;
-}
-
-// End of a CTA's range in phase ph: store the segment, count it, reduce if last.
-template <int MT>
-__device__ __forceinline__ void flush_segment(const EngineParams& p, int ph, int cu, long long b,
-                                              long long Wtot, int slice, float (&y)[4 * MT],
-                                              int lane, int tokE, int colbase, unsigned epoch) {
-  const PhaseParams& P = p.ph[ph];
-  const int seg = segment_index(p, ph, cu, b, Wtot);
-  const int wt = cu >> (P.nmat - 1);
-  const int sub = wt * kSlices + slice;
-  store_partials<MT>(partial_slot<MT>(P, cu, seg, slice), y, lane, tokE, colbase);
-  __threadfence();
-  __syncwarp();
-  unsigned last = 0;
-  if (lane == 0) last = count_segment(p, ph, wt, slice, Wtot) ? 1u : 0u;
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) {
-    __threadfence();
-    fixup_tile<MT>(p, ph, wt, slice, Wtot, lane, epoch);
-    __syncwarp();
-    if (lane == 0) atomicExch(&P.counters[sub], 0u);
-  }
-#pragma unroll
-  for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
 }
 
 // Consumer warps: x (optionally rmsnorm'ed, src/kernels/shaders.zig:16-56) -> records.
 // x and the norm weight are read first and the weight producer is held at named barrier 2
 // until every consumer has them in registers: reads issued after the weight stream starts
 // queue behind megabytes of TMA traffic.
-template <int MT>
+template <int MT, int GS>
 __device__ void prologue(const EngineParams& p, int warp, int lane, float* s_red, float* s_rms,
                          uint8_t* rec0s) {
   const int nchunks = p.K0 / kTileCols;
@@ -758,7 +794,7 @@ __device__ void prologue(const EngineParams& p, int warp, int lane, float* s_red
       v[2] = v[2] * rms[tok] * w.z;
       v[3] = v[3] * rms[tok] * w.w;
     }
-    build_records<MT>(v, tok, p.gs0, recs + (size_t)(ch * kTileCols / p.gs0) * p.frag0_bytes,
+    build_records<MT>(v, tok, GS, recs + (size_t)(ch * kTileCols / GS) * p.frag0_bytes,
                       p.frag0_bytes, lane);
   };
 #pragma unroll
@@ -801,36 +837,41 @@ __device__ __forceinline__ bool wait_slot(uint64_t* bar, uint32_t parity, const 
 
 // Warp roles: warps 0..kNC-1 consume stages, warp kNC (weight warp) streams the packed weights,
 // scales and zero points of every item, warp kNC+1 (record warp) copies each item's activation
-// record once it is ready, warp kNC+2 (flush warp) completes the split-K segments that end in
-// the middle of a CTA's range (the consumers only store their partial sums and move on; the
-// flush warp makes them visible, counts them and runs the tile epilogue when it is last).  Each
-// stage's full barrier takes one arrival from each producer warp.
+// record once it is ready, warp kNC+2 (flush warp) completes every split-K segment: the
+// consumers only store their partial sums and move on; the flush warp makes them visible and
+// counts them, and for each sub-tile whose last segment it counted it posts a fixup job to the
+// consumer warp of that slice, which runs it between items (the eight slices' reductions run in
+// parallel and no consumer waits on a global round trip of the counting).  Each stage's full
+// barrier takes one arrival from each producer warp.
 constexpr int kWeightWarp = kNC;
 constexpr int kRecordWarp = kNC + 1;
 constexpr int kFlushWarp = kNC + 2;
 constexpr int kThreads = (kNC + 3) * 32;
 constexpr int kFlushSlots = 4;  // flush events in flight between the consumers and the flush warp
+constexpr int kJobSlots = 16;   // fixup jobs in flight from the flush warp to one consumer warp
 
-// An item ends its column unit in the middle of the CTA's range of the phase (its split-K
-// segment is handed to the flush warp) rather than at the end of the range.
-__device__ __forceinline__ bool mid_range_flush(const PhaseParams& P, const ItemIter& it) {
-  return it.grp == P.g1 - 1 && it.i != it.n - 1;
+// An item ends a split-K segment: the last item of its column unit or of the CTA's range.
+__device__ __forceinline__ bool ends_segment(const ItemIter& it) {
+  return it.grp == it.g1 - 1 || it.i == it.n - 1;
 }
 
-template <int MT>
+template <int MT, int GS>
 __global__ void __launch_bounds__(kThreads, 1)
     int4_engine_kernel(const __grid_constant__ TmapPack maps, const __grid_constant__ EngineParams p) {
   extern __shared__ uint8_t smem_raw[];
+  __shared__ PhaseParams s_ph[kMaxPhases];
   __shared__ float s_red[MT * kNC];
   __shared__ float s_rms[MT];
-  __shared__ unsigned s_epoch;
   __shared__ volatile long long s_armed;   // items whose weights the weight warp has armed
   __shared__ volatile int s_wdone;         // weight warp has left its loop (s_armed final)
   __shared__ volatile int s_records;       // this CTA's prologue records are written
   __shared__ volatile int s_abort;
   __shared__ volatile int s_never;         // stays 0: a wait that must not be cut short
-  __shared__ uint64_t s_fbar[kFlushSlots];  // mid-range flush events (kNC consumer arrivals)
+  __shared__ uint64_t s_fbar[kFlushSlots];  // flush events (kNC consumer arrivals)
   __shared__ volatile int s_fdone;         // flush events the flush warp has completed
+  __shared__ volatile int s_job[kNC][kJobSlots];  // fixup jobs per slice: (phase << 16) | tile
+  __shared__ volatile int s_job_head[kNC];        // jobs posted (flush warp)
+  __shared__ volatile int s_job_tail[kNC];        // jobs done (consumer warp)
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.stages;
@@ -839,6 +880,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(auxs + (size_t)S * p.aux_stage_bytes);
   uint64_t* empty = full + S;
   uint8_t* rec0s = reinterpret_cast<uint8_t*>(empty + S) + 16 - (smem_addr(empty + S) & 15u);
+  {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.ph);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(s_ph);
+    const int words = p.nphases * (int)(sizeof(PhaseParams) / 4);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
+  const PhaseTable T{s_ph, p.nphases};
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 2);
@@ -846,19 +894,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kFlushSlots; ++i) mbar_init(&s_fbar[i], kNC);
     s_fdone = 0;
+    for (int i = 0; i < kNC; ++i) s_job_head[i] = s_job_tail[i] = 0;
     fence_mbar_init();
     s_records = 0;
     s_abort = 0;
     s_never = 0;
     s_armed = 0;
     s_wdone = 0;
-    s_epoch = ld_acquire_u32(&p.sync->epoch);
     trace_event(p, 0);
   }
   __syncthreads();
-  const unsigned epoch = s_epoch;
-  const long long Ptot = gridDim.x;
-  const long long b = blockIdx.x;
+  const unsigned Ptot = gridDim.x;
+  const int b = blockIdx.x;
   // consumer ring position (function scope for the drain at the end)
   int slot = 0;
   uint32_t parity = 0;
@@ -868,34 +915,52 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------- weight producer warp ---------------------------------
     const uint64_t pol_stream = l2_evict_first();
     ItemIter wi;
-    iter_start(wi, p, b, Ptot);
+    iter_start(wi, T, b, Ptot);
     long long G = 0;
     int wslot = 0;
     uint32_t wround = 0;
-    named_barrier(2, (kNC + 1) * 32);  // the consumers have read x
-    while (wi.ph < p.nphases) {
+    // The first two stages go out at once; the rest wait until the consumers have read x
+    // (reads issued behind megabytes of stage traffic would stall the prologue).
+    constexpr long long kEarlyStages = 2;
+    bool x_read = false;
+    WeightPhase W{};
+    int wph = -1;
+    while (wi.ph < T.n) {
+      if (!x_read && G >= kEarlyStages) {
+        named_barrier(2, (kNC + 1) * 32);
+        x_read = true;
+      }
       if (wround > 0 && !wait_slot(&empty[wslot], (wround - 1) & 1, &s_abort, p.err, p.timeout_ns)) {
         s_abort = 1;
         break;
       }
       if (s_abort) break;
-      const PhaseParams& P = p.ph[wi.ph];
+      if (wi.ph != wph) {
+        wph = wi.ph;
+        const PhaseParams& P = T.ph[wph];
+        W.map_base = P.map_base;
+        for (int i = 0; i < kMaxMats; ++i) {
+          W.scales[i] = P.scales[i];
+          W.zeros[i] = P.zeros[i];
+        }
+      }
       if (lane == 0) {
         if (G == 0) trace_event(p, 7);
-        mbar_arrive_expect_tx(&full[wslot], item_weight_bytes(P, wi));
+        mbar_arrive_expect_tx(&full[wslot], item_weight_bytes(wi));
       }
       __syncwarp();
-      issue_weights(maps, P, wi, tiles + (size_t)wslot * p.tile_stage_bytes,
+      issue_weights(maps, W, wi, tiles + (size_t)wslot * p.tile_stage_bytes,
                     auxs + (size_t)wslot * p.aux_stage_bytes, &full[wslot], pol_stream, lane);
       __syncwarp();
       ++G;
       if (lane == 0) s_armed = G;
-      iter_next(wi, p, b, Ptot);
+      iter_next(wi, T, b, Ptot);
       if (++wslot == S) {
         wslot = 0;
         ++wround;
       }
     }
+    if (!x_read) named_barrier(2, (kNC + 1) * 32);
     if (lane == 0) {
       s_armed = G;
       __threadfence_block();
@@ -904,51 +969,112 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kRecordWarp) {
     // ---------------------------- record producer warp ---------------------------------
+    // Prologue records: already in shared memory (plain arrival) or copied per item from this
+    // CTA's global copy.  Records of h: once the gate/up segment counter of the item's h
+    // sub-tile is complete, the warp reduces the sub-tile (kept for the sub-tile's other group)
+    // and writes the item's record straight into the stage.
     const uint64_t pol_keep = l2_evict_last();
     ItemIter fi;
-    iter_start(fi, p, b, Ptot);
+    iter_start(fi, T, b, Ptot);
     long long F = 0;
     int fslot = 0;
     bool aborted = false;
     uint64_t t_wait = 0;
-    while (fi.ph < p.nphases) {
+    RecordPhase RP{};
+    int rph = -1;
+    int h_sub = -1;   // h sub-tile whose values are in hv
+    int h_src = 0;    // its producing phase
+    float hv[MT][4];  // this lane's 4 h values of h_sub, per token
+    unsigned src_done = 0;  // producing phases seen complete (bit per phase): no more polls
+    while (fi.ph < T.n) {
       if (s_abort) {
         aborted = true;
         break;
       }
+      if (fi.ph != rph) {
+        rph = fi.ph;
+        const PhaseParams& P = T.ph[rph];
+        RP.frag_in = P.frag_in;
+        RP.frag_cta_stride = P.frag_cta_stride;
+        RP.src_first = P.src_first;
+        RP.src_count = P.src_count;
+      }
       // only items whose weights are armed (their slot is free and the full barrier is in
       // the phase this arrival belongs to)
       bool go = F < s_armed;
-      const PhaseParams& P = p.ph[fi.ph];
-      if (go && P.ready_in == nullptr && p.rec0_smem) {
+      if (go && fi.rec_pro && p.rec0_smem) {
         // the consumers read this item's record from shared memory: complete the arrival
         if (lane == 0) mbar_arrive(&full[fslot]);
         __syncwarp();
         ++F;
-        iter_next(fi, p, b, Ptot);
+        iter_next(fi, T, b, Ptot);
         fslot = fslot + 1 == S ? 0 : fslot + 1;
         t_wait = 0;
         continue;
       }
-      if (go) {
-        if (P.ready_in == nullptr) {
-          go = s_records != 0;
-        } else {
-          unsigned v = 0;
-          if (lane == 0) v = ld_acquire_u32(&P.ready_in[fi.grp * P.gs / kTileCols]);
-          go = __shfl_sync(0xffffffffu, v, 0) == epoch + 1;
+      if (go && fi.rec_pro) {
+        go = s_records != 0;
+        if (go) {
+          fence_proxy_async();  // records were written by generic stores
+          if (lane == 0) {
+            uint8_t* aux = auxs + (size_t)fslot * p.aux_stage_bytes;
+            mbar_arrive_expect_tx(&full[fslot], (uint32_t)fi.frag_bytes);
+            issue_frag(RP, fi, b, aux, &full[fslot], pol_keep);
+          }
+          __syncwarp();
+        }
+      } else if (go) {
+        const int h0 = fi.grp * GS;  // first h column of the item's group
+        const int wt_h = h0 / kWideCols, sl_h = (h0 % kWideCols) / kTileCols;
+        const int sub = wt_h * kSlices + sl_h;
+        if (sub != h_sub) {
+          int a = RP.src_first;
+          while (a + 1 < RP.src_first + RP.src_count && wt_h >= T.ph[a].wt1) ++a;
+          const PhaseParams& A = T.ph[a];
+          if (!(src_done >> a & 1u)) {
+            // the sub-tile's count, and the whole producing phase's (one complete phase
+            // means no more polls for its sub-tiles)
+            const unsigned total = (unsigned)(red_segments(T, a, 2 * wt_h, Ptot) +
+                                              red_segments(T, a, 2 * wt_h + 1, Ptot));
+            const unsigned ptotal = (unsigned)A.done_total;
+            unsigned v = 0, pv = 0;
+            if (lane == 0) {
+              v = ld_acquire_u32(&A.counters[sub]);
+              pv = ld_acquire_u32(&p.phase_done[a]);
+            }
+            v = __shfl_sync(0xffffffffu, v, 0);
+            pv = __shfl_sync(0xffffffffu, pv, 0);
+            if (pv == ptotal) src_done |= 1u << a;
+            go = v == total || pv == ptotal;
+          }
+          if (go) {
+            reduce_silu_mul<MT>(T, a, wt_h, sl_h, Ptot, lane, p.m, hv);
+            h_sub = sub;
+            h_src = a;
+          }
+        }
+        if (go) {
+          const int gi = (h0 % kTileCols) / GS;  // the item's group within the sub-tile
+          uint8_t* rec = frag_slot(auxs + (size_t)fslot * p.aux_stage_bytes);
+#pragma unroll
+          for (int tok = 0; tok < MT; ++tok)
+            build_records<MT>(hv[tok], tok, GS, rec - (size_t)gi * fi.frag_bytes, fi.frag_bytes,
+                              lane, gi);
+          // h itself, once: by the item of output tile 0
+          const PhaseParams& A = T.ph[h_src];
+          if (A.out && fi.cu == 0 && lane / (GS / 4) == gi) {
+            for (int tok = 0; tok < p.m && tok < MT; ++tok)
+              *reinterpret_cast<float4*>(A.out + (size_t)tok * A.ldo + wt_h * kWideCols +
+                                         sl_h * kTileCols + 4 * lane) =
+                  make_float4(hv[tok][0], hv[tok][1], hv[tok][2], hv[tok][3]);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[fslot]);
         }
       }
       if (go) {
-        fence_proxy_async();  // records were written by generic stores
-        if (lane == 0) {
-          uint8_t* aux = auxs + (size_t)fslot * p.aux_stage_bytes;
-          mbar_arrive_expect_tx(&full[fslot], (uint32_t)P.frag_bytes);
-          issue_frag(P, fi, b, aux, &full[fslot], pol_keep);
-        }
-        __syncwarp();
         ++F;
-        iter_next(fi, p, b, Ptot);
+        iter_next(fi, T, b, Ptot);
         fslot = fslot + 1 == S ? 0 : fslot + 1;
         t_wait = 0;
       } else {
@@ -978,11 +1104,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kFlushWarp) {
     // ------------------------------- flush warp ----------------------------------------
     ItemIter hi;
-    iter_start(hi, p, b, Ptot);
+    iter_start(hi, T, b, Ptot);
     int k = 0;
-    while (hi.ph < p.nphases) {
-      const PhaseParams& P = p.ph[hi.ph];
-      if (mid_range_flush(P, hi)) {
+    bool fok = true;
+    while (fok && hi.ph < T.n) {
+      if (ends_segment(hi)) {
+        const PhaseParams& P = T.ph[hi.ph];
         if (!wait_slot(&s_fbar[k % kFlushSlots], (uint32_t)(k / kFlushSlots) & 1u, &s_abort, p.err,
                        p.timeout_ns)) {
           s_abort = 1;
@@ -991,21 +1118,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();  // the consumers' partial sums (acquired through the barrier)
         const int wt = hi.cu >> (P.nmat - 1);
         const int ns = active_slices(P, wt);
-        const bool last = lane < ns && count_segment(p, hi.ph, wt, lane, Ptot);
-        unsigned won = __ballot_sync(0xffffffffu, last);
-        if (won) __threadfence();
-        while (won) {
-          const int sl = __ffs(won) - 1;
-          won &= won - 1;
-          fixup_tile<MT>(p, hi.ph, wt, sl, Ptot, lane, epoch);
+        if (P.epi == kEpiSiluMul) {
+          // the consumers of h reduce it once the sub-tile's count is complete
+          if (lane < ns) atomicAdd(&P.counters[wt * kSlices + lane], 1u);
+          if (lane == 0) atomicAdd(&p.phase_done[hi.ph], (unsigned)ns);
           __syncwarp();
-          if (lane == 0) atomicExch(&P.counters[wt * kSlices + sl], 0u);
+          if (lane == 0) s_fdone = k + 1;
+          ++k;
+          iter_next(hi, T, b, Ptot);
+          continue;
         }
-        __syncwarp();
+        const bool last = lane < ns && count_segment(T, hi.ph, wt, lane, Ptot);
+        if (__ballot_sync(0xffffffffu, last)) __threadfence();  // the other CTAs' partials
+        if (last) {
+          // lane = slice: post the fixup to that slice's consumer warp
+          const int h = s_job_head[lane];
+          const uint64_t t0 = global_timer_ns();
+          while (h - s_job_tail[lane] >= kJobSlots && !s_abort) {
+            if (global_timer_ns() - t0 > p.timeout_ns) {
+              atomicOr(p.err, kErrFlagWait);
+              s_abort = 1;
+              break;
+            }
+          }
+          s_job[lane][h % kJobSlots] = (hi.ph << 16) | wt;
+          __threadfence_block();
+          s_job_head[lane] = h + 1;
+        }
+        fok = __all_sync(0xffffffffu, !s_abort);
         if (lane == 0) s_fdone = k + 1;
         ++k;
       }
-      iter_next(hi, p, b, Ptot);
+      iter_next(hi, T, b, Ptot);
     }
   } else {
     // ------------------------------- consumer warps ------------------------------------
@@ -1020,11 +1164,95 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int c = 0; c < 4 / MT; ++c) cls_mask[c] = (q / MT == c) ? 0xffffffffu : 0u;
 
     ItemIter it;
-    iter_start(it, p, b, Ptot);
+    iter_start(it, T, b, Ptot);
     bool ok = true;
-    int fk = 0;  // mid-range flush events handed to the flush warp
+    int fk = 0;  // flush events handed to the flush warp
+    // Fixup jobs the flush warp posted for this slice: reduce the sub-tile's partials, run its
+    // epilogue and return its counter to zero for the next launch.
+    int job_tail = 0;  // jobs of this slice run so far (s_job_tail mirrors it for the flush warp)
+    auto run_jobs = [&]() {
+      for (;;) {
+        const int h = __shfl_sync(0xffffffffu, lane == 0 ? s_job_head[slice] : 0, 0);
+        if (job_tail == h) break;
+        const int job = s_job[slice][job_tail % kJobSlots];
+        __threadfence_block();
+        const int jph = job >> 16, jwt = job & 0xffff;
+        fixup_tile<MT, GS>(p, T, jph, jwt, slice, Ptot, lane);
+        __syncwarp();
+        if (lane == 0) atomicExch(&T.ph[jph].counters[jwt * kSlices + slice], 0u);
+        ++job_tail;
+        __syncwarp();
+        if (lane == 0) s_job_tail[slice] = job_tail;
+      }
+    };
+    // Runs fixup jobs until the flush warp has completed `n` flush events (bounded; gives up
+    // on an abort).  Lane 0 decides, so the warp leaves the loop together.
+    auto wait_flushes = [&](int n) {
+      const uint64_t t0 = global_timer_ns();
+      for (;;) {
+        int st = 0;
+        if (lane == 0) {
+          if (s_fdone >= n) st = 1;
+          else if (s_abort) st = 2;
+          else if (global_timer_ns() - t0 > p.timeout_ns) {
+            atomicOr(p.err, kErrFlagWait);
+            s_abort = 1;
+            st = 2;
+          }
+        }
+        st = __shfl_sync(0xffffffffu, st, 0);
+        run_jobs();
+        if (st) break;
+      }
+    };
+    // Waits for stage `sl` in phase `par`; runs fixup jobs meanwhile (another CTA may be waiting
+    // for the records one of them produces).  Returns false on an abort or a timeout.
+    auto wait_full = [&](int sl, uint32_t par) -> bool {
+      if (__all_sync(0xffffffffu, mbar_try_wait(&full[sl], par))) return true;
+      const uint64_t t0 = global_timer_ns();
+      for (;;) {
+        run_jobs();
+        if (__all_sync(0xffffffffu, mbar_try_wait_hint(&full[sl], par, 256))) return true;
+        int st = 0;
+        if (lane == 0) {
+          if (s_abort) st = 1;
+          else if (global_timer_ns() - t0 > p.timeout_ns) {
+            atomicOr(p.err, kErrTmaWait);
+            st = 1;
+          }
+        }
+        if (__shfl_sync(0xffffffffu, st, 0)) return false;
+      }
+    };
+    // Ends a split-K segment: stores this slice's partial sums and hands the segment to the
+    // flush warp (which counts it; the reduction runs later as a fixup job).
+    float y[4 * MT];
+#pragma unroll
+    for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+    auto hand_off = [&](const PhaseParams& P, int ph, int cu, bool active) {
+      if (active)
+        store_partials<MT>(partial_slot<MT>(P, cu, segment_index(T, ph, cu, b, Ptot), slice), y,
+                           lane, tokE, colbase);
+#pragma unroll
+      for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+      __syncwarp();
+      // the event slot is free once the flush warp has completed event fk - kFlushSlots
+      wait_flushes(fk - kFlushSlots + 1);
+      if (lane == 0) mbar_arrive(&s_fbar[fk % kFlushSlots]);
+      ++fk;
+    };
+    // Stage pointers of the item in slot sl.
+    auto stage_tile = [&](int sl) {
+      return tiles + (size_t)sl * p.tile_stage_bytes + slice * kTileCols;
+    };
+    auto stage_aux = [&](int sl) { return auxs + (size_t)sl * p.aux_stage_bytes; };
+    const bool rec0_smem = p.rec0_smem != 0;
+    auto item_rec = [&](const ItemIter& x, int sl) -> const uint8_t* {
+      return (x.rec_pro && rec0_smem) ? rec0s + (size_t)x.grp * x.frag_bytes
+                                      : frag_slot(stage_aux(sl));
+    };
 
-    prologue<MT>(p, warp, lane, s_red, s_rms, rec0s);
+    prologue<MT, GS>(p, warp, lane, s_red, s_rms, rec0s);
     named_barrier(1, kNC * 32);
     if (threadIdx.x == 0) {
       __threadfence_block();
@@ -1032,51 +1260,123 @@ __global__ void __launch_bounds__(kThreads, 1)
       trace_event(p, 1);
     }
 
-    float y[4 * MT];
-#pragma unroll
-    for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
-    int D[8][4];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) D[r][0] = D[r][1] = D[r][2] = D[r][3] = 0;
-    int cur_ph = -1;
-    while (ok && it.ph < p.nphases) {
-      const int ph = it.ph;
-      const PhaseParams& P = p.ph[ph];
-      if (ph != cur_ph) {
-        if (cur_ph >= 0 && threadIdx.x == 0) trace_event(p, 3 + (cur_ph ? 2 : 0));
-        cur_ph = ph;
-      }
-      if (!wait_slot(&full[slot], parity, &s_abort, p.err, p.timeout_ns)) {
-        ok = false;
-        s_abort = 1;
-        break;
-      }
-      if (consumed == 0 && threadIdx.x == 0) trace_event(p, 9);
-      const int wt = it.cu >> (P.nmat - 1);
-      const bool active = slice < active_slices(P, wt);
-      const uint8_t* ax = auxs + (size_t)slot * p.aux_stage_bytes;
-      const uint8_t* tl = tiles + (size_t)slot * p.tile_stage_bytes + slice * kTileCols;
-      const uint8_t* rec = (P.ready_in == nullptr && p.rec0_smem)
-                               ? rec0s + (size_t)it.grp * P.frag_bytes
-                               : frag_slot(const_cast<uint8_t*>(ax));
-      if constexpr (MT <= 2) {
-        if (active) {
-          const uint8_t* scp = ax + slice * kScaleBytes;
-          const uint8_t* zpp = ax + kSlices * kScaleBytes + slice * kZeroBytes;
-          switch (P.gs) {
-            case 16: dp_item<MT, 8>(tl, rec, scp, zpp, it.s0, it.s1, lane, &empty[slot], y); break;
-            case 32: dp_item<MT, 16>(tl, rec, scp, zpp, it.s0, it.s1, lane, &empty[slot], y); break;
-            case 64: dp_item<MT, 32>(tl, rec, scp, zpp, it.s0, it.s1, lane, &empty[slot], y); break;
-            default: dp_item<MT, 64>(tl, rec, scp, zpp, it.s0, it.s1, lane, &empty[slot], y); break;
-          }
+    if constexpr (MT <= 2) {
+      // Software-pipelined over chunks of HB rows: the shared-memory loads of the next chunk
+      // (possibly of the next item) are issued before the dp2a work of the current one, and a
+      // stage is released as soon as its last chunk is loaded.
+      constexpr int R = GS / 2;                    // packed rows per item
+      constexpr int HB = R <= 32 ? R / 2 : 16;     // rows per chunk
+      constexpr int NCH = R / HB;                  // chunks per item (2 or 4)
+      uint32_t wA[HB], wB[HB];
+      uint4 XA[MT][HB / 4], XB[MT][HB / 4];
+      DpMeta<MT> Mc, Mn;
+      bool have = it.ph < T.n;
+      if (have) {
+        if (!wait_full(slot, parity)) {
+          ok = false;
+          s_abort = 1;
+          have = false;
         } else {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[slot]);
+          if (threadIdx.x == 0) trace_event(p, 9);
+          const uint8_t* rec = item_rec(it, slot);
+          dp_load_meta<MT, GS>(stage_aux(slot), rec, slice, lane, it.s0, it.s1, Mc);
+          dp_load_rows<HB>(stage_tile(slot), 0, it.s0 * kStepRows, it.s1 * kStepRows, lane, wA);
+          dp_load_x<MT, HB>(rec, dp_tok_stride(GS), 0, XA);
         }
-      } else {
+      }
+      while (have) {
+        const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
+        const uint8_t* tl = stage_tile(slot);
+        const uint8_t* rec = item_rec(it, slot);
+        const bool seg_end = ends_segment(it);
+        // the fixup-job queue head, read now and looked at after this item's work
+        const int jh = lane == 0 ? s_job_head[slice] : 0;
+        ItemIter nx = it;
+        iter_next(nx, T, b, Ptot);
+        const int nslot = slot + 1 == S ? 0 : slot + 1;
+        const uint32_t npar = slot + 1 == S ? parity ^ 1u : parity;
+        const bool prefetch = !seg_end && nx.ph < T.n;
+        bool next_loaded = false;
+        int aL[MT][4], aH[MT][4];
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) aL[m][i] = aH[m][i] = 0;
+#pragma unroll
+        for (int c = 0; c < NCH; c += 2) {
+          dp_load_rows<HB>(tl, (c + 1) * HB, r0, r1, lane, wB);
+          dp_load_x<MT, HB>(rec, dp_tok_stride(GS), (c + 1) * HB, XB);
+          bool nready = false;
+          if (c + 2 == NCH) {
+            // every byte of this stage is loaded (in issue order before the arrival)
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            // probe the next stage now; the answer is looked at after this chunk's work
+            if (prefetch) nready = mbar_test_wait(&full[nslot], npar);
+          }
+          dp_compute<MT, HB>(wA, XA, aL, aH);
+          if (c + 2 < NCH) {
+            dp_load_rows<HB>(tl, (c + 2) * HB, r0, r1, lane, wA);
+            dp_load_x<MT, HB>(rec, dp_tok_stride(GS), (c + 2) * HB, XA);
+          } else if (prefetch) {
+            // the next item's first chunk, while this item's last chunk computes (a segment
+            // end is handed off first: other CTAs may wait for it)
+            if (!__all_sync(0xffffffffu, nready) && !wait_full(nslot, npar)) {
+              ok = false;
+            } else {
+              const uint8_t* nrec = item_rec(nx, nslot);
+              dp_load_meta<MT, GS>(stage_aux(nslot), nrec, slice, lane, nx.s0, nx.s1, Mn);
+              dp_load_rows<HB>(stage_tile(nslot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
+              dp_load_x<MT, HB>(nrec, dp_tok_stride(GS), 0, XA);
+              next_loaded = true;
+            }
+          }
+          dp_compute<MT, HB>(wB, XB, aL, aH);
+        }
+        dp_epilogue<MT>(Mc, aL, aH, y);
+        ++consumed;
+        slot = nslot;  // ring position of item `consumed` (the drain after an error starts here)
+        parity = npar;
+        if (seg_end) hand_off(T.ph[it.ph], it.ph, it.cu, slice < item_slices(it));
+        if (__shfl_sync(0xffffffffu, jh, 0) != job_tail) run_jobs();
+        if (!ok) {
+          s_abort = 1;
+          break;
+        }
+        if (nx.ph >= T.n) break;
+        if (!next_loaded) {
+          if (!wait_full(slot, parity)) {
+            ok = false;
+            s_abort = 1;
+            break;
+          }
+          const uint8_t* nrec = item_rec(nx, slot);
+          dp_load_meta<MT, GS>(stage_aux(slot), nrec, slice, lane, nx.s0, nx.s1, Mn);
+          dp_load_rows<HB>(stage_tile(slot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
+          dp_load_x<MT, HB>(nrec, dp_tok_stride(GS), 0, XA);
+        }
+        it = nx;
+        Mc = Mn;
+      }
+    } else {
+      int D[8][4];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) D[r][0] = D[r][1] = D[r][2] = D[r][3] = 0;
+      while (ok && it.ph < T.n) {
+        if (!wait_full(slot, parity)) {
+          ok = false;
+          s_abort = 1;
+          break;
+        }
+        if (consumed == 0 && threadIdx.x == 0) trace_event(p, 9);
+        const bool active = slice < item_slices(it);
+        const uint8_t* ax = stage_aux(slot);
+        const uint8_t* tl = stage_tile(slot);
+        const uint8_t* rec = item_rec(it, slot);
         if (active) {
-          const int kbg = P.spg >= 4 ? P.spg / 4 : 1;    // 32-pair blocks per group
-          const int nrows = P.spg >= 4 ? 32 : 8 * P.spg;  // valid rows per block
+          constexpr int spg = GS / 16;
+          constexpr int kbg = spg >= 4 ? spg / 4 : 1;    // 32-pair blocks per group
+          constexpr int nrows = spg >= 4 ? 32 : 8 * spg;  // valid rows per block
           const uint4* rb = reinterpret_cast<const uint4*>(rec);
           const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
           for (int kb = 0; kb < kbg; ++kb) {
@@ -1087,49 +1387,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int2* sums = reinterpret_cast<const int2*>(rec + 128 * MT * kbg);
           group_epilogue<MT>(ax + slice * kScaleBytes,
                              ax + kSlices * kScaleBytes + slice * kZeroBytes, sums,
-                             reinterpret_cast<const float*>(sums + P.spg * MT), it.s0, it.s1,
+                             reinterpret_cast<const float*>(sums + spg * MT), it.s0, it.s1,
                              tokE, colbase, D, y);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
-      }
-      ++consumed;
-      if (++slot == S) {
-        slot = 0;
-        parity ^= 1u;
-      }
-      const int cu = it.cu;
-      const bool mid = mid_range_flush(P, it);
-      const bool last_of_range = it.i == it.n - 1;
-      iter_next(it, p, b, Ptot);
-      if (mid) {
-        // store the partial sums and hand the segment to the flush warp
-        if (active)
-          store_partials<MT>(partial_slot<MT>(P, cu, segment_index(p, ph, cu, b, Ptot), slice), y,
-                             lane, tokE, colbase);
-#pragma unroll
-        for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
-        __syncwarp();
-        if (lane == 0) {
-          // the event slot is free once the flush warp has completed event fk - kFlushSlots
-          const uint64_t t0 = global_timer_ns();
-          while (s_fdone < fk - kFlushSlots + 1 && !s_abort) {
-            if (global_timer_ns() - t0 > p.timeout_ns) {
-              atomicOr(p.err, kErrFlagWait);
-              s_abort = 1;
-              break;
-            }
-          }
-          mbar_arrive(&s_fbar[fk % kFlushSlots]);
+        ++consumed;
+        if (++slot == S) {
+          slot = 0;
+          parity ^= 1u;
         }
-        ++fk;
-      } else if (last_of_range) {
-        if (active)
-          flush_segment<MT>(p, ph, cu, b, Ptot, slice, y, lane, tokE, colbase, epoch);
-#pragma unroll
-        for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+        const int cu = it.cu, ph = it.ph;
+        const bool flush = ends_segment(it);
+        iter_next(it, T, b, Ptot);
+        if (flush) hand_off(T.ph[ph], ph, cu, active);
+        run_jobs();
       }
     }
+    // every flush event completed by the flush warp and every fixup job of this slice run
+    wait_flushes(fk);
     if (threadIdx.x == 0) trace_event(p, 5);
   }
   __syncthreads();
@@ -1145,21 +1421,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (threadIdx.x == 0) {
-    // the last CTA to finish advances the epoch (the next launch's ready flags)
+    // the last CTA to finish (every CTA's reads of the counters are done) returns the
+    // kEpiSiluMul segment counters to zero for the next launch and counts the launch
     __threadfence();
     if (atomicAdd(&p.sync->done, 1u) == gridDim.x - 1) {
-      atomicExch(&p.sync->done, 0u);
       __threadfence();
-      atomicExch(&p.sync->epoch, epoch + 1);
+      for (int i = 0; i < p.zero_count; ++i) p.zero_counters[i] = 0u;
+      atomicExch(&p.sync->done, 0u);
+      atomicAdd(&p.sync->epoch, 1u);
     }
     trace_event(p, 6);
   }
 }
 
-template <int MT>
+template <int MT, int GS>
 cudaError_t launch_mt(const TmapPack& maps, const EngineParams& p, int grid, size_t smem,
                       cudaStream_t stream) {
-  auto kern = int4_engine_kernel<MT>;
+  auto kern = int4_engine_kernel<MT, GS>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);
@@ -1173,12 +1451,36 @@ cudaError_t launch_mt(const TmapPack& maps, const EngineParams& p, int grid, siz
   return cudaLaunchKernelEx(&cfg, kern, maps, p);
 }
 
-template <int MT>
+template <int MT, int GS>
 cudaError_t prepare_mt(size_t smem, int* blocks) {
-  auto kern = int4_engine_kernel<MT>;
+  auto kern = int4_engine_kernel<MT, GS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kern, kThreads, smem);
+}
+
+// (MT, GS) instantiations: MT in {1, 2, 4} tokens, GS in {16, 32, 64, 128}.
+template <int MT>
+cudaError_t occupancy_gs(int gs, size_t smem, int* blocks) {
+  switch (gs) {
+    case 16: return prepare_mt<MT, 16>(smem, blocks);
+    case 32: return prepare_mt<MT, 32>(smem, blocks);
+    case 64: return prepare_mt<MT, 64>(smem, blocks);
+    case 128: return prepare_mt<MT, 128>(smem, blocks);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int MT>
+cudaError_t launch_gs(int gs, const TmapPack& maps, const EngineParams& p, int grid, size_t smem,
+                      cudaStream_t stream) {
+  switch (gs) {
+    case 16: return launch_mt<MT, 16>(maps, p, grid, smem, stream);
+    case 32: return launch_mt<MT, 32>(maps, p, grid, smem, stream);
+    case 64: return launch_mt<MT, 64>(maps, p, grid, smem, stream);
+    case 128: return launch_mt<MT, 128>(maps, p, grid, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
@@ -1213,21 +1515,21 @@ bool engine_plan_smem(int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes,
   return false;
 }
 
-cudaError_t engine_occupancy(int mt, size_t smem, int* blocks) {
+cudaError_t engine_occupancy(int mt, int gs, size_t smem, int* blocks) {
   switch (mt) {
-    case 1: return prepare_mt<1>(smem, blocks);
-    case 2: return prepare_mt<2>(smem, blocks);
-    case 4: return prepare_mt<4>(smem, blocks);
+    case 1: return occupancy_gs<1>(gs, smem, blocks);
+    case 2: return occupancy_gs<2>(gs, smem, blocks);
+    case 4: return occupancy_gs<4>(gs, smem, blocks);
     default: return cudaErrorInvalidValue;
   }
 }
 
-cudaError_t engine_launch(int mt, const TmapPack& maps, const EngineParams& p, int grid,
+cudaError_t engine_launch(int mt, int gs, const TmapPack& maps, const EngineParams& p, int grid,
                           size_t smem, cudaStream_t stream) {
   switch (mt) {
-    case 1: return launch_mt<1>(maps, p, grid, smem, stream);
-    case 2: return launch_mt<2>(maps, p, grid, smem, stream);
-    case 4: return launch_mt<4>(maps, p, grid, smem, stream);
+    case 1: return launch_gs<1>(gs, maps, p, grid, smem, stream);
+    case 2: return launch_gs<2>(gs, maps, p, grid, smem, stream);
+    case 4: return launch_gs<4>(gs, maps, p, grid, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }

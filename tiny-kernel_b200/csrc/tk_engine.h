@@ -12,12 +12,13 @@
 // Work unit = one k-step (16 k values = 8 packed rows) of a 1024-column wide tile of one
 // matrix; each CTA owns a contiguous range of every phase's units (stream-K) and its 8
 // consumer warps take one 128-column slice each.  Partial sums of a 128-column sub-tile are
-// reduced deterministically (in phase and CTA order) by the last warp to finish it; the
-// phases [red_first, red_first + red_count) add into the same outputs.  There is no
-// grid-wide barrier: every CTA builds its own prologue records, and a record of h is consumed
-// only after its producer sub-tile has published a ready flag for this launch.  Splitting the
-// gate/up tiles into P ranges lets the down projection of range j run while later ranges are
-// still being reduced.
+// reduced deterministically (in phase and CTA order); the phases [red_first, red_first +
+// red_count) add into the same outputs.  An output (y) sub-tile is reduced by the last warp to
+// finish it.  The gate/up partial sums are not reduced by their producers: every CTA that
+// consumes an h sub-tile waits for its segment counter to be complete and reduces it itself
+// (silu(gate) * up, then the records of its own items).  There is no grid-wide barrier.
+// Splitting the gate/up tiles into P ranges lets the down projection of range j run while
+// later ranges are still being produced.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -74,13 +75,14 @@ __host__ __device__ constexpr int record_bytes(int gs, int mt) {
 }
 
 enum EpilogueKind : int {
-  kEpiStore = 0,    // out[tok][col] = sum (+ residual[tok][col])
-  kEpiSiluMul = 1,  // h = silu(mat0) * mat1 -> optional h out + next phase's records
+  kEpiStore = 0,    // out[tok][col] = sum (+ residual[tok][col]), by the last segment's warp
+  kEpiSiluMul = 1,  // partial sums stay in `partials`; a phase with src_count > 0 builds its
+                    // records from silu(mat0) * mat1 of them (and writes h to `out` if set)
 };
 
 // Launch-to-launch synchronisation state (device memory, zeroed once).
 struct SyncState {
-  unsigned epoch;  // launches completed; ready flags of launch E carry E + 1
+  unsigned epoch;  // launches completed
   unsigned pad0[31];
   unsigned done;   // CTAs finished in the current launch
   unsigned pad1[31];
@@ -99,11 +101,12 @@ struct PhaseParams {
   int map_base;     // tensor maps of matrix i: map[map_base + 2i] (group box), +1 (step box)
   const uint16_t* scales[kMaxMats];
   const uint8_t* zeros[kMaxMats];
-  const uint8_t* frag_in;     // activation records, one per group of K (global group index)
-  long long frag_cta_stride;  // bytes between CTAs' private copies (0: one shared copy)
-  int frag_bytes;
-  const unsigned* ready_in;   // per 128-value sub-tile of K: record ready when == epoch + 1;
-                              // null: the records are the prologue's
+  const uint8_t* frag_in;     // prologue records in global memory, one per group of K
+  long long frag_cta_stride;  // bytes between CTAs' private copies
+  int frag_bytes;             // record bytes per group
+  int src_first, src_count;   // src_count > 0: records built from the kEpiSiluMul partial sums
+                              // of phases [src_first, src_first + src_count); else the prologue's
+  int done_total;             // kEpiSiluMul: sum over its column units of segments * slices
   float* partials;         // [N/1024 * nmat][maxseg][kSlices][MT][128], shared by the reduction
   unsigned* counters;      // [N / 128] per sub-tile, zero between launches, shared likewise
   int maxseg;              // segments per column unit summed over the reduction's phases
@@ -112,10 +115,6 @@ struct PhaseParams {
   int ldo;
   const float* residual;   // kEpiStore: optional
   int ldr;
-  uint8_t* frag_out;       // kEpiSiluMul: records for the next phase
-  unsigned* ready_out;     // kEpiSiluMul: per 128-column sub-tile flags
-  int next_gs;
-  int next_frag_bytes;
 };
 
 struct EngineParams {
@@ -141,6 +140,11 @@ struct EngineParams {
   int stages;
   int tile_stage_bytes;
   int aux_stage_bytes;
+  // segment counters the last CTA to finish returns to zero (the kEpiSiluMul reductions'),
+  // and per kEpiSiluMul phase the (segment, slice) pairs it has completed (inside that range)
+  unsigned* zero_counters;
+  int zero_count;
+  unsigned* phase_done;  // [kMaxPhases]
   // sync + errors
   unsigned long long* trace;  // optional [gridDim.x][kTraceEvents] globaltimer stamps
   SyncState* sync;

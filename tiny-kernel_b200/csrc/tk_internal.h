@@ -12,13 +12,13 @@ namespace tk {
 // tk_engine.cu
 int engine_warps_per_cta();
 size_t engine_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes);
-// Picks the ring depth and where phase-0 records live for a smem budget: records in shared
-// memory with >= 4 stages when they fit, else records in global memory with up to 5 stages.
-// Returns false when not even 2 stages fit.
+// Picks the deepest ring (up to kMaxStages) that fits a smem budget, with the prologue records
+// in shared memory when they fit beside it.  Returns false when not even 2 stages fit.
 bool engine_plan_smem(int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes, int smem_limit,
                       int* stages, int* rec0_smem, size_t* smem);
-cudaError_t engine_occupancy(int mt, size_t smem, int* blocks);
-cudaError_t engine_launch(int mt, const TmapPack& maps, const EngineParams& p, int grid,
+// The kernel is instantiated per tokens (mt in {1, 2, 4}) and group size (16, 32, 64, 128).
+cudaError_t engine_occupancy(int mt, int gs, size_t smem, int* blocks);
+cudaError_t engine_launch(int mt, int gs, const TmapPack& maps, const EngineParams& p, int grid,
                           size_t smem, cudaStream_t stream);
 
 // tk_simple.cu -- CUDA-core kernels: reference-order fallbacks and the small ops.

@@ -62,6 +62,8 @@ struct TmapEntry {
 };
 
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // 2 s per bounded wait
+// shared memory the engine kernel declares statically (phase table, job queues, barriers)
+constexpr int kStaticSmemReserve = 4096;
 
 }  // namespace
 
@@ -77,10 +79,9 @@ struct tk_device {
   int ffn_split = 1;  // gate/up tile ranges of the FFN (TK_FFN_SPLIT, 1..4)
   SyncState* sync = nullptr;
   unsigned* err = nullptr;
-  ScratchBuf frag[2];
-  ScratchBuf partials[2];
-  ScratchBuf counters[2];
-  ScratchBuf ready;  // per 128-column sub-tile flags of the FFN intermediate
+  ScratchBuf frag[1];      // per-CTA prologue records when they do not fit in shared memory
+  ScratchBuf partials[2];  // split-K partial sums: [0] first reduction, [1] second
+  ScratchBuf counters[2];  // segment counters per 128-column sub-tile of each
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   std::vector<TmapEntry> tmaps;
 };
@@ -200,6 +201,21 @@ int max_segments(const PhaseParams& P, long long Wtot) {
   return mx;
 }
 
+// Sum over the phase's column units of (CTA ranges holding the unit) * (slices of its tile):
+// the (segment, slice) pairs a kEpiSiluMul phase completes.
+int phase_done_total(const PhaseParams& P, long long Wtot) {
+  const long long W = std::min<long long>(Wtot, P.units);
+  const long long per = (long long)P.groups * P.spg;
+  long long tot = 0;
+  for (long long c = 0; c < (long long)P.tiles * P.nmat; ++c) {
+    const long long a = c * per;
+    const long long ns = warp_of_unit_h(a + per - 1, P.units, W) - warp_of_unit_h(a, P.units, W) + 1;
+    const int wt = P.wt0 + (int)(c / P.nmat);
+    tot += ns * std::min(kSlices, (P.N - wt * kWideCols) / kTileCols);
+  }
+  return (int)tot;
+}
+
 // One phase over the wide tiles [wt0, wt1) of N and the groups [g0, g1) of K (all of them
 // when wt1 / g1 are negative); a reduction of its own until bind_partials says otherwise.
 void fill_phase(PhaseParams& P, int K, int N, int gs, int nmat, int mt, int wt0 = 0, int wt1 = -1,
@@ -237,7 +253,8 @@ int bind_partials(tk_device* d, EngineParams& p, int first, int count, int idx, 
   const size_t pbytes = tiles_all * F.nmat * maxseg * kSlices * mt * kTileCols * sizeof(float);
   int st = scratch_ensure(d, d->partials[idx], pbytes);
   if (st != TK_OK) return st;
-  st = scratch_ensure(d, d->counters[idx], (size_t)(F.N / kTileCols) * sizeof(unsigned));
+  // one counter per 128-column sub-tile, then one per phase (kEpiSiluMul completion)
+  st = scratch_ensure(d, d->counters[idx], (size_t)(F.N / kTileCols + kMaxPhases) * sizeof(unsigned));
   if (st != TK_OK) return st;
   for (int q = first; q < first + count; ++q) {
     PhaseParams& P = p.ph[q];
@@ -253,6 +270,10 @@ int bind_partials(tk_device* d, EngineParams& p, int first, int count, int idx, 
 int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, cudaStream_t st) {
   int spg_max = 0, fb_max = 0;
   for (int q = 0; q < p.nphases; ++q) {
+    // the kernel's stream-K arithmetic is 32-bit
+    if (p.ph[q].units * (long long)d->sm_count >= (1LL << 31))
+      return fail(TK_ERR_UNSUPPORTED, "phase of %lld work units is too large for one launch",
+                  p.ph[q].units);
     spg_max = std::max(spg_max, p.ph[q].spg);
     fb_max = std::max(fb_max, p.ph[q].frag_bytes);
   }
@@ -261,7 +282,7 @@ int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, c
   int stages = 0, rec0_smem = 0;
   size_t smem = 0;
   const int rec0_bytes = (p.K0 / p.gs0) * p.frag0_bytes;
-  if (!engine_plan_smem(p.tile_stage_bytes, p.aux_stage_bytes, rec0_bytes, d->smem_optin - 2048,
+  if (!engine_plan_smem(p.tile_stage_bytes, p.aux_stage_bytes, rec0_bytes, d->smem_optin - kStaticSmemReserve,
                         &stages, &rec0_smem, &smem))
     return fail(TK_ERR_UNSUPPORTED, "engine ring does not fit in shared memory");
   if (d->stages_override > 0 && d->stages_override < stages) {
@@ -278,9 +299,9 @@ int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, c
   p.err = d->err;
   p.timeout_ns = d->timeout_ns;
   int blocks = 0;
-  TK_CUDA_TRY(engine_occupancy(mt, smem, &blocks));
+  TK_CUDA_TRY(engine_occupancy(mt, p.gs0, smem, &blocks));
   if (blocks < 1) return fail(TK_ERR_UNSUPPORTED, "engine kernel cannot be resident");
-  TK_CUDA_TRY(engine_launch(mt, maps, p, d->sm_count, smem, st));
+  TK_CUDA_TRY(engine_launch(mt, p.gs0, maps, p, d->sm_count, smem, st));
   return TK_OK;
 }
 
@@ -348,10 +369,6 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   const long long rec_stride = (long long)(hidden / gs) * record_bytes(gs, mt);  // per-CTA records
   int stt = scratch_ensure(d, d->frag[0], (size_t)Wtot * rec_stride);
   if (stt != TK_OK) return stt;
-  stt = scratch_ensure(d, d->frag[1], (size_t)groups_h * record_bytes(gs, mt));
-  if (stt != TK_OK) return stt;
-  stt = scratch_ensure(d, d->ready, (size_t)(inter / kTileCols) * sizeof(unsigned));
-  if (stt != TK_OK) return stt;
   for (int j = 0; j < nsplit; ++j) {
     const int t0 = tiles_i * j / nsplit, t1 = tiles_i * (j + 1) / nsplit;
     PhaseParams& A = p.ph[j];
@@ -366,10 +383,6 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
     A.epi = kEpiSiluMul;
     A.out = h_out;
     A.ldo = inter;
-    A.frag_out = static_cast<uint8_t*>(d->frag[1].ptr);
-    A.ready_out = static_cast<unsigned*>(d->ready.ptr);
-    A.next_gs = gs;
-    A.next_frag_bytes = record_bytes(gs, mt);
     const int g0 = std::min(groups_h, t0 * kWideCols / gs);
     const int g1 = j == nsplit - 1 ? groups_h : std::min(groups_h, t1 * kWideCols / gs);
     PhaseParams& B = p.ph[nsplit + j];
@@ -377,8 +390,8 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
     B.map_base = 4;  // down: maps 4,5
     B.scales[0] = down->scales;
     B.zeros[0] = down->zeros;
-    B.frag_in = static_cast<const uint8_t*>(d->frag[1].ptr);
-    B.ready_in = static_cast<const unsigned*>(d->ready.ptr);
+    B.src_first = 0;  // records from silu(gate) * up of the gate/up phases
+    B.src_count = nsplit;
     B.epi = kEpiStore;
     B.out = out;
     B.ldo = hidden;
@@ -387,8 +400,12 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   }
   stt = bind_partials(d, p, 0, nsplit, 0, mt, Wtot, false);
   if (stt != TK_OK) return stt;
+  for (int j = 0; j < nsplit; ++j) p.ph[j].done_total = phase_done_total(p.ph[j], Wtot);
   stt = bind_partials(d, p, nsplit, nsplit, 1, mt, Wtot, true);
   if (stt != TK_OK) return stt;
+  p.zero_counters = static_cast<unsigned*>(d->counters[0].ptr);
+  p.zero_count = inter / kTileCols + kMaxPhases;
+  p.phase_done = p.zero_counters + inter / kTileCols;
   p.x = x;
   p.ldx = hidden;
   p.K0 = hidden;
@@ -477,8 +494,8 @@ void tk_device_destroy(tk_device* d) {
   if (!d) return;
   cudaSetDevice(d->ordinal);
   if (d->stream) cudaStreamSynchronize(d->stream);
-  for (auto* b : {&d->frag[0], &d->frag[1], &d->partials[0], &d->partials[1], &d->counters[0],
-                  &d->counters[1], &d->ready})
+  for (auto* b : {&d->frag[0], &d->partials[0], &d->partials[1], &d->counters[0],
+                  &d->counters[1]})
     if (b->ptr) cudaFree(b->ptr);
   if (d->sync) cudaFree(d->sync);
   if (d->err) cudaFree(d->err);
@@ -507,7 +524,7 @@ int tk_device_check_error(tk_device* d) {
   TK_CUDA_TRY(cudaDeviceSynchronize());
   TK_CUDA_TRY(cudaMemset(d->err, 0, 256));
   TK_CUDA_TRY(cudaMemset(d->sync, 0, sizeof(SyncState)));
-  for (auto* b : {&d->counters[0], &d->counters[1], &d->ready})
+  for (auto* b : {&d->counters[0], &d->counters[1]})
     if (b->ptr) TK_CUDA_TRY(cudaMemset(b->ptr, 0, b->cap));
   return fail(TK_ERR_TIMEOUT, "device-side bounded wait gave up (error bits 0x%x)", h);
 }
@@ -868,7 +885,7 @@ int noalloc_engine_chunk(unsigned char* scratch, int sm_count, int smem_optin, c
   int stages = 0, rec0_smem = 0;
   size_t smem = 0;
   if (!engine_plan_smem(p.tile_stage_bytes, p.aux_stage_bytes, P.groups * P.frag_bytes,
-                        smem_optin - 2048, &stages, &rec0_smem, &smem))
+                        smem_optin - kStaticSmemReserve, &stages, &rec0_smem, &smem))
     return fail(TK_ERR_UNSUPPORTED, "engine ring does not fit in shared memory");
   p.stages = stages;
   p.rec0_smem = rec0_smem;
@@ -877,9 +894,9 @@ int noalloc_engine_chunk(unsigned char* scratch, int sm_count, int smem_optin, c
   p.err = reinterpret_cast<unsigned*>(scratch + off_err);
   p.timeout_ns = kDefaultTimeoutNs;
   int blocks = 0;
-  TK_CUDA_TRY(engine_occupancy(mt, smem, &blocks));
+  TK_CUDA_TRY(engine_occupancy(mt, p.gs0, smem, &blocks));
   if (blocks < 1) return fail(TK_ERR_UNSUPPORTED, "engine kernel cannot be resident");
-  TK_CUDA_TRY(engine_launch(mt, maps, p, sm_count, smem, st));
+  TK_CUDA_TRY(engine_launch(mt, p.gs0, maps, p, sm_count, smem, st));
   return TK_OK;
 }
 
