@@ -7,6 +7,9 @@ rmsnorm(eps 1e-5) -> gate/up INT4 GEMV (4096 -> 14336) -> silu(gate)*up -> down 
 (group 64, f16 scales, 4-bit zero points).  One step = one FFN forward = one launch of the
 persistent engine.  With --gpus N (torchrun, one rank per GPU) the FFN is tensor-parallel:
 gate/up column-split, down row-split, one NCCL all-reduce of the f32 partial outputs.
+--model 70b: the Llama-3-70B FFN shape (8192 -> 28672 -> 8192).  --layers L: one step is a
+stack of L FFN blocks with their own weights, each x <- x + FFN(x) (the residual is added
+once: by rank 0's kernel, before the all-reduce).
 
 value     whole-job algorithmic GB/s: FFN bytes (weights + x + norm weight + out) per step
           x steps / max-over-ranks device time; inputs resident in HBM; L2 defeated by
@@ -37,6 +40,7 @@ import numpy as np  # noqa: E402
 
 HIDDEN, INTER, GS, EPS = 4096, 14336, 64, 1e-5
 SEED = 20261201
+MODELS = {"8b": ("Llama-3-8B", 4096, 14336), "70b": ("Llama-3-70B", 8192, 28672)}
 
 
 def ffn_bytes(m, hidden, inter, gs):
@@ -124,8 +128,9 @@ def run_reference(args, world, rank):
     import cpu
     from tiny_kernel import data
     m = args.batch
-    W = data.make_ffn(SEED, HIDDEN, INTER, GS)
-    x = data.make_x(SEED, "x", m, HIDDEN)
+    name, hidden, inter = MODELS[args.model]
+    W = data.make_ffn(SEED, hidden, inter, GS)
+    x = data.make_x(SEED, "x", m, hidden)
     threads = cpu.default_threads()
     runner = cpu.FFNRunner(W, m, EPS, threads=threads)
     for _ in range(max(1, min(args.warmup, 3))):
@@ -138,17 +143,19 @@ def run_reference(args, world, rank):
     for _ in range(steps):
         runner(x)
     dt = time.perf_counter() - t0
-    nbytes = ffn_bytes(m, HIDDEN, INTER, GS)
+    nbytes = ffn_bytes(m, hidden, inter, GS)
     gbs = nbytes * steps / dt / 1e9
+    L = args.layers
     line = {
         "impl": "reference", "metric": "INT4 FFN decode HBM GB/s", "value": round(gbs, 3),
         "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": round(dt / steps * 1e3, 4), "higher_is_better": True,
+        "ms_per_step": round(dt / steps * 1e3 * L, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "tokens_per_s": round(m * steps / dt, 2),
-        "config": {"workload": f"Llama-3-8B INT4 FFN decode (rmsnorm->gate/up->silu*up->down), batch {m}",
-                   "hidden": HIDDEN, "inter": INTER, "group_size": GS, "batch": m,
-                   "parallelism": "host CPU", "steps_requested": args.steps},
+        "tokens_per_s": round(m * steps / dt / L, 2),
+        "config": {"workload": workload_name(name, m, L),
+                   "hidden": hidden, "inter": inter, "group_size": GS, "batch": m, "layers": L,
+                   "parallelism": "host CPU", "steps_requested": args.steps,
+                   "sample": "one FFN block per timed step (every block of a stack is the same work)"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{steps} full FFN steps (the reference's Metal shaders cannot "
                                    f"run here: Zig + Metal; this is their C++ std::thread "
@@ -159,7 +166,29 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline_sample(W, x, m):
+def workload_name(name, m, layers):
+    base = f"{name} INT4 FFN decode (rmsnorm->gate/up->silu*up->down), batch {m}"
+    return base if layers == 1 else f"{name} INT4 decode stack: {layers} FFN blocks with residual, batch {m}"
+
+
+def device_ffn(seed, layer, hidden, inter, gs, device):
+    """Synthetic INT4 FFN weights of the given (shard) shape generated on the GPU: uniform
+    codes and zero points, f16 scales uniform [0.005, 0.02], norm weight ~ N(1, 0.05)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1000003 + layer)
+
+    def mat(K, N):
+        w = torch.randint(0, 256, (K // 2, N), dtype=torch.uint8, generator=g, device=device)
+        sc = (torch.rand((K // gs, N), generator=g, device=device) * 0.015 + 0.005).half()
+        z = torch.randint(0, 256, (K // gs, N // 2), dtype=torch.uint8, generator=g, device=device)
+        return [w, sc.view(torch.int16), z]
+
+    nw = (1.0 + 0.05 * torch.randn(hidden, generator=g, device=device)).float()
+    return nw, mat(hidden, inter), mat(hidden, inter), mat(inter, hidden)
+
+
+def cpu_baseline_sample(W, x, m, hidden, inter):
     import cpu
     threads = cpu.default_threads()
     runner = cpu.FFNRunner(W, m, EPS, threads=threads)
@@ -172,9 +201,9 @@ def cpu_baseline_sample(W, x, m):
         if time.perf_counter() - t0 > 10.0 or n >= 200:
             break
     dt = time.perf_counter() - t0
-    return {"value": round(ffn_bytes(m, HIDDEN, INTER, GS) * n / dt / 1e9, 3), "unit": "GB/s",
+    return {"value": round(ffn_bytes(m, hidden, inter, GS) * n / dt / 1e9, 3), "unit": "GB/s",
             "cores": threads, "kind": "port",
-            "sample": f"{n} full FFN steps on the host ({dt:.1f} s), C++ std::thread transcription "
+            "sample": f"{n} full FFN blocks on the host ({dt:.1f} s), C++ std::thread transcription "
                       f"of the reference shaders (oracle/cpu_baseline.cpp)"}
 
 
@@ -184,6 +213,8 @@ def main():
     ap.add_argument("--steps", type=int, default=4000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--model", default="8b", choices=sorted(MODELS))
+    ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
@@ -200,7 +231,7 @@ def main():
     import torch
     import tiny_kernel as tk
     from tiny_kernel import data, ops
-    from tiny_kernel.tp import shard_ffn
+    from tiny_kernel.tp import shard_bounds, shard_ffn
 
     torch.cuda.set_device(local)
     pg = None
@@ -212,10 +243,11 @@ def main():
         pg = dist
     dev = tk.init(local)
     m = args.batch
-    W_full = data.make_ffn(SEED, HIDDEN, INTER, GS)
-    W = shard_ffn(W_full, rank, world)
-    inter = W.inter
-    x_host = data.make_x(SEED, "x", m, HIDDEN)
+    L = args.layers
+    name, hidden, inter_full = MODELS[args.model]
+    shard_bounds(inter_full, GS, rank, world)  # validates the split
+    inter = inter_full // world
+    x_host = data.make_x(SEED, "x", m, hidden)
 
     def to_dev(a):
         a = np.ascontiguousarray(a)
@@ -223,25 +255,59 @@ def main():
             a = a.view(np.int16)
         return torch.from_numpy(a).cuda()
 
-    step_bytes_total = ffn_bytes(m, HIDDEN, INTER, GS)
-    shard_bytes = sum(M.nbytes for M in (W.gate, W.up, W.down))
+    # per-GPU weights: the seeded host generator (the oracle's) for the default one-block 8B
+    # workload, which the CPU baseline also runs; a GPU-side generator of the shard's shapes
+    # for the larger workloads (gigabytes of host-side generation otherwise)
+    layer_bytes = ffn_bytes(m, hidden, inter_full, GS)
+    step_bytes_total = L * layer_bytes
+    host_gen = args.model == "8b" and L == 1
+    W_full = data.make_ffn(SEED, hidden, inter_full, GS) if host_gen else None
+    shard_w_bytes = (2 * data.int4_matrix_bytes(hidden, inter, GS) +
+                     data.int4_matrix_bytes(inter, hidden, GS))
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
-    copies = max(4, math.ceil(3 * l2 / shard_bytes))
-    base = [to_dev(a) for M in (W.gate, W.up, W.down) for a in (M.w, M.s, M.z)]
-    sets = [base] + [[t.clone() for t in base] for _ in range(copies - 1)]
-    mats = [[ops.matrix(*s[3 * j:3 * j + 3]) for j in range(3)] for s in sets]
-    nw = to_dev(W.norm_w)
-    x = to_dev(x_host)
-    out = torch.empty((m, HIDDEN), dtype=torch.float32, device="cuda")
+    copies = max(4 if L == 1 else 1, math.ceil(3 * l2 / (L * shard_w_bytes)))
+    layers = []  # [copy][layer] -> (norm weight, gate, up, down) device tensors
+    if host_gen:
+        W = shard_ffn(W_full, rank, world)
+        mats = [[to_dev(a) for a in (M.w, M.s, M.z)] for M in (W.gate, W.up, W.down)]
+        nw = to_dev(W.norm_w)
+        layers.append([(nw, mats[0], mats[1], mats[2])])
+        for _ in range(copies - 1):
+            layers.append([(nw, [t.clone() for t in mats[0]], [t.clone() for t in mats[1]],
+                            [t.clone() for t in mats[2]])])
+    else:
+        for c in range(copies):
+            layers.append([device_ffn(SEED + 7919 * c + 104729 * rank, l, hidden, inter, GS, "cuda")
+                           for l in range(L)])
+    mats = [[(nw, ops.matrix(*g), ops.matrix(*u), ops.matrix(*d)) for (nw, g, u, d) in cl]
+            for cl in layers]
+    x0 = to_dev(x_host)
+    xa = torch.empty((m, hidden), dtype=torch.float32, device="cuda")
+    xb = torch.empty((m, hidden), dtype=torch.float32, device="cuda")
     stream = torch.cuda.Stream()
+    # stacks carry the residual (added once, by rank 0's kernel, before the all-reduce)
+    residual = L > 1 and rank == 0
+
+    def run_step(i, x_in, bufs, sync):
+        """One step: L blocks; returns the buffer that holds the step's output."""
+        cur = x_in
+        for l in range(L):
+            nw, g, u, d = mats[i % copies][l]
+            out = bufs[l % 2]
+            ops.int4_ffn(dev, cur, nw, g, u, d, out, m, hidden, inter, GS, eps=EPS,
+                         residual=residual, stream=None if sync else stream.cuda_stream, sync=sync)
+            if pg is not None:
+                if sync:
+                    pg.all_reduce(out)
+                    torch.cuda.current_stream().synchronize()
+                else:
+                    with torch.cuda.stream(stream):
+                        pg.all_reduce(out)
+            cur = out
+        return cur
 
     def step(i):
-        g, u, d = mats[i % copies]
-        ops.int4_ffn(dev, x, nw, g, u, d, out, m, HIDDEN, inter, GS, eps=EPS,
-                     stream=stream.cuda_stream, sync=False)
-        if pg is not None:
-            with torch.cuda.stream(stream):
-                pg.all_reduce(out)
+        run_step(i, x0, (xa, xb), False)
 
     # warm-up (also sizes the engine's scratch before any capture)
     for i in range(args.warmup):
@@ -250,14 +316,18 @@ def main():
     dev.synchronize()
 
     graph = None
+    per_graph = max(1, min(args.steps, 4000 // L))
+    reps = math.ceil(args.steps / per_graph)
+    steps_timed = args.steps
     if not args.no_graph and pg is None:
         try:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
-                for i in range(args.steps):
+                for i in range(per_graph):
                     step(i)
             graph.replay()
             stream.synchronize()
+            steps_timed = reps * per_graph
         except Exception as e:  # capture unsupported: fall back to stream launches
             print(f"# graph capture failed ({e}); timing stream launches", file=sys.stderr)
             graph = None
@@ -270,9 +340,10 @@ def main():
         ev0.record(stream)
         if graph is not None:
             with torch.cuda.stream(stream):
-                graph.replay()
+                for _ in range(reps):
+                    graph.replay()
         else:
-            for i in range(args.steps):
+            for i in range(steps_timed):
                 step(i)
         ev1.record(stream)
         ev1.synchronize()
@@ -284,40 +355,35 @@ def main():
         ms = float(t.item())
     from tiny_kernel._lib import check, lib
     check(lib().tk_device_check_error(dev.handle))
-    ms_per_step = ms / args.steps
-    value = step_bytes_total * args.steps / (ms / 1e3) / 1e9
+    ms_per_step = ms / steps_timed
+    value = step_bytes_total * steps_timed / (ms / 1e3) / 1e9
     peak, peak_kind = load_peaks()
-    per_gpu_bytes = shard_bytes + m * HIDDEN * 4 * 2 + HIDDEN * 4
+    per_gpu_bytes = L * (shard_w_bytes + m * hidden * 4 * 2 + hidden * 4)
     achieved = per_gpu_bytes / (ms_per_step / 1e3) / 1e9
 
     # ---- end to end through the synchronous C ABI with host buffers -------------------
     import ctypes as C
-    L = lib()
-    xb = tk.Buffer(dev, "f32", m * HIDDEN, kind=2)   # pinned host
-    ob = tk.Buffer(dev, "f32", m * HIDDEN, kind=2)
-    np.copyto(np.frombuffer((C.c_char * xb.nbytes).from_address(xb.ptr), np.float32), x_host.reshape(-1))
-    xd = torch.empty((m, HIDDEN), dtype=torch.float32, device="cuda")
-    e2e_steps = min(args.steps, 2000)
-    for i in range(5):
-        check(L.tk_buffer_upload(dev.handle, xd.data_ptr(), xb.ptr, xb.nbytes))
-        g, u, d = mats[i % copies]
-        ops.int4_ffn(dev, xd, nw, g, u, d, out, m, HIDDEN, inter, GS, eps=EPS)
-        if pg is not None:
-            pg.all_reduce(out)
-        check(L.tk_buffer_download(dev.handle, ob.ptr, out.data_ptr(), ob.nbytes))
+    Lb = lib()
+    xb_host = tk.Buffer(dev, "f32", m * hidden, kind=2)   # pinned host
+    ob_host = tk.Buffer(dev, "f32", m * hidden, kind=2)
+    np.copyto(np.frombuffer((C.c_char * xb_host.nbytes).from_address(xb_host.ptr), np.float32),
+              x_host.reshape(-1))
+    xd = torch.empty((m, hidden), dtype=torch.float32, device="cuda")
+    e2e_steps = max(1, min(steps_timed, 2000 // L))
+    for i in range(3):
+        check(Lb.tk_buffer_upload(dev.handle, xd.data_ptr(), xb_host.ptr, xb_host.nbytes))
+        res = run_step(i, xd, (xa, xb), True)
+        check(Lb.tk_buffer_download(dev.handle, ob_host.ptr, res.data_ptr(), ob_host.nbytes))
     if pg is not None:
         pg.barrier()
+    torch.cuda.synchronize()
     devstream = torch.cuda.ExternalStream(dev.stream())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(devstream)
     for i in range(e2e_steps):
-        check(L.tk_buffer_upload(dev.handle, xd.data_ptr(), xb.ptr, xb.nbytes))
-        g, u, d = mats[i % copies]
-        ops.int4_ffn(dev, xd, nw, g, u, d, out, m, HIDDEN, inter, GS, eps=EPS)
-        if pg is not None:
-            pg.all_reduce(out)
-            torch.cuda.current_stream().synchronize()
-        check(L.tk_buffer_download(dev.handle, ob.ptr, out.data_ptr(), ob.nbytes))
+        check(Lb.tk_buffer_upload(dev.handle, xd.data_ptr(), xb_host.ptr, xb_host.nbytes))
+        res = run_step(i, xd, (xa, xb), True)
+        check(Lb.tk_buffer_download(dev.handle, ob_host.ptr, res.data_ptr(), ob_host.nbytes))
     e1.record(devstream)
     e1.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -331,36 +397,39 @@ def main():
         cpu_base = None
         if world == 1 and not args.no_cpu_baseline:
             try:
-                cpu_base = cpu_baseline_sample(W_full, x_host, m)
+                Wc = W_full if W_full is not None else data.make_ffn(SEED, hidden, inter_full, GS)
+                cpu_base = cpu_baseline_sample(Wc, x_host, m, hidden, inter_full)
             except Exception as e:
                 cpu_base = {"value": None, "unit": "GB/s", "cores": None, "kind": "port",
                             "sample": f"unavailable: {e}"}
+        traffic = load_traffic(m, world) if (args.model == "8b" and L == 1) else None
         line = {
             "metric": "INT4 FFN decode HBM GB/s", "value": round(value, 2), "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "n_gpus": world, "steps": steps_timed, "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
-            "tokens_per_s": round(m * args.steps / (ms / 1e3), 1),
+            "tokens_per_s": round(m * steps_timed / (ms / 1e3), 1),
             "pct_of_peak": round(100.0 * achieved / peak, 2),
             "pct_of_8tbs": round(100.0 * achieved / 8000.0, 2),
             "config": {
-                "workload": f"Llama-3-8B INT4 FFN decode (rmsnorm->gate/up->silu*up->down), batch {m}",
-                "hidden": HIDDEN, "inter": INTER, "group_size": GS, "batch": m,
+                "workload": workload_name(name, m, L),
+                "hidden": hidden, "inter": inter_full, "group_size": GS, "batch": m, "layers": L,
                 "parallelism": f"tp{world}", "weight_copies": copies,
-                "l2_guard": f"{copies} rotating weight copies = {copies * shard_bytes / 1e6:.0f} MB per GPU (> 3x L2)",
+                "l2_guard": f"{copies} weight copies x {L} block(s) = "
+                            f"{copies * L * shard_w_bytes / 1e6:.0f} MB per GPU (> 3x L2)",
                 "launch": "cuda-graph" if graph is not None else "stream",
                 "bytes_per_step": step_bytes_total,
             },
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind, "traffic": load_traffic(m, world),
-                         "kernel": "tk::int4_engine_kernel (FFN, 2 phases)"},
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         "kernel": "tk::int4_engine_kernel (FFN, gate/up then down)"},
             "cpu_baseline": cpu_base,
             "e2e": {"value": round(e2e, 3), "unit": "GB/s",
-                    "h2d_bytes_per_step": m * HIDDEN * 4, "d2h_bytes_per_step": m * HIDDEN * 4,
+                    "h2d_bytes_per_step": m * hidden * 4, "d2h_bytes_per_step": m * hidden * 4,
                     "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 5)},
-            "gpu_launches": args.steps,
+            "gpu_launches": steps_timed * L * (1 + (m - 1) // 4),
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
