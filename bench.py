@@ -319,7 +319,9 @@ def main():
     per_graph = max(1, min(args.steps, 4000 // L))
     reps = math.ceil(args.steps / per_graph)
     steps_timed = args.steps
-    if not args.no_graph and pg is None:
+    if not args.no_graph:
+        # one graph per rank; with several ranks it holds the NCCL all-reduces too (released
+        # before the process group is destroyed)
         try:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
