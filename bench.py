@@ -49,13 +49,19 @@ def ffn_bytes(m, hidden, inter, gs):
     return w + m * hidden * 4 + hidden * 4 + m * hidden * 4
 
 
+def ffn_flops(m, hidden, inter):
+    """Multiply-adds of the three projections, 2 FLOPs each."""
+    return 2 * m * 3 * hidden * inter
+
+
 def load_peaks():
+    """(HBM GB/s, dense f16/bf16 TFLOP/s burst, which)."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return 6650.0, 1590.0, "fallback"
 
 
 def load_traffic(m, n_gpus):
@@ -309,11 +315,15 @@ def main():
     def step(i):
         run_step(i, x0, (xa, xb), False)
 
-    # warm-up (also sizes the engine's scratch before any capture)
+    # warm-up (also sizes the engine's scratch before any capture); the last warm-up step
+    # counts the kernels one step enqueues
     for i in range(args.warmup):
+        n0 = dev.launch_count()
         step(i)
+        launches_per_step = dev.launch_count() - n0
     stream.synchronize()
     dev.synchronize()
+    ffn_path = ops.ffn_path(m, hidden, inter, GS)
 
     graph = None
     per_graph = max(1, min(args.steps, 4000 // L))
@@ -359,9 +369,13 @@ def main():
     check(lib().tk_device_check_error(dev.handle))
     ms_per_step = ms / steps_timed
     value = step_bytes_total * steps_timed / (ms / 1e3) / 1e9
-    peak, peak_kind = load_peaks()
+    peak, peak_tc, peak_kind = load_peaks()
     per_gpu_bytes = L * (shard_w_bytes + m * hidden * 4 * 2 + hidden * 4)
+    per_gpu_flops = L * ffn_flops(m, hidden, inter)
     achieved = per_gpu_bytes / (ms_per_step / 1e3) / 1e9
+    tflops = per_gpu_flops / (ms_per_step / 1e3) / 1e12
+    # the bound of the step: whichever of HBM bytes and tensor FLOPs takes longer at peak
+    tensor_bound = per_gpu_flops / (peak_tc * 1e12) > per_gpu_bytes / (peak * 1e9)
 
     # ---- end to end through the synchronous C ABI with host buffers -------------------
     import ctypes as C
@@ -405,6 +419,21 @@ def main():
                 cpu_base = {"value": None, "unit": "GB/s", "cores": None, "kind": "port",
                             "sample": f"unavailable: {e}"}
         traffic = load_traffic(m, world) if (args.model == "8b" and L == 1) else None
+        if ffn_path == 2:
+            kern = ("tk::int4_gemm_kernel x2 (gate/up with silu*up, down split-K) + rmsnorm, "
+                    "f16 cast, split-K reduction: the whole step")
+        else:
+            kern = "tk::int4_engine_kernel (FFN, gate/up then down)"
+        if tensor_bound:
+            roofline = {"bound": "tensor", "achieved": round(tflops, 2), "peak": peak_tc,
+                        "unit": "TFLOP/s", "frac": round(tflops / peak_tc, 4),
+                        "peak_kind": peak_kind + " bf16 dense (burst)", "traffic": traffic,
+                        "kernel": kern, "hbm_gbs": round(achieved, 2)}
+        else:
+            roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                        "unit": "GB/s", "frac": round(achieved / peak, 4),
+                        "peak_kind": peak_kind, "traffic": traffic, "kernel": kern,
+                        "tflops": round(tflops, 2)}
         line = {
             "metric": "INT4 FFN decode HBM GB/s", "value": round(value, 2), "unit": "GB/s",
             "n_gpus": world, "steps": steps_timed, "warmup": args.warmup,
@@ -421,17 +450,15 @@ def main():
                 "l2_guard": f"{copies} weight copies x {L} block(s) = "
                             f"{copies * L * shard_w_bytes / 1e6:.0f} MB per GPU (> 3x L2)",
                 "launch": "cuda-graph" if graph is not None else "stream",
+                "path": {2: "tcgen05 GEMM", 1: "streaming engine"}.get(ffn_path, "CUDA-core"),
                 "bytes_per_step": step_bytes_total,
             },
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind, "traffic": traffic,
-                         "kernel": "tk::int4_engine_kernel (FFN, gate/up then down)"},
+            "roofline": roofline,
             "cpu_baseline": cpu_base,
             "e2e": {"value": round(e2e, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": m * hidden * 4, "d2h_bytes_per_step": m * hidden * 4,
                     "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 5)},
-            "gpu_launches": steps_timed * L * (1 + (m - 1) // 4),
+            "gpu_launches": steps_timed * launches_per_step,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -83,6 +83,9 @@ void tk_device_destroy(tk_device *dev);
 const char *tk_device_name(tk_device *dev);
 /* Number of SMs the persistent kernels size their grid to. */
 int tk_device_sm_count(tk_device *dev);
+/* Kernels enqueued through this device so far (every launch of every entry point, also
+ * those recorded into a CUDA graph). No counterpart in the reference. */
+uint64_t tk_device_launch_count(tk_device *dev);
 /* The device's CUDA stream (cudaStream_t) used by the synchronous entry points. */
 void *tk_device_stream(tk_device *dev);
 /* Waits for all work queued on the device's stream; returns any deferred kernel error. */
@@ -199,9 +202,14 @@ int tk_qmatmul_int4_noalloc(const float *x, const uint8_t *w_packed, const uint1
                             const uint8_t *zeros, float *out, uint32_t m, uint32_t k,
                             uint32_t n, uint32_t group_size, void *stream);
 
-/* Which path tk_qmatmul_int4 / tk_int4_ffn would take for a shape:
- * 1 = tensor-core engine, 0 = CUDA-core fallback, <0 = invalid shape. */
+/* Which path tk_qmatmul_int4 would take for a shape with 16-byte aligned buffers and the
+ * default device settings: 2 = tcgen05 GEMM (m >= 16), 1 = streaming engine (m < 16, or a
+ * shape the GEMM does not tile), 0 = CUDA-core fallback, <0 = invalid shape.
+ * No counterpart in the reference (one shader serves every shape there). */
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t group_size);
+
+/* The same for tk_int4_ffn over [m][hidden] with an intermediate size inter. */
+int tk_int4_ffn_path(uint32_t m, uint32_t hidden, uint32_t inter, uint32_t group_size);
 
 #ifdef __cplusplus
 }

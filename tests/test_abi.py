@@ -43,6 +43,12 @@ def test_calls_without_gpu():
     assert L.tk_qmatmul_int4_path(1, 4800, 14336, 48) == 0
     assert L.tk_qmatmul_int4_path(1, 4096, 14335, 64) == -1
     assert L.tk_qmatmul_int4_path(1, 100, 64, 8) == -1
+    assert L.tk_qmatmul_int4_path(16, 4096, 14336, 64) == 2
+    assert L.tk_qmatmul_int4_path(16, 4096, 14464, 64) == 1   # 14464 % 256 != 0
+    assert L.tk_qmatmul_int4_path(15, 4096, 14336, 64) == 1
+    assert L.tk_int4_ffn_path(1, 4096, 14336, 64) == 1
+    assert L.tk_int4_ffn_path(16, 4096, 14336, 64) == 2
+    assert L.tk_int4_ffn_path(16, 4800, 9600, 48) == 0
 
 
 def test_null_arguments_rejected():

@@ -1,0 +1,65 @@
+// tk_gemm.h -- parameters of the batch >= 16 INT4 GEMM (tcgen05 / tensor memory).
+//
+// Y[M][N] = X[M][K] . W[K][N] with W in the reference's packed INT4 layout
+// (src/kernels/shaders.zig:442-501): the weights are dequantised in shared memory to f16
+// ((q - z) * scale, one rounding) and multiplied on the 5th-generation tensor cores with f32
+// accumulators in tensor memory.  MMA M = 128 output columns (the dequantised weights, A,
+// MN-major), MMA N = a tile of NT tokens (the f16 activations, B, K-major); both with the
+// 128-byte swizzle.
+// A CTA computes two 128-column tiles (two matrices at the same columns -- gate and up -- or
+// 256 adjacent columns of one matrix) for NT tokens over a range of K.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+namespace tk {
+
+constexpr int kGemmTileCols = 128;  // MMA M: output columns per tile
+constexpr int kGemmTiles = 2;       // tiles per CTA
+constexpr int kGemmKStep = 64;      // k per pipeline stage (32 packed rows)
+constexpr int kGemmDequantWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kGemmDequantWarps;  // warp 0 TMA, warp 1 MMA, dequant
+constexpr int kGemmATileBytes = kGemmTileCols * kGemmKStep * 2;  // one dequantised f16 tile
+constexpr int kGemmMaxRawStages = 12;
+constexpr int kGemmMaxAStages = 4;
+
+enum GemmEpilogue : int {
+  kGemmStore = 0,    // out[m][n] = acc (+ residual[m][n])
+  kGemmSiluMul = 1,  // h = silu(tile 0) * tile 1 -> h16 (f16, the next GEMM's activations), h32
+  kGemmPartial = 2,  // out[split][m][n] = acc (reduced by a separate pass)
+};
+
+struct GemmParams {
+  int M, K, N, gs;
+  int splits;  // the K steps are split evenly over gridDim.z
+  int pair;    // 1: tile t from matrix t at the same columns; 0: matrix 0, 256 adjacent columns
+  const uint16_t* scales[kGemmTiles];
+  const uint8_t* zeros[kGemmTiles];
+  int epi;
+  float* out;
+  const float* residual;
+  __half* h16;
+  float* h32;
+  int raw_stages;      // ring of TMA copies: activations, packed weights, scales, zero points
+  int raw_stage_bytes;
+  int a_stages;        // ring of dequantised A tiles (both tiles of a step)
+  unsigned* err;
+  unsigned long long timeout_ns;
+};
+
+struct GemmMaps {
+  CUtensorMap x;                 // f16 activations [rows][K], box 64 x NT, 128-byte swizzle
+  CUtensorMap w[kGemmTiles];     // packed weights [K/2][N] u8, box 128 x 32
+};
+
+// Shared-memory bytes of one stage of the TMA ring for a token tile of nt (1024-aligned):
+// activations (nt rows of 64 f16), packed rows of both tiles (4 KB each), scales and zero
+// points of up to 4 groups per tile.
+__host__ __device__ constexpr int gemm_raw_stage_bytes(int nt) {
+  return (nt * 128 + kGemmTiles * 4096 + kGemmTiles * 4 * (256 + 64) + 1023) & ~1023;
+}
+// One stage of the dequantised ring: both A tiles.
+constexpr int kGemmAStageBytes = kGemmTiles * kGemmATileBytes;
+
+}  // namespace tk

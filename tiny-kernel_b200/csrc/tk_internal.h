@@ -5,7 +5,10 @@
 #include <cstddef>
 #include <cstdint>
 
+#include <cuda_fp16.h>
+
 #include "tk_engine.h"
+#include "tk_gemm.h"
 
 namespace tk {
 
@@ -34,5 +37,12 @@ cudaError_t launch_fused_rmsnorm_rope(const float* x, const float* w, const floa
                                       int head_dim, int pos, float eps, cudaStream_t st);
 cudaError_t launch_silu_mul(const float* g, const float* u, float* out, int n, cudaStream_t st);
 cudaError_t launch_add(const float* a, const float* b, float* out, int n, cudaStream_t st);
+cudaError_t launch_f32_to_f16(const float* x, __half* y, long long n, cudaStream_t st);
+cudaError_t launch_splitk_reduce(const float* part, int splits, long long mn, const float* residual,
+                                 float* y, cudaStream_t st);
+
+// tk_gemm.cu -- batch >= 16 GEMM (tcgen05); nt = token tile in {16, 32, 64, 128, 256}
+cudaError_t gemm_launch(int nt, const GemmMaps& maps, const GemmParams& p, dim3 grid, size_t smem,
+                        cudaStream_t st);
 
 }  // namespace tk

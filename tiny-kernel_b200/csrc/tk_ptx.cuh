@@ -1,8 +1,8 @@
 // tk_ptx.cuh -- thin inline-PTX wrappers used by the sm_100a kernels.
 //
 // mbarrier transaction barriers, TMA (cp.async.bulk / cp.async.bulk.tensor) loads
-// into shared memory, L2 eviction hints, the m16n8k32 int8 tensor-core MMA, dp2a, and a
-// bounded wait helper.  No cluster multicast is used anywhere in this project.
+// into shared memory, L2 eviction hints, the m16n8k32 int8 tensor-core MMA, dp2a, tcgen05
+// (MMA issue/commit, tensor-memory alloc/load), and a bounded wait helper.  No cluster multicast is used anywhere in this project.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -166,6 +166,76 @@ __device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
+
+// ---- tcgen05 (5th-generation tensor cores, accumulators in tensor memory) ----------------
+// Shared-memory matrix descriptor (sm100 version 1): start address, leading / stride byte
+// offsets (16-byte units), layout (0 = no swizzle, 2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t umma_smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                                   uint32_t layout) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+// Instruction descriptor of kind::f16: f32 accumulate, A and B f16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (0u << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+// The same with A MN-major (A stored as k rows of M contiguous elements).
+__host__ __device__ constexpr uint32_t umma_idesc_f16_amn(int m, int n) {
+  return umma_idesc_f16(m, n) | (1u << 15);
+}
+// D[tmem] (+)= A[smem] x B[smem] (f16 inputs, f32 accumulate), issued by one thread.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+// Arrives (once) on an mbarrier when every tcgen05.mma issued so far by this thread completes.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tcgen05_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tcgen05_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+// Orders this thread's generic shared-memory writes before later async-proxy reads
+// (tcgen05.mma operands) of shared memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Warp-collective tensor-memory allocation (address written to *slot) and release.
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_addr(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// Warp-collective load of 8 consecutive 32-bit columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 }  // namespace tk
 
 namespace tk {

@@ -46,6 +46,13 @@ int fail(int status, const char* fmt, ...) {
                   __LINE__);                                                                  \
   } while (0)
 
+// A kernel launch on a device: counted (tk_device_launch_count), then checked.
+#define TK_LAUNCH(dev, expr) \
+  do {                       \
+    ++(dev)->launches;       \
+    TK_CUDA_TRY(expr);       \
+  } while (0)
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
 std::once_flag g_encode_once;
 
@@ -82,7 +89,11 @@ struct tk_device {
   ScratchBuf frag[1];      // per-CTA prologue records when they do not fit in shared memory
   ScratchBuf partials[2];  // split-K partial sums: [0] first reduction, [1] second
   ScratchBuf counters[2];  // segment counters per 128-column sub-tile of each
+  // batch >= 16 GEMM path: f16 activations, normalised x (f32), f16 h, split-K partials
+  ScratchBuf g_x16, g_xn, g_h16, g_part;
+  int gemm_enabled = 1;  // TK_GEMM=0 routes every batch through the engine
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
+  unsigned long long launches = 0;      // kernels enqueued through this device
   std::vector<TmapEntry> tmaps;
 };
 
@@ -301,7 +312,7 @@ int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, c
   int blocks = 0;
   TK_CUDA_TRY(engine_occupancy(mt, p.gs0, smem, &blocks));
   if (blocks < 1) return fail(TK_ERR_UNSUPPORTED, "engine kernel cannot be resident");
-  TK_CUDA_TRY(engine_launch(mt, p.gs0, maps, p, d->sm_count, smem, st));
+  TK_LAUNCH(d, engine_launch(mt, p.gs0, maps, p, d->sm_count, smem, st));
   return TK_OK;
 }
 
@@ -427,6 +438,183 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   return launch_engine(d, mt, maps, p, st);
 }
 
+// ---- batch >= 16: the tcgen05 GEMM path (tk_gemm.cu) ----------------------------------------
+
+constexpr int kGemmMinRows = 16;
+
+int gemm_nt(int m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256; }
+
+// Shapes the GEMM takes: k in whole 64-steps of whole groups, columns in whole CTA tiles.
+bool gemm_shape(uint32_t k, uint32_t n, uint32_t gs, bool pair) {
+  return k % kGemmKStep == 0 && (gs == 16 || gs == 32 || gs == 64 || gs == 128) && k % gs == 0 &&
+         n % (pair ? kGemmTileCols : kGemmTiles * kGemmTileCols) == 0;
+}
+
+// f16 activations [rows][k] for the B operand: box 64 x nt, 128-byte swizzle (rows beyond
+// `rows` read as zero).
+int act_tmap(const void* base, uint64_t k, uint64_t rows, uint32_t nt, CUtensorMap* out) {
+  int st = get_encoder();
+  if (st != TK_OK) return st;
+  cuuint64_t dims[2] = {k, rows};
+  cuuint64_t strides[1] = {k * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kGemmKStep, nt};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed (%d)", (int)r);
+  return TK_OK;
+}
+
+// Packed weights [k/2][n] for the dequantisers: box 128 columns x 32 packed rows.
+int gemm_wtmap(const void* w, uint64_t n, uint64_t k, CUtensorMap* out) {
+  int st = get_encoder();
+  if (st != TK_OK) return st;
+  cuuint64_t dims[2] = {n, k / 2};
+  cuuint64_t strides[1] = {n};
+  cuuint32_t box[2] = {(cuuint32_t)kGemmTileCols, (cuuint32_t)(kGemmKStep / 2)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode_tiled(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed (%d)", (int)r);
+  return TK_OK;
+}
+
+// One GEMM launch: colblocks CTA column tiles x token tiles x splits.
+int gemm_run(tk_device* d, const GemmMaps& maps, GemmParams& p, int nt, int colblocks,
+             cudaStream_t st) {
+  // a short ring of dequantised tiles, the rest of shared memory for the TMA ring
+  const int avail = d->smem_optin - kStaticSmemReserve - 1024;
+  p.a_stages = nt >= 128 ? 2 : 3;
+  p.raw_stage_bytes = gemm_raw_stage_bytes(nt);
+  p.raw_stages = std::min(kGemmMaxRawStages, (avail - p.a_stages * kGemmAStageBytes) / p.raw_stage_bytes);
+  if (p.raw_stages < 2) return fail(TK_ERR_UNSUPPORTED, "GEMM stages do not fit in shared memory");
+  p.err = d->err;
+  p.timeout_ns = d->timeout_ns;
+  const size_t smem = 1024 + (size_t)p.a_stages * kGemmAStageBytes +
+                      (size_t)p.raw_stages * p.raw_stage_bytes;
+  const dim3 grid((unsigned)colblocks, (unsigned)((p.M + nt - 1) / nt), (unsigned)p.splits);
+  TK_LAUNCH(d, gemm_launch(nt, maps, p, grid, smem, st));
+  return TK_OK;
+}
+
+// K splits so that the grid covers the SMs (each split a whole number of 64-k steps).
+int gemm_splits(tk_device* d, int ctas, int k) {
+  const int steps = k / kGemmKStep;
+  return std::max(1, std::min({steps, d->sm_count / ctas, 16}));
+}
+
+// y[m][n] (+)= x[m][k] . W for m >= 16 rows on the tensor cores.
+int qmatmul_gemm(tk_device* d, const float* x, const uint8_t* w, const uint16_t* s,
+                 const uint8_t* z, float* out, int m, int k, int n, int gs, cudaStream_t st) {
+  const int nt = gemm_nt(m);
+  int stt = scratch_ensure(d, d->g_x16, (size_t)m * k * 2);
+  if (stt != TK_OK) return stt;
+  __half* x16 = static_cast<__half*>(d->g_x16.ptr);
+  TK_LAUNCH(d, launch_f32_to_f16(x, x16, (long long)m * k, st));
+  GemmMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  if ((stt = act_tmap(x16, k, m, nt, &maps.x)) != TK_OK) return stt;
+  if ((stt = gemm_wtmap(w, n, k, &maps.w[0])) != TK_OK) return stt;
+  maps.w[1] = maps.w[0];
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = m;
+  p.K = k;
+  p.N = n;
+  p.gs = gs;
+  p.pair = 0;
+  p.scales[0] = p.scales[1] = s;
+  p.zeros[0] = p.zeros[1] = z;
+  const int colblocks = n / (kGemmTiles * kGemmTileCols);
+  p.splits = gemm_splits(d, colblocks * ((m + nt - 1) / nt), k);
+  if (p.splits == 1) {
+    p.epi = kGemmStore;
+    p.out = out;
+    return gemm_run(d, maps, p, nt, colblocks, st);
+  }
+  stt = scratch_ensure(d, d->g_part, (size_t)p.splits * m * n * 4);
+  if (stt != TK_OK) return stt;
+  p.epi = kGemmPartial;
+  p.out = static_cast<float*>(d->g_part.ptr);
+  if ((stt = gemm_run(d, maps, p, nt, colblocks, st)) != TK_OK) return stt;
+  TK_LAUNCH(d, launch_splitk_reduce(p.out, p.splits, (long long)m * n, nullptr, out, st));
+  return TK_OK;
+}
+
+// The INT4 FFN for m >= 16 rows: rmsnorm -> f16, gate/up GEMM with silu(gate) * up in its
+// epilogue (h in f16 for the down GEMM, and in f32 when asked), down GEMM split over K,
+// reduction (+ residual).
+int ffn_gemm(tk_device* d, const float* x, const float* norm_w, const tk_int4_matrix* gate,
+             const tk_int4_matrix* up, const tk_int4_matrix* down, float* out, float* h_out,
+             int m, int hidden, int inter, int gs, float eps, bool residual, cudaStream_t st) {
+  const int nt = gemm_nt(m);
+  int stt;
+  if ((stt = scratch_ensure(d, d->g_xn, (size_t)m * hidden * 4)) != TK_OK) return stt;
+  if ((stt = scratch_ensure(d, d->g_x16, (size_t)m * hidden * 2)) != TK_OK) return stt;
+  if ((stt = scratch_ensure(d, d->g_h16, (size_t)m * inter * 2)) != TK_OK) return stt;
+  float* xn = static_cast<float*>(d->g_xn.ptr);
+  __half* x16 = static_cast<__half*>(d->g_x16.ptr);
+  __half* h16 = static_cast<__half*>(d->g_h16.ptr);
+  TK_LAUNCH(d, launch_rmsnorm(x, norm_w, xn, m, hidden, eps, st));
+  TK_LAUNCH(d, launch_f32_to_f16(xn, x16, (long long)m * hidden, st));
+  // gate/up: tile 0 = gate, tile 1 = up at the same 128 columns
+  GemmMaps ma;
+  std::memset(&ma, 0, sizeof(ma));
+  if ((stt = act_tmap(x16, hidden, m, nt, &ma.x)) != TK_OK) return stt;
+  if ((stt = gemm_wtmap(gate->w_packed, inter, hidden, &ma.w[0])) != TK_OK) return stt;
+  if ((stt = gemm_wtmap(up->w_packed, inter, hidden, &ma.w[1])) != TK_OK) return stt;
+  GemmParams a;
+  std::memset(&a, 0, sizeof(a));
+  a.M = m;
+  a.K = hidden;
+  a.N = inter;
+  a.gs = gs;
+  a.splits = 1;
+  a.pair = 1;
+  a.scales[0] = gate->scales;
+  a.scales[1] = up->scales;
+  a.zeros[0] = gate->zeros;
+  a.zeros[1] = up->zeros;
+  a.epi = kGemmSiluMul;
+  a.h16 = h16;
+  a.h32 = h_out;
+  if ((stt = gemm_run(d, ma, a, nt, inter / kGemmTileCols, st)) != TK_OK) return stt;
+  // down: 256 adjacent output columns per CTA, K split to cover the SMs
+  GemmMaps mb;
+  std::memset(&mb, 0, sizeof(mb));
+  if ((stt = act_tmap(h16, inter, m, nt, &mb.x)) != TK_OK) return stt;
+  if ((stt = gemm_wtmap(down->w_packed, hidden, inter, &mb.w[0])) != TK_OK) return stt;
+  mb.w[1] = mb.w[0];
+  GemmParams b;
+  std::memset(&b, 0, sizeof(b));
+  b.M = m;
+  b.K = inter;
+  b.N = hidden;
+  b.gs = gs;
+  b.pair = 0;
+  b.scales[0] = b.scales[1] = down->scales;
+  b.zeros[0] = b.zeros[1] = down->zeros;
+  const int colblocks = hidden / (kGemmTiles * kGemmTileCols);
+  b.splits = gemm_splits(d, colblocks * ((m + nt - 1) / nt), inter);
+  if (b.splits == 1) {
+    b.epi = kGemmStore;
+    b.out = out;
+    b.residual = residual ? x : nullptr;
+    return gemm_run(d, mb, b, nt, colblocks, st);
+  }
+  if ((stt = scratch_ensure(d, d->g_part, (size_t)b.splits * m * hidden * 4)) != TK_OK) return stt;
+  b.epi = kGemmPartial;
+  b.out = static_cast<float*>(d->g_part.ptr);
+  if ((stt = gemm_run(d, mb, b, nt, colblocks, st)) != TK_OK) return stt;
+  TK_LAUNCH(d, launch_splitk_reduce(b.out, b.splits, (long long)m * hidden, residual ? x : nullptr,
+                                   out, st));
+  return TK_OK;
+}
+
 bool matrix_aligned(const tk_int4_matrix* a) {
   return a && aligned16(a->w_packed) && aligned16(a->scales) && aligned16(a->zeros);
 }
@@ -477,6 +665,7 @@ int tk_device_create(int ordinal, tk_device** out) {
   d->smem_optin = (int)d->prop.sharedMemPerBlockOptin;
   if (const char* env = std::getenv("TK_ENGINE_STAGES")) d->stages_override = std::atoi(env);
   if (const char* env = std::getenv("TK_FFN_SPLIT")) d->ffn_split = std::atoi(env);
+  if (const char* env = std::getenv("TK_GEMM")) d->gemm_enabled = std::atoi(env);
   if (const char* env = std::getenv("TK_WAIT_TIMEOUT_MS"))
     d->timeout_ns = (unsigned long long)std::atoll(env) * 1000000ull;
   if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -495,7 +684,7 @@ void tk_device_destroy(tk_device* d) {
   cudaSetDevice(d->ordinal);
   if (d->stream) cudaStreamSynchronize(d->stream);
   for (auto* b : {&d->frag[0], &d->partials[0], &d->partials[1], &d->counters[0],
-                  &d->counters[1]})
+                  &d->counters[1], &d->g_x16, &d->g_xn, &d->g_h16, &d->g_part})
     if (b->ptr) cudaFree(b->ptr);
   if (d->sync) cudaFree(d->sync);
   if (d->err) cudaFree(d->err);
@@ -506,6 +695,7 @@ void tk_device_destroy(tk_device* d) {
 
 const char* tk_device_name(tk_device* d) { return d ? d->name : ""; }
 int tk_device_sm_count(tk_device* d) { return d ? d->sm_count : 0; }
+uint64_t tk_device_launch_count(tk_device* d) { return d ? d->launches : 0; }
 void* tk_device_stream(tk_device* d) { return d ? static_cast<void*>(d->stream) : nullptr; }
 
 int tk_device_synchronize(tk_device* d) {
@@ -604,7 +794,19 @@ int tk_buffer_download(tk_device* d, void* dst, const void* src, size_t bytes) {
 
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
   if (m == 0 || k == 0 || n == 0 || gs == 0 || gs % 8 || k % gs || n % 2) return -1;
-  return engine_shape(k, n, gs) ? 1 : 0;
+  if (!engine_shape(k, n, gs)) return 0;
+  return m >= kGemmMinRows && gemm_shape(k, n, gs, false) ? 2 : 1;
+}
+
+int tk_int4_ffn_path(uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs) {
+  if (m == 0 || hidden == 0 || inter == 0 || gs == 0 || gs % 8 || hidden % gs || inter % gs ||
+      hidden % 2 || inter % 2)
+    return -1;
+  if (!engine_shape(hidden, inter, gs) || !engine_shape(inter, hidden, gs)) return 0;
+  return m >= kGemmMinRows && gemm_shape(hidden, inter, gs, true) &&
+                 gemm_shape(inter, hidden, gs, false)
+             ? 2
+             : 1;
 }
 
 int tk_qmatmul_int4_async(tk_device* d, const float* x, const uint8_t* w, const uint16_t* s,
@@ -619,9 +821,11 @@ int tk_qmatmul_int4_async(tk_device* d, const float* x, const uint8_t* w, const 
   const bool fast = engine_shape(k, n, gs) && aligned16(x) && aligned16(w) && aligned16(s) &&
                     aligned16(z) && aligned16(out);
   if (!fast) {
-    TK_CUDA_TRY(launch_qmatmul_int4_generic(x, w, s, z, out, (int)m, (int)k, (int)n, (int)gs, cs));
+    TK_LAUNCH(d, launch_qmatmul_int4_generic(x, w, s, z, out, (int)m, (int)k, (int)n, (int)gs, cs));
     return TK_OK;
   }
+  if (d->gemm_enabled && m >= kGemmMinRows && gemm_shape(k, n, gs, false))
+    return qmatmul_gemm(d, x, w, s, z, out, (int)m, (int)k, (int)n, (int)gs, cs);
   for (uint32_t r = 0; r < m; r += 4) {
     const uint32_t mm = std::min<uint32_t>(4, m - r);
     st = qmatmul_engine_chunk(d, x + (size_t)r * k, w, s, z, out + (size_t)r * n, (int)mm, (int)k,
@@ -645,7 +849,7 @@ int tk_dequant_int4(tk_device* d, const uint8_t* w, const uint16_t* s, const uin
   if (st != TK_OK) return st;
   st = set_device(d);
   if (st != TK_OK) return st;
-  TK_CUDA_TRY(launch_dequant_int4(w, s, z, out, (int)k, (int)n, (int)gs, d->stream));
+  TK_LAUNCH(d, launch_dequant_int4(w, s, z, out, (int)k, (int)n, (int)gs, d->stream));
   return sync_and_check(d, d->stream);
 }
 
@@ -655,7 +859,7 @@ int tk_rmsnorm_async(tk_device* d, const float* x, const float* w, float* out, u
   if (rows == 0 || dim == 0) return fail(TK_ERR_ARG, "zero dimension");
   int st = set_device(d);
   if (st != TK_OK) return st;
-  TK_CUDA_TRY(launch_rmsnorm(x, w, out, (int)rows, (int)dim, eps, pick_stream(d, stream)));
+  TK_LAUNCH(d, launch_rmsnorm(x, w, out, (int)rows, (int)dim, eps, pick_stream(d, stream)));
   return TK_OK;
 }
 
@@ -674,7 +878,7 @@ int tk_fused_rmsnorm_rope_async(tk_device* d, const float* x, const float* w, co
     return fail(TK_ERR_ARG, "dim=%u must be a positive multiple of an even head_dim=%u", dim, head_dim);
   int st = set_device(d);
   if (st != TK_OK) return st;
-  TK_CUDA_TRY(launch_fused_rmsnorm_rope(x, w, cosc, sinc, out, (int)rows, (int)dim, (int)head_dim,
+  TK_LAUNCH(d, launch_fused_rmsnorm_rope(x, w, cosc, sinc, out, (int)rows, (int)dim, (int)head_dim,
                                         (int)pos, eps, pick_stream(d, stream)));
   return TK_OK;
 }
@@ -693,7 +897,7 @@ int tk_silu_mul_async(tk_device* d, const float* g, const float* u, float* out, 
   if (n == 0) return TK_OK;
   int st = set_device(d);
   if (st != TK_OK) return st;
-  TK_CUDA_TRY(launch_silu_mul(g, u, out, (int)n, pick_stream(d, stream)));
+  TK_LAUNCH(d, launch_silu_mul(g, u, out, (int)n, pick_stream(d, stream)));
   return TK_OK;
 }
 
@@ -723,6 +927,10 @@ int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const t
                     aligned16(x) && aligned16(norm_w) && aligned16(out) &&
                     (!h_out || aligned16(h_out)) && matrix_aligned(gate) && matrix_aligned(up) &&
                     matrix_aligned(down);
+  if (fast && d->gemm_enabled && m >= kGemmMinRows && gemm_shape(hidden, inter, gs, true) &&
+      gemm_shape(inter, hidden, gs, false))
+    return ffn_gemm(d, x, norm_w, gate, up, down, out, h_out, (int)m, (int)hidden, (int)inter,
+                    (int)gs, eps, residual, cs);
   if (fast) {
     for (uint32_t r = 0; r < m; r += 4) {
       const uint32_t mm = std::min<uint32_t>(4, m - r);
@@ -741,16 +949,16 @@ int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const t
   TK_CUDA_TRY(cudaMallocAsync(&u, mi * 4, cs));
   TK_CUDA_TRY(cudaMallocAsync(&h, mi * 4, cs));
   TK_CUDA_TRY(cudaMallocAsync(&y, mh * 4, cs));
-  TK_CUDA_TRY(launch_rmsnorm(x, norm_w, normed, (int)m, (int)hidden, eps, cs));
-  TK_CUDA_TRY(launch_qmatmul_int4_generic(normed, gate->w_packed, gate->scales, gate->zeros, g, (int)m,
+  TK_LAUNCH(d, launch_rmsnorm(x, norm_w, normed, (int)m, (int)hidden, eps, cs));
+  TK_LAUNCH(d, launch_qmatmul_int4_generic(normed, gate->w_packed, gate->scales, gate->zeros, g, (int)m,
                                           (int)hidden, (int)inter, (int)gs, cs));
-  TK_CUDA_TRY(launch_qmatmul_int4_generic(normed, up->w_packed, up->scales, up->zeros, u, (int)m,
+  TK_LAUNCH(d, launch_qmatmul_int4_generic(normed, up->w_packed, up->scales, up->zeros, u, (int)m,
                                           (int)hidden, (int)inter, (int)gs, cs));
-  TK_CUDA_TRY(launch_silu_mul(g, u, h, (int)mi, cs));
+  TK_LAUNCH(d, launch_silu_mul(g, u, h, (int)mi, cs));
   if (h_out) TK_CUDA_TRY(cudaMemcpyAsync(h_out, h, mi * 4, cudaMemcpyDeviceToDevice, cs));
-  TK_CUDA_TRY(launch_qmatmul_int4_generic(h, down->w_packed, down->scales, down->zeros, y, (int)m,
+  TK_LAUNCH(d, launch_qmatmul_int4_generic(h, down->w_packed, down->scales, down->zeros, y, (int)m,
                                           (int)inter, (int)hidden, (int)gs, cs));
-  if (residual) TK_CUDA_TRY(launch_add(x, y, out, (int)mh, cs));
+  if (residual) TK_LAUNCH(d, launch_add(x, y, out, (int)mh, cs));
   else TK_CUDA_TRY(cudaMemcpyAsync(out, y, mh * 4, cudaMemcpyDeviceToDevice, cs));
   for (float* p : {normed, g, u, h, y}) TK_CUDA_TRY(cudaFreeAsync(p, cs));
   return TK_OK;

@@ -128,7 +128,33 @@ __global__ void add_kernel(const float* __restrict__ a, const float* __restrict_
   out[i] = a[i] + b[i];
 }
 
+__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2half_rn(x[i]);
+}
+
+// y[m][n] = sum over splits (in split order) of part[split][m][n] (+ residual[m][n])
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, long long mn,
+                                     const float* __restrict__ residual, float* __restrict__ y) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= mn) return;
+  float a = 0.f;
+  for (int s = 0; s < splits; ++s) a += part[(long long)s * mn + i];
+  y[i] = residual ? residual[i] + a : a;
+}
+
 }  // namespace
+
+cudaError_t launch_f32_to_f16(const float* x, __half* y, long long n, cudaStream_t st) {
+  f32_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, y, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_splitk_reduce(const float* part, int splits, long long mn, const float* residual,
+                                 float* y, cudaStream_t st) {
+  splitk_reduce_kernel<<<(unsigned)((mn + 255) / 256), 256, 0, st>>>(part, splits, mn, residual, y);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_qmatmul_int4_generic(const float* x, const uint8_t* w, const uint16_t* s,
                                         const uint8_t* z, float* out, int m, int k, int n,

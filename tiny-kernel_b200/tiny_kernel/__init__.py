@@ -111,6 +111,10 @@ class Device:
     def sm_count(self) -> int:
         return _lib.lib().tk_device_sm_count(self.handle)
 
+    def launch_count(self) -> int:
+        """Kernels enqueued through this device so far (graph captures included)."""
+        return int(_lib.lib().tk_device_launch_count(self.handle))
+
     def stream(self) -> int:
         return _lib.lib().tk_device_stream(self.handle)
 

@@ -47,6 +47,7 @@ SIGNATURES = {
     "tk_device_destroy": (None, [vp]),
     "tk_device_name": (C.c_char_p, [vp]),
     "tk_device_sm_count": (i32, [vp]),
+    "tk_device_launch_count": (C.c_uint64, [vp]),
     "tk_device_stream": (vp, [vp]),
     "tk_device_synchronize": (i32, [vp]),
     "tk_device_check_error": (i32, [vp]),
@@ -57,6 +58,7 @@ SIGNATURES = {
     "tk_qmatmul_int4": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),
     "tk_qmatmul_int4_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
     "tk_qmatmul_int4_path": (i32, [u32, u32, u32, u32]),
+    "tk_int4_ffn_path": (i32, [u32, u32, u32, u32]),
     "tk_qmatmul_int4_noalloc": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
     "tk_rmsnorm": (i32, [vp, vp, vp, vp, u32, u32, f32]),
     "tk_rmsnorm_async": (i32, [vp, vp, vp, vp, u32, u32, f32, vp]),

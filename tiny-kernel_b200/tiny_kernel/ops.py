@@ -101,5 +101,11 @@ def dequant_int4(device, w_packed, scales, zeros, out, k, n, group_size):
 
 
 def path(m, k, n, group_size) -> int:
-    """1 = tensor-core engine, 0 = CUDA-core fallback, -1 = invalid shape."""
+    """qmatmul_int4's path: 2 = tcgen05 GEMM, 1 = streaming engine, 0 = CUDA-core fallback,
+    -1 = invalid shape."""
     return _lib.lib().tk_qmatmul_int4_path(int(m), int(k), int(n), int(group_size))
+
+
+def ffn_path(m, hidden, inter, group_size) -> int:
+    """int4_ffn's path, with the same codes as path()."""
+    return _lib.lib().tk_int4_ffn_path(int(m), int(hidden), int(inter), int(group_size))
