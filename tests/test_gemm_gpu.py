@@ -36,6 +36,7 @@ def run_qmatmul(torch, tkdev, x, M):
     (40, 1024, 512, 32),      # a ragged token tile
     (128, 256, 768, 128),
     (300, 512, 512, 16),      # two token tiles of 256
+    (24, 1024, 512, 32),      # a ragged token tile of 32
 ])
 def test_gemm_qmatmul_vs_oracle(torch_cuda, tkdev, m, K, N, gs):
     assert ops.path(m, K, N, gs) == 2

@@ -18,7 +18,7 @@ namespace tk {
 constexpr int kGemmTileCols = 128;  // MMA M: output columns per tile
 constexpr int kGemmTiles = 2;       // tiles per CTA
 constexpr int kGemmKStep = 64;      // k per pipeline stage (32 packed rows)
-constexpr int kGemmDequantWarps = 8;
+constexpr int kGemmDequantWarps = 16;  // warp d: tile d/8, k rows 8(d%8) .. 8(d%8)+7 of a step
 constexpr int kGemmThreads = 64 + 32 * kGemmDequantWarps;  // warp 0 TMA, warp 1 MMA, dequant
 constexpr int kGemmATileBytes = kGemmTileCols * kGemmKStep * 2;  // one dequantised f16 tile
 constexpr int kGemmMaxRawStages = 12;
@@ -44,14 +44,44 @@ struct GemmParams {
   int raw_stages;      // ring of TMA copies: activations, packed weights, scales, zero points
   int raw_stage_bytes;
   int a_stages;        // ring of dequantised A tiles (both tiles of a step)
+  int aux_stages;      // tensor-memory kernel: ring of scales / zero points (8 groups a stage)
+  int tm;              // 1: the tensor-memory kernel
   unsigned* err;
   unsigned long long timeout_ns;
+  unsigned long long* trace;  // optional per-CTA cycle counts (kTraceEvents slots per CTA)
+  int trace_ctas;             // CTAs (in launch order) that record
 };
 
 struct GemmMaps {
   CUtensorMap x;                 // f16 activations [rows][K], box 64 x NT, 128-byte swizzle
   CUtensorMap w[kGemmTiles];     // packed weights [K/2][N] u8, box 128 x 32
+  CUtensorMap sc[kGemmTiles];    // scales [K/gs][N] f16, box 128 x 8 groups (tensor-memory kernel)
+  CUtensorMap ze[kGemmTiles];    // zero points [K/gs][N/2] u8, box 64 x 8 groups (ditto)
 };
+
+// Tensor-memory kernel (token tiles up to kGemmTmemMaxNT, K a multiple of 128): the
+// dequantised A tiles live in tensor memory; a step is 128 k (64 packed rows); the weights
+// arrive with the 128-byte swizzle; scales and zero points arrive 8 groups at a time in their
+// own ring.
+constexpr int kGemmTmemMaxNT = 64;   // 128- and 256-token tiles: the shared-memory kernel
+constexpr int kGemmTmKStep = 128;
+constexpr int kGemmTmDequantWarps = 8;  // warp d: tile d/4, tensor-memory lane quarter (d+2)%4
+constexpr int kGemmTmThreads = 64 + 32 * kGemmTmDequantWarps;
+constexpr int kGemmTmWeightTile = kGemmTileCols * kGemmTmKStep / 2;  // 8 KB of packed rows
+constexpr int kGemmAuxGroups = 8;
+constexpr int kGemmAuxStageBytes = kGemmTiles * kGemmAuxGroups * (256 + 64);  // 5120
+constexpr int kGemmMaxAuxStages = 4;
+constexpr int kGemmTmemMaxAStages = 3;
+// activations (two 64-k chunks of nt rows), then both packed-weight tiles
+__host__ __device__ constexpr int gemm_tm_raw_stage_bytes(int nt) {
+  return 2 * nt * 128 + kGemmTiles * kGemmTmWeightTile;
+}
+// Steps (128 k) covered by one stage of the scale / zero-point ring (8 groups).
+__host__ __device__ constexpr int gemm_aux_steps(int gs) { return gs / 16; }
+// The tensor-memory kernel takes token tiles up to 64 and K in whole 128-k steps.
+__host__ __device__ constexpr bool gemm_use_tm(int nt, int k) {
+  return nt <= kGemmTmemMaxNT && k % kGemmTmKStep == 0;
+}
 
 // Shared-memory bytes of one stage of the TMA ring for a token tile of nt (1024-aligned):
 // activations (nt rows of 64 f16), packed rows of both tiles (4 KB each), scales and zero

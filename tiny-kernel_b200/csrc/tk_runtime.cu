@@ -89,8 +89,8 @@ struct tk_device {
   ScratchBuf frag[1];      // per-CTA prologue records when they do not fit in shared memory
   ScratchBuf partials[2];  // split-K partial sums: [0] first reduction, [1] second
   ScratchBuf counters[2];  // segment counters per 128-column sub-tile of each
-  // batch >= 16 GEMM path: f16 activations, normalised x (f32), f16 h, split-K partials
-  ScratchBuf g_x16, g_xn, g_h16, g_part;
+  // batch >= 16 GEMM path: f16 activations, f16 h, split-K partials
+  ScratchBuf g_x16, g_h16, g_part;
   int gemm_enabled = 1;  // TK_GEMM=0 routes every batch through the engine
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   unsigned long long launches = 0;      // kernels enqueued through this device
@@ -467,43 +467,101 @@ int act_tmap(const void* base, uint64_t k, uint64_t rows, uint32_t nt, CUtensorM
   return TK_OK;
 }
 
-// Packed weights [k/2][n] for the dequantisers: box 128 columns x 32 packed rows.
-int gemm_wtmap(const void* w, uint64_t n, uint64_t k, CUtensorMap* out) {
+// Packed weights [k/2][n] for the dequantisers: box 128 columns x 32 packed rows; for the
+// tensor-memory kernel 64 packed rows with the 128-byte swizzle.
+int gemm_wtmap(const void* w, uint64_t n, uint64_t k, bool tm, CUtensorMap* out) {
   int st = get_encoder();
   if (st != TK_OK) return st;
+  const bool swizzle = tm;
   cuuint64_t dims[2] = {n, k / 2};
   cuuint64_t strides[1] = {n};
-  cuuint32_t box[2] = {(cuuint32_t)kGemmTileCols, (cuuint32_t)(kGemmKStep / 2)};
+  cuuint32_t box[2] = {(cuuint32_t)kGemmTileCols, (cuuint32_t)((tm ? kGemmTmKStep : kGemmKStep) / 2)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode_tiled(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims,
                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                              swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed (%d)", (int)r);
   return TK_OK;
+}
+
+// Scales [k/gs][n] (f16, box 128 columns x 8 groups) and zero points [k/gs][n/2] (u8, box 64 x
+// 8 groups) for the tensor-memory kernel's scale ring.
+int gemm_auxmaps(const uint16_t* s, const uint8_t* z, uint64_t n, uint64_t k, uint64_t gs,
+                 CUtensorMap* sc, CUtensorMap* ze) {
+  int st = get_encoder();
+  if (st != TK_OK) return st;
+  cuuint32_t estr[2] = {1, 1};
+  {
+    cuuint64_t dims[2] = {n, k / gs};
+    cuuint64_t strides[1] = {n * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kGemmTileCols, (cuuint32_t)kGemmAuxGroups};
+    CUresult r = g_encode_tiled(sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(s),
+                                dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", (int)r);
+  }
+  {
+    cuuint64_t dims[2] = {n / 2, k / gs};
+    cuuint64_t strides[1] = {n / 2};
+    cuuint32_t box[2] = {(cuuint32_t)(kGemmTileCols / 2), (cuuint32_t)kGemmAuxGroups};
+    CUresult r = g_encode_tiled(ze, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(z),
+                                dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TK_ERR_CUDA, "cuTensorMapEncodeTiled (zero points) failed (%d)", (int)r);
+  }
+  return TK_OK;
+}
+
+// Weight maps of tile t: packed weights (swizzled for the tensor-memory kernel) and, for that
+// kernel, the scale / zero-point maps.
+int gemm_matrix_maps(GemmMaps& maps, int t, const uint8_t* w, const uint16_t* s, const uint8_t* z,
+                     int n, int k, int gs, int nt) {
+  const bool tm = gemm_use_tm(nt, k);
+  int st = gemm_wtmap(w, n, k, tm, &maps.w[t]);
+  if (st != TK_OK || !tm) return st;
+  return gemm_auxmaps(s, z, n, k, gs, &maps.sc[t], &maps.ze[t]);
 }
 
 // One GEMM launch: colblocks CTA column tiles x token tiles x splits.
 int gemm_run(tk_device* d, const GemmMaps& maps, GemmParams& p, int nt, int colblocks,
              cudaStream_t st) {
-  // a short ring of dequantised tiles, the rest of shared memory for the TMA ring
   const int avail = d->smem_optin - kStaticSmemReserve - 1024;
-  p.a_stages = nt >= 128 ? 2 : 3;
-  p.raw_stage_bytes = gemm_raw_stage_bytes(nt);
-  p.raw_stages = std::min(kGemmMaxRawStages, (avail - p.a_stages * kGemmAStageBytes) / p.raw_stage_bytes);
+  size_t smem = 0;
+  p.tm = gemm_use_tm(nt, p.K) ? 1 : 0;
+  if (p.tm) {
+    // dequantised tiles in tensor memory: shared memory holds the TMA ring and the scale ring
+    p.a_stages = nt >= 128 ? 2 : 3;
+    p.aux_stages = 3;
+    p.raw_stage_bytes = gemm_tm_raw_stage_bytes(nt);
+    p.raw_stages = std::min(kGemmMaxRawStages,
+                            (avail - p.aux_stages * kGemmAuxStageBytes) / p.raw_stage_bytes);
+    smem = 1024 + (size_t)p.raw_stages * p.raw_stage_bytes + (size_t)p.aux_stages * kGemmAuxStageBytes;
+  } else {
+    // a short ring of dequantised tiles, the rest of shared memory for the TMA ring
+    p.a_stages = nt >= 128 ? 2 : 3;
+    p.aux_stages = 0;
+    p.raw_stage_bytes = gemm_raw_stage_bytes(nt);
+    p.raw_stages = std::min(kGemmMaxRawStages, (avail - p.a_stages * kGemmAStageBytes) / p.raw_stage_bytes);
+    smem = 1024 + (size_t)p.a_stages * kGemmAStageBytes + (size_t)p.raw_stages * p.raw_stage_bytes;
+  }
   if (p.raw_stages < 2) return fail(TK_ERR_UNSUPPORTED, "GEMM stages do not fit in shared memory");
   p.err = d->err;
   p.timeout_ns = d->timeout_ns;
-  const size_t smem = 1024 + (size_t)p.a_stages * kGemmAStageBytes +
-                      (size_t)p.raw_stages * p.raw_stage_bytes;
+  p.trace = d->trace;
+  p.trace_ctas = d->sm_count;
+  if (d->trace)
+    TK_CUDA_TRY(cudaMemsetAsync(d->trace, 0, (size_t)d->sm_count * kTraceEvents * 8, st));
   const dim3 grid((unsigned)colblocks, (unsigned)((p.M + nt - 1) / nt), (unsigned)p.splits);
   TK_LAUNCH(d, gemm_launch(nt, maps, p, grid, smem, st));
   return TK_OK;
 }
 
 // K splits so that the grid covers the SMs (each split a whole number of 64-k steps).
-int gemm_splits(tk_device* d, int ctas, int k) {
-  const int steps = k / kGemmKStep;
+int gemm_splits(tk_device* d, int ctas, int k, int nt) {
+  const int steps = k / (gemm_use_tm(nt, k) ? kGemmTmKStep : kGemmKStep);
   return std::max(1, std::min({steps, d->sm_count / ctas, 16}));
 }
 
@@ -518,8 +576,10 @@ int qmatmul_gemm(tk_device* d, const float* x, const uint8_t* w, const uint16_t*
   GemmMaps maps;
   std::memset(&maps, 0, sizeof(maps));
   if ((stt = act_tmap(x16, k, m, nt, &maps.x)) != TK_OK) return stt;
-  if ((stt = gemm_wtmap(w, n, k, &maps.w[0])) != TK_OK) return stt;
+  if ((stt = gemm_matrix_maps(maps, 0, w, s, z, n, k, gs, nt)) != TK_OK) return stt;
   maps.w[1] = maps.w[0];
+  maps.sc[1] = maps.sc[0];
+  maps.ze[1] = maps.ze[0];
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
   p.M = m;
@@ -530,7 +590,7 @@ int qmatmul_gemm(tk_device* d, const float* x, const uint8_t* w, const uint16_t*
   p.scales[0] = p.scales[1] = s;
   p.zeros[0] = p.zeros[1] = z;
   const int colblocks = n / (kGemmTiles * kGemmTileCols);
-  p.splits = gemm_splits(d, colblocks * ((m + nt - 1) / nt), k);
+  p.splits = gemm_splits(d, colblocks * ((m + nt - 1) / nt), k, nt);
   if (p.splits == 1) {
     p.epi = kGemmStore;
     p.out = out;
@@ -545,7 +605,7 @@ int qmatmul_gemm(tk_device* d, const float* x, const uint8_t* w, const uint16_t*
   return TK_OK;
 }
 
-// The INT4 FFN for m >= 16 rows: rmsnorm -> f16, gate/up GEMM with silu(gate) * up in its
+// The INT4 FFN for m >= 16 rows: rmsnorm (written as f16), gate/up GEMM with silu(gate) * up in its
 // epilogue (h in f16 for the down GEMM, and in f32 when asked), down GEMM split over K,
 // reduction (+ residual).
 int ffn_gemm(tk_device* d, const float* x, const float* norm_w, const tk_int4_matrix* gate,
@@ -553,20 +613,21 @@ int ffn_gemm(tk_device* d, const float* x, const float* norm_w, const tk_int4_ma
              int m, int hidden, int inter, int gs, float eps, bool residual, cudaStream_t st) {
   const int nt = gemm_nt(m);
   int stt;
-  if ((stt = scratch_ensure(d, d->g_xn, (size_t)m * hidden * 4)) != TK_OK) return stt;
   if ((stt = scratch_ensure(d, d->g_x16, (size_t)m * hidden * 2)) != TK_OK) return stt;
   if ((stt = scratch_ensure(d, d->g_h16, (size_t)m * inter * 2)) != TK_OK) return stt;
-  float* xn = static_cast<float*>(d->g_xn.ptr);
   __half* x16 = static_cast<__half*>(d->g_x16.ptr);
   __half* h16 = static_cast<__half*>(d->g_h16.ptr);
-  TK_LAUNCH(d, launch_rmsnorm(x, norm_w, xn, m, hidden, eps, st));
-  TK_LAUNCH(d, launch_f32_to_f16(xn, x16, (long long)m * hidden, st));
+  TK_LAUNCH(d, launch_rmsnorm_f16(x, norm_w, x16, m, hidden, eps, st));
   // gate/up: tile 0 = gate, tile 1 = up at the same 128 columns
   GemmMaps ma;
   std::memset(&ma, 0, sizeof(ma));
   if ((stt = act_tmap(x16, hidden, m, nt, &ma.x)) != TK_OK) return stt;
-  if ((stt = gemm_wtmap(gate->w_packed, inter, hidden, &ma.w[0])) != TK_OK) return stt;
-  if ((stt = gemm_wtmap(up->w_packed, inter, hidden, &ma.w[1])) != TK_OK) return stt;
+  if ((stt = gemm_matrix_maps(ma, 0, gate->w_packed, gate->scales, gate->zeros, inter, hidden, gs,
+                              nt)) != TK_OK)
+    return stt;
+  if ((stt = gemm_matrix_maps(ma, 1, up->w_packed, up->scales, up->zeros, inter, hidden, gs, nt)) !=
+      TK_OK)
+    return stt;
   GemmParams a;
   std::memset(&a, 0, sizeof(a));
   a.M = m;
@@ -587,8 +648,12 @@ int ffn_gemm(tk_device* d, const float* x, const float* norm_w, const tk_int4_ma
   GemmMaps mb;
   std::memset(&mb, 0, sizeof(mb));
   if ((stt = act_tmap(h16, inter, m, nt, &mb.x)) != TK_OK) return stt;
-  if ((stt = gemm_wtmap(down->w_packed, hidden, inter, &mb.w[0])) != TK_OK) return stt;
+  if ((stt = gemm_matrix_maps(mb, 0, down->w_packed, down->scales, down->zeros, hidden, inter, gs,
+                              nt)) != TK_OK)
+    return stt;
   mb.w[1] = mb.w[0];
+  mb.sc[1] = mb.sc[0];
+  mb.ze[1] = mb.ze[0];
   GemmParams b;
   std::memset(&b, 0, sizeof(b));
   b.M = m;
@@ -599,7 +664,7 @@ int ffn_gemm(tk_device* d, const float* x, const float* norm_w, const tk_int4_ma
   b.scales[0] = b.scales[1] = down->scales;
   b.zeros[0] = b.zeros[1] = down->zeros;
   const int colblocks = hidden / (kGemmTiles * kGemmTileCols);
-  b.splits = gemm_splits(d, colblocks * ((m + nt - 1) / nt), inter);
+  b.splits = gemm_splits(d, colblocks * ((m + nt - 1) / nt), inter, nt);
   if (b.splits == 1) {
     b.epi = kGemmStore;
     b.out = out;
@@ -684,7 +749,7 @@ void tk_device_destroy(tk_device* d) {
   cudaSetDevice(d->ordinal);
   if (d->stream) cudaStreamSynchronize(d->stream);
   for (auto* b : {&d->frag[0], &d->partials[0], &d->partials[1], &d->counters[0],
-                  &d->counters[1], &d->g_x16, &d->g_xn, &d->g_h16, &d->g_part})
+                  &d->counters[1], &d->g_x16, &d->g_h16, &d->g_part})
     if (b->ptr) cudaFree(b->ptr);
   if (d->sync) cudaFree(d->sync);
   if (d->err) cudaFree(d->err);

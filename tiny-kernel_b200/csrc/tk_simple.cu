@@ -81,6 +81,22 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   for (int i = threadIdx.x; i < dim; i += blockDim.x) out[off + i] = x[off + i] * rms * w[i];
 }
 
+// rmsnorm of one row, written as f16 (the activations of the tensor-core GEMM).
+__global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                   __half* __restrict__ out, int dim, float eps) {
+  __shared__ float red[32];
+  const size_t off = (size_t)blockIdx.x * dim;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float v = x[off + i];
+    ss = fmaf(v, v, ss);
+  }
+  const float tot = block_sum(ss, red);
+  const float rms = rsqrtf(tot / (float)dim + eps);
+  for (int i = threadIdx.x; i < dim; i += blockDim.x)
+    out[off + i] = __float2half_rn(x[off + i] * rms * w[i]);
+}
+
 __global__ void fused_rmsnorm_rope_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                           const float* __restrict__ cosc,
                                           const float* __restrict__ sinc, float* __restrict__ out,
@@ -176,6 +192,12 @@ cudaError_t launch_dequant_int4(const uint8_t* w, const uint16_t* s, const uint8
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int rows, int dim,
                            float eps, cudaStream_t st) {
   rmsnorm_kernel<<<rows, 256, 0, st>>>(x, w, out, dim, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_f16(const float* x, const float* w, __half* out, int rows, int dim,
+                               float eps, cudaStream_t st) {
+  rmsnorm_f16_kernel<<<rows, 512, 0, st>>>(x, w, out, dim, eps);
   return cudaGetLastError();
 }
 
