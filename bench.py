@@ -49,6 +49,12 @@ def ffn_bytes(m, hidden, inter, gs):
     return w + m * hidden * 4 + hidden * 4 + m * hidden * 4
 
 
+def ffn_weight_bytes(hidden, inter, gs):
+    """Packed weights + scales + zero points of the three matrices."""
+    from tiny_kernel.data import int4_matrix_bytes
+    return 2 * int4_matrix_bytes(hidden, inter, gs) + int4_matrix_bytes(inter, hidden, gs)
+
+
 def ffn_flops(m, hidden, inter):
     """Multiply-adds of the three projections, 2 FLOPs each."""
     return 2 * m * 3 * hidden * inter
@@ -158,6 +164,7 @@ def run_reference(args, world, rank):
         "ms_per_step": round(dt / steps * 1e3 * L, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "tokens_per_s": round(m * steps / dt / L, 2),
+        "ref_style_gibs": round(ffn_weight_bytes(hidden, inter, GS) * steps / dt / 2**30, 3),
         "config": {"workload": workload_name(name, m, L),
                    "hidden": hidden, "inter": inter, "group_size": GS, "batch": m, "layers": L,
                    "parallelism": "host CPU", "steps_requested": args.steps,
@@ -441,6 +448,9 @@ def main():
             "scaling": "strong", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
             "tokens_per_s": round(m * steps_timed / (ms / 1e3), 1),
+            # the reference bench's own figure (src/bench.zig:259-263): weight bytes only, in GiB/s
+            "ref_style_gibs": round(L * ffn_weight_bytes(hidden, inter_full, GS) * steps_timed /
+                                    (ms / 1e3) / 2**30, 2),
             "pct_of_peak": round(100.0 * achieved / peak, 2),
             "pct_of_8tbs": round(100.0 * achieved / 8000.0, 2),
             "config": {

@@ -164,6 +164,35 @@ int tk_int4_ffn_async(tk_device *dev, const float *x, const float *norm_weight,
                       uint32_t hidden, uint32_t inter, uint32_t group_size, float eps,
                       uint32_t flags, void *stream);
 
+/* ---- tensor parallelism -------------------------------------------------------------
+ * The additive tensor-parallel FFN (no counterpart in the reference, which runs on one Apple GPU).
+ * One process (or thread) per GPU.  Rank r holds the shard: gate/up columns and down K-rows
+ * [r*I/tp, (r+1)*I/tp) of the full FFN (inter_shard = I/tp); x, the norm weight and out are full
+ * size on every rank.  tk_int4_ffn_tp computes the shard's partial output and sums it across
+ * the ranks in place (NCCL all-reduce, f32, on the device's stream or the given one); with
+ * TK_FFN_RESIDUAL the residual is added once (by rank 0) before the sum.  NCCL (libnccl.so.2) is
+ * loaded at the first tk_tp_* call; TK_ERR_NCCL when it is missing or a NCCL call fails.
+ * Every rank must make the same tk_tp_* calls in the same order. */
+#define TK_TP_UNIQUE_ID_BYTES 128
+typedef struct tk_tp tk_tp;
+/* Rank 0 creates the group's id and hands it to the other ranks (any channel). */
+int tk_tp_unique_id(uint8_t id[TK_TP_UNIQUE_ID_BYTES]);
+/* Joins the group (blocks until all nranks have joined). */
+int tk_tp_create(tk_device *dev, int nranks, int rank, const uint8_t id[TK_TP_UNIQUE_ID_BYTES],
+                 tk_tp **out);
+void tk_tp_destroy(tk_tp *tp);
+int tk_int4_ffn_tp(tk_tp *tp, const float *x, const float *norm_weight,
+                   const tk_int4_matrix *gate, const tk_int4_matrix *up,
+                   const tk_int4_matrix *down, float *out, uint32_t m, uint32_t hidden,
+                   uint32_t inter_shard, uint32_t group_size, float eps, uint32_t flags);
+int tk_int4_ffn_tp_async(tk_tp *tp, const float *x, const float *norm_weight,
+                         const tk_int4_matrix *gate, const tk_int4_matrix *up,
+                         const tk_int4_matrix *down, float *out, uint32_t m, uint32_t hidden,
+                         uint32_t inter_shard, uint32_t group_size, float eps, uint32_t flags,
+                         void *stream);
+/* In-place sum of an f32 device buffer across the group (the FFN's exchange step). */
+int tk_tp_allreduce_sum_f32(tk_tp *tp, float *buf, size_t count, void *stream);
+
 /* Test hook (bit-exactness of dequantisation, shaders.zig:474-495):
  * out f32 [k][n] = float(scale[g][n]) * (float(q[k][n]) - float(zero[g][n])). */
 int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *scales,

@@ -56,3 +56,22 @@ def test_null_arguments_rejected():
     assert L.tk_device_create(0, None) == _lib.TK_ERR_ARG
     assert L.tk_qmatmul_int4(None, None, None, None, None, None, 1, 64, 32, 8) == _lib.TK_ERR_ARG
     assert b"NULL" in L.tk_last_error_string()
+
+
+def test_tp_group_id_and_argument_checks():
+    """tk_tp_*: the group id comes from NCCL (loaded at first use, no GPU needed for the id);
+    malformed calls are refused before any NCCL or CUDA work."""
+    import ctypes as C
+
+    from tiny_kernel import tp
+    L = _lib.lib()
+    a, b = tp.unique_id(), tp.unique_id()
+    assert len(a) == _lib.TK_TP_UNIQUE_ID_BYTES and a != b
+    idbuf = (C.c_uint8 * _lib.TK_TP_UNIQUE_ID_BYTES).from_buffer_copy(a)
+    h = C.c_void_p()
+    assert L.tk_tp_create(None, 2, 0, idbuf, C.byref(h)) == _lib.TK_ERR_ARG
+    assert L.tk_tp_unique_id(None) == _lib.TK_ERR_ARG
+    assert L.tk_int4_ffn_tp(None, None, None, None, None, None, None, 1, 128, 128, 64, 1e-5, 0) \
+        == _lib.TK_ERR_ARG
+    assert L.tk_tp_allreduce_sum_f32(None, None, 0, None) == _lib.TK_ERR_ARG
+    L.tk_tp_destroy(None)  # no-op

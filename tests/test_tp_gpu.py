@@ -1,4 +1,5 @@
-"""GPU parity of the tensor-parallel INT4 FFN: one process per GPU, NCCL all-reduce.
+"""GPU parity of the tensor-parallel INT4 FFN: one process per GPU, NCCL all-reduce, both through
+torch.distributed and through the library's own C ABI group (tk_tp_*).
 
 Rank r runs the engine on its shard (gate/up columns and down rows [r*I/tp, (r+1)*I/tp),
 tiny_kernel.tp.shard_ffn); the f32 partial outputs are summed by an NCCL all-reduce over
@@ -88,6 +89,69 @@ def test_tp_ffn_vs_oracle(torch_cuda, tmp_path, world):
              (2, 256, 512, 64, True)]
     out = tmp_path / "errs.npy"
     mp.start_processes(_rank, args=(world, _free_port(), cases, str(out)), nprocs=world,
+                       join=True, start_method="spawn")
+    errs = np.load(out)
+    assert len(errs) == len(cases)
+    assert np.all(errs <= TOL), errs
+
+
+def _rank_native(rank, world, uid, cases, result_path):
+    """One rank of the C-ABI path: tk_tp_create + tk_int4_ffn_tp (NCCL inside libtkcuda)."""
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "tiny-kernel_b200"), os.path.join(root, "oracle")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import torch
+
+    import oracle
+    import tiny_kernel as tk
+    from tiny_kernel import data
+    from tiny_kernel.tp import Group, shard_ffn
+
+    torch.cuda.set_device(rank)
+    dev = tk.init(rank)
+    group = Group(dev, world, rank, uid)
+    errs = []
+    try:
+        for (m, hidden, inter, gs, residual) in cases:
+            W = data.make_ffn(43, hidden, inter, gs)
+            x = data.make_x(44, f"tpn{m}", m, hidden)
+            S = shard_ffn(W, rank, world)
+
+            def d(a):
+                a = np.ascontiguousarray(a)
+                return torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else a).cuda()
+
+            out = torch.empty((m, hidden), dtype=torch.float32, device="cuda")
+            group.int4_ffn(d(x), d(S.norm_w), [d(a) for a in (S.gate.w, S.gate.s, S.gate.z)],
+                           [d(a) for a in (S.up.w, S.up.s, S.up.z)],
+                           [d(a) for a in (S.down.w, S.down.s, S.down.z)], out, m, hidden,
+                           S.inter, gs, eps=EPS, residual=residual)
+            if rank == 0:
+                ref = oracle.ffn_f64(x, W.norm_w, W.gate, W.up, W.down, EPS, residual=residual)
+                errs.append(float(oracle.normwise_err(out.cpu().numpy(), ref)))
+    finally:
+        group.close()
+        dev.deinit()
+    if rank == 0:
+        np.save(result_path, np.array(errs))
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_ffn_native_group_vs_oracle(torch_cuda, tmp_path, world):
+    if torch_cuda.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    from tiny_kernel.tp import unique_id
+    cases = [(1, 4096, 14336, 64, False),   # config 1, TP2
+             (1, 1024, 2048, 64, True),     # residual added once (rank 0)
+             (16, 1024, 2048, 64, False)]   # batch 16: the tcgen05 GEMM on each shard
+    out = tmp_path / "errs_native.npy"
+    mp.start_processes(_rank_native, args=(world, unique_id(), cases, str(out)), nprocs=world,
                        join=True, start_method="spawn")
     errs = np.load(out)
     assert len(errs) == len(cases)

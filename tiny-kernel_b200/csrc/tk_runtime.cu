@@ -8,6 +8,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cstdarg>
@@ -1214,3 +1216,137 @@ extern "C" int tk_qmatmul_int4_noalloc(const float* x, const uint8_t* w, const u
   if (h != 0) return fail(TK_ERR_TIMEOUT, "device-side bounded wait gave up (error bits 0x%x)", h);
   return TK_OK;
 }
+
+// ---- tensor parallelism: NCCL resolved at first use ----------------------------------------
+
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+std::once_flag g_nccl_once;
+NcclApi g_nccl;
+
+int nccl_api(const NcclApi** out) {
+  std::call_once(g_nccl_once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    g_nccl.get_unique_id = reinterpret_cast<decltype(g_nccl.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    g_nccl.comm_init_rank = reinterpret_cast<decltype(g_nccl.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    g_nccl.all_reduce = reinterpret_cast<decltype(g_nccl.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    g_nccl.error_string = reinterpret_cast<decltype(g_nccl.error_string)>(dlsym(h, "ncclGetErrorString"));
+    g_nccl.ok = g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.all_reduce &&
+                g_nccl.comm_destroy && g_nccl.error_string;
+  });
+  if (!g_nccl.ok) return fail(TK_ERR_NCCL, "NCCL (libnccl.so.2) could not be loaded");
+  *out = &g_nccl;
+  return TK_OK;
+}
+
+int nccl_fail(const NcclApi* n, const char* what, ncclResult_t r) {
+  return fail(TK_ERR_NCCL, "%s failed: %s", what, n->error_string(r));
+}
+
+static_assert(sizeof(ncclUniqueId) == TK_TP_UNIQUE_ID_BYTES, "NCCL unique id size");
+
+}  // namespace
+
+struct tk_tp {
+  tk_device* dev = nullptr;
+  ncclComm_t comm = nullptr;
+  int nranks = 0, rank = 0;
+};
+
+extern "C" {
+
+int tk_tp_unique_id(uint8_t id[TK_TP_UNIQUE_ID_BYTES]) {
+  if (!id) return fail(TK_ERR_ARG, "id is NULL");
+  const NcclApi* n = nullptr;
+  int st = nccl_api(&n);
+  if (st != TK_OK) return st;
+  ncclUniqueId u;
+  ncclResult_t r = n->get_unique_id(&u);
+  if (r != ncclSuccess) return nccl_fail(n, "ncclGetUniqueId", r);
+  std::memcpy(id, &u, sizeof(u));
+  return TK_OK;
+}
+
+int tk_tp_create(tk_device* d, int nranks, int rank, const uint8_t id[TK_TP_UNIQUE_ID_BYTES],
+                 tk_tp** out) {
+  if (!d || !id || !out) return fail(TK_ERR_ARG, "NULL argument");
+  *out = nullptr;
+  if (nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(TK_ERR_ARG, "rank %d of %d is out of range", rank, nranks);
+  const NcclApi* n = nullptr;
+  int st = nccl_api(&n);
+  if (st != TK_OK) return st;
+  if ((st = set_device(d)) != TK_OK) return st;
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof(u));
+  tk_tp* tp = new tk_tp();
+  tp->dev = d;
+  tp->nranks = nranks;
+  tp->rank = rank;
+  ncclResult_t r = n->comm_init_rank(&tp->comm, nranks, u, rank);
+  if (r != ncclSuccess) {
+    delete tp;
+    return nccl_fail(n, "ncclCommInitRank", r);
+  }
+  *out = tp;
+  return TK_OK;
+}
+
+void tk_tp_destroy(tk_tp* tp) {
+  if (!tp) return;
+  const NcclApi* n = nullptr;
+  if (tp->comm && nccl_api(&n) == TK_OK) {
+    cudaSetDevice(tp->dev->ordinal);
+    n->comm_destroy(tp->comm);
+  }
+  delete tp;
+}
+
+int tk_tp_allreduce_sum_f32(tk_tp* tp, float* buf, size_t count, void* stream) {
+  if (!tp || (!buf && count)) return fail(TK_ERR_ARG, "NULL argument");
+  const NcclApi* n = nullptr;
+  int st = nccl_api(&n);
+  if (st != TK_OK) return st;
+  if ((st = set_device(tp->dev)) != TK_OK) return st;
+  ncclResult_t r = n->all_reduce(buf, buf, count, ncclFloat32, ncclSum, tp->comm,
+                                 pick_stream(tp->dev, stream));
+  if (r != ncclSuccess) return nccl_fail(n, "ncclAllReduce", r);
+  return TK_OK;
+}
+
+int tk_int4_ffn_tp_async(tk_tp* tp, const float* x, const float* norm_w, const tk_int4_matrix* gate,
+                         const tk_int4_matrix* up, const tk_int4_matrix* down, float* out,
+                         uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs, float eps,
+                         uint32_t flags, void* stream) {
+  if (!tp) return fail(TK_ERR_ARG, "tp is NULL");
+  // the residual is added once, by rank 0, before the sum
+  const uint32_t f = tp->rank == 0 ? flags : (flags & ~TK_FFN_RESIDUAL);
+  int st = tk_int4_ffn_async(tp->dev, x, norm_w, gate, up, down, out, nullptr, m, hidden, inter, gs,
+                             eps, f, stream);
+  if (st != TK_OK) return st;
+  return tk_tp_allreduce_sum_f32(tp, out, (size_t)m * hidden, stream);
+}
+
+int tk_int4_ffn_tp(tk_tp* tp, const float* x, const float* norm_w, const tk_int4_matrix* gate,
+                   const tk_int4_matrix* up, const tk_int4_matrix* down, float* out, uint32_t m,
+                   uint32_t hidden, uint32_t inter, uint32_t gs, float eps, uint32_t flags) {
+  int st = tk_int4_ffn_tp_async(tp, x, norm_w, gate, up, down, out, m, hidden, inter, gs, eps,
+                                flags, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(tp->dev, tp->dev->stream);
+}
+
+}  // extern "C"

@@ -26,6 +26,7 @@ TK_MEM_SHARED = 1
 TK_MEM_HOST = 2
 
 TK_FFN_RESIDUAL = 1
+TK_TP_UNIQUE_ID_BYTES = 128
 
 vp = C.c_void_p
 u32 = C.c_uint32
@@ -72,6 +73,15 @@ SIGNATURES = {
                                 C.POINTER(Int4MatrixC), vp, vp, u32, u32, u32, u32, f32, u32,
                                 vp]),
     "tk_dequant_int4": (i32, [vp, vp, vp, vp, vp, u32, u32, u32]),
+    "tk_tp_unique_id": (i32, [vp]),
+    "tk_tp_create": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),
+    "tk_tp_destroy": (None, [vp]),
+    "tk_tp_allreduce_sum_f32": (i32, [vp, vp, C.c_size_t, vp]),
+    "tk_int4_ffn_tp": (i32, [vp, vp, vp, C.POINTER(Int4MatrixC), C.POINTER(Int4MatrixC),
+                             C.POINTER(Int4MatrixC), vp, u32, u32, u32, u32, f32, u32]),
+    "tk_int4_ffn_tp_async": (i32, [vp, vp, vp, C.POINTER(Int4MatrixC), C.POINTER(Int4MatrixC),
+                                   C.POINTER(Int4MatrixC), vp, u32, u32, u32, u32, f32, u32,
+                                   vp]),
     "tk_device_trace_enable": (i32, [vp, i32]),
     "tk_device_trace_read": (i32, [vp, vp, C.c_size_t, C.POINTER(C.c_size_t)]),
 }

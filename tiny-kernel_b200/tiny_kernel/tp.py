@@ -10,8 +10,11 @@ The residual (x + FFN(x), src/model/llama.zig:220-231) is added once, after the 
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import numpy as np
 
+from . import _lib
 from .data import FFNWeights, Int4Matrix
 
 
@@ -41,3 +44,60 @@ def shard_ffn(W: FFNWeights, rank: int, world: int) -> FFNWeights:
                       np.ascontiguousarray(D.s[c0 // gs:c1 // gs]),
                       np.ascontiguousarray(D.z[c0 // gs:c1 // gs]), c1 - c0, D.N, gs)
     return FFNWeights(W.norm_w, cols(W.gate), cols(W.up), down, W.hidden, c1 - c0, gs)
+
+
+def unique_id() -> bytes:
+    """A new group id (tk_tp_unique_id); rank 0 makes it and hands it to the other ranks."""
+    buf = (C.c_uint8 * _lib.TK_TP_UNIQUE_ID_BYTES)()
+    _lib.check(_lib.lib().tk_tp_unique_id(buf))
+    return bytes(buf)
+
+
+class Group:
+    """A tensor-parallel group through the C ABI (tk_tp_*, NCCL inside libtkcuda): the native
+    path a non-Python caller takes, with no torch.distributed involved."""
+
+    def __init__(self, device, nranks: int, rank: int, uid: bytes):
+        if len(uid) != _lib.TK_TP_UNIQUE_ID_BYTES:
+            raise ValueError("group id must be 128 bytes")
+        self.rank, self.nranks = rank, nranks
+        idbuf = (C.c_uint8 * _lib.TK_TP_UNIQUE_ID_BYTES).from_buffer_copy(uid)
+        h = C.c_void_p()
+        _lib.check(_lib.lib().tk_tp_create(device.handle, nranks, rank, idbuf, C.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            _lib.lib().tk_tp_destroy(self.handle)
+            self.handle = None
+
+    def allreduce_sum(self, buf, count: int, stream=None):
+        _lib.check(_lib.lib().tk_tp_allreduce_sum_f32(self.handle, _ptr(buf), int(count), stream))
+
+    def int4_ffn(self, x, norm_weight, gate, up, down, out, m, hidden, inter_shard, group_size,
+                 eps=1e-5, residual=False, stream=None, sync=True):
+        """tk_int4_ffn_tp: this rank's shard, then the in-place sum over the group."""
+        g, u, d = (_matrix(a) for a in (gate, up, down))
+        flags = _lib.TK_FFN_RESIDUAL if residual else 0
+        L = _lib.lib()
+        if sync and stream is None:
+            st = L.tk_int4_ffn_tp(self.handle, _ptr(x), _ptr(norm_weight), C.byref(g), C.byref(u),
+                                  C.byref(d), _ptr(out), int(m), int(hidden), int(inter_shard),
+                                  int(group_size), float(eps), flags)
+        else:
+            st = L.tk_int4_ffn_tp_async(self.handle, _ptr(x), _ptr(norm_weight), C.byref(g),
+                                        C.byref(u), C.byref(d), _ptr(out), int(m), int(hidden),
+                                        int(inter_shard), int(group_size), float(eps), flags,
+                                        stream)
+        _lib.check(st)
+
+
+def _ptr(v) -> int:
+    return v if isinstance(v, int) else v.data_ptr()
+
+
+def _matrix(a):
+    if isinstance(a, _lib.Int4MatrixC):
+        return a
+    w, s, z = a
+    return _lib.Int4MatrixC(_ptr(w), _ptr(s), _ptr(z))
