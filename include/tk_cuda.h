@@ -193,6 +193,21 @@ int tk_int4_ffn_tp_async(tk_tp *tp, const float *x, const float *norm_weight,
 /* In-place sum of an f32 device buffer across the group (the FFN's exchange step). */
 int tk_tp_allreduce_sum_f32(tk_tp *tp, float *buf, size_t count, void *stream);
 
+/* ---- fp32 matvec ---------------------------------------------------------------------
+ * Replaces Matvec.forward(x, W, out, K, N) (src/kernels/fused.zig:62-89, shaders.zig:184-226):
+ * out[n] = sum_k W[n*K + k] * x[k], W f32 row-major [N][K] (out_dim, in_dim).  Generalised: any
+ * K (the shader stages x in a 4096-float threadgroup array).  fp32 accumulation in a different
+ * order than the shader's sequential one. */
+int tk_matvec(tk_device *dev, const float *x, const float *W, float *out, uint32_t K, uint32_t N);
+int tk_matvec_async(tk_device *dev, const float *x, const float *W, float *out, uint32_t K,
+                    uint32_t N, void *stream);
+/* Replaces MatvecDual.forward(x, W1, W2, out1, out2, K, N) (fused.zig:102-133,
+ * shaders.zig:228-266): two matvecs sharing x, one pass. */
+int tk_matvec_dual(tk_device *dev, const float *x, const float *W1, const float *W2,
+                   float *out1, float *out2, uint32_t K, uint32_t N);
+int tk_matvec_dual_async(tk_device *dev, const float *x, const float *W1, const float *W2,
+                         float *out1, float *out2, uint32_t K, uint32_t N, void *stream);
+
 /* Test hook (bit-exactness of dequantisation, shaders.zig:474-495):
  * out f32 [k][n] = float(scale[g][n]) * (float(q[k][n]) - float(zero[g][n])). */
 int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *scales,

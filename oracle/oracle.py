@@ -109,6 +109,27 @@ def ffn_f64(x, norm_w, gate, up, down, eps: float, residual: bool = False,
     return (y, h) if return_h else y
 
 
+def matvec_f64(x, W, K: int, N: int) -> np.ndarray:
+    """Matvec (src/kernels/shaders.zig:184-226): out[n] = sum_k W[n*K + k] * x[k], W row-major
+    [N][K]; computed in f64."""
+    Wm = np.asarray(W, dtype=np.float64).reshape(N, K)
+    return Wm @ np.asarray(x, dtype=np.float64).reshape(K)
+
+
+def matvec_f32_sequential(x, W, K: int, N: int) -> np.ndarray:
+    """The shader's own f32 order (shaders.zig:211-215): acc += x[k] * W[n*K + k] for k = 0..K-1.
+    Pure-Python loop: small cases only."""
+    Wm = np.asarray(W, dtype=np.float32).reshape(N, K)
+    xs = np.asarray(x, dtype=np.float32).reshape(K)
+    out = np.zeros(N, dtype=np.float32)
+    for n in range(N):
+        acc = np.float32(0.0)
+        for k in range(K):
+            acc = np.float32(acc + np.float32(xs[k] * Wm[n, k]))
+        out[n] = acc
+    return out
+
+
 def normwise_err(y, ref) -> float:
     """max_i |y_i - ref_i| / max_i |ref_i| (the path's error metric)."""
     y = np.asarray(y, dtype=np.float64)

@@ -115,3 +115,16 @@ def test_oracle_catches_a_planted_layout_mistake():
     swapped = ((M.w >> 4) | (M.w << 4)).astype(np.uint8)
     bad = oracle.qmatmul_f64(x, swapped, M.s, M.z, 128, 64, 32)
     assert oracle.normwise_err(bad, good) > 1e-2
+
+
+def test_matvec_oracle_matches_shader_order():
+    """The f64 Matvec oracle against the shader's own sequential f32 loop (shaders.zig:211-215)
+    on a small case: the two differ only by f32 rounding."""
+    rng = np.random.default_rng(5)
+    K, N = 33, 7
+    x = rng.standard_normal(K).astype(np.float32)
+    W = rng.standard_normal((N, K)).astype(np.float32)
+    y64 = oracle.matvec_f64(x, W, K, N)
+    y32 = oracle.matvec_f32_sequential(x, W, K, N)
+    assert np.allclose(y64, W.astype(np.float64) @ x.astype(np.float64))
+    assert oracle.normwise_err(y32, y64) < 1e-6

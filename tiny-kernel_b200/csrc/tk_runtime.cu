@@ -859,6 +859,37 @@ int tk_buffer_download(tk_device* d, void* dst, const void* src, size_t bytes) {
   return TK_OK;
 }
 
+int tk_matvec_dual_async(tk_device* d, const float* x, const float* W1, const float* W2, float* out1,
+                         float* out2, uint32_t K, uint32_t N, void* stream) {
+  if (!d || !x || !W1 || !out1) return fail(TK_ERR_ARG, "NULL argument");
+  if ((W2 == nullptr) != (out2 == nullptr)) return fail(TK_ERR_ARG, "W2 and out2 go together");
+  if (K == 0 || N == 0) return fail(TK_ERR_ARG, "K and N must be positive");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_LAUNCH(d, launch_matvec_f32(x, W1, W2, out1, out2, (int)K, (int)N, d->sm_count,
+                                 pick_stream(d, stream)));
+  return TK_OK;
+}
+
+int tk_matvec_dual(tk_device* d, const float* x, const float* W1, const float* W2, float* out1,
+                   float* out2, uint32_t K, uint32_t N) {
+  if (!W2 || !out2) return fail(TK_ERR_ARG, "NULL argument");
+  int st = tk_matvec_dual_async(d, x, W1, W2, out1, out2, K, N, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
+int tk_matvec_async(tk_device* d, const float* x, const float* W, float* out, uint32_t K,
+                    uint32_t N, void* stream) {
+  return tk_matvec_dual_async(d, x, W, nullptr, out, nullptr, K, N, stream);
+}
+
+int tk_matvec(tk_device* d, const float* x, const float* W, float* out, uint32_t K, uint32_t N) {
+  int st = tk_matvec_async(d, x, W, out, K, N, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
   if (m == 0 || k == 0 || n == 0 || gs == 0 || gs % 8 || k % gs || n % 2) return -1;
   if (!engine_shape(k, n, gs)) return 0;

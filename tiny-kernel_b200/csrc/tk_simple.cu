@@ -9,6 +9,9 @@
 //    812-824; one CTA per row for the reductions.
 #include <cuda_fp16.h>
 
+#include <algorithm>
+#include <cstdint>
+
 #include "tk_internal.h"
 
 namespace tk {
@@ -79,6 +82,86 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   const float tot = block_sum(ss, red);
   const float rms = rsqrtf(tot / (float)dim + eps);
   for (int i = threadIdx.x; i < dim; i += blockDim.x) out[off + i] = x[off + i] * rms * w[i];
+}
+
+// fp32 matvec, W [N][K] row-major (src/kernels/shaders.zig:184-266): out[n] = sum_k W[n][k] x[k].
+// One warp per row (the NMAT matrices' rows share the x loads), float4 streams of each row with
+// four independent partial sums per lane, a butterfly sum at the end.  x is re-read from L1.
+// vec: K % 4 == 0 and 16-byte aligned rows; otherwise scalar loads.
+template <int NMAT>
+__global__ void __launch_bounds__(256) matvec_f32_kernel(const float* __restrict__ x,
+                                                         const float* __restrict__ W0,
+                                                         const float* __restrict__ W1,
+                                                         float* __restrict__ out0,
+                                                         float* __restrict__ out1, int K, int N,
+                                                         int vec) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < N; n += warps) {
+    float acc[NMAT][4];
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
+    const float* r0 = W0 + (size_t)n * K;
+    const float* r1 = NMAT > 1 ? W1 + (size_t)n * K : nullptr;
+    if (vec) {
+      const float4* x4 = reinterpret_cast<const float4*>(x);
+      const float4* a4 = reinterpret_cast<const float4*>(r0);
+      const float4* b4 = reinterpret_cast<const float4*>(r1);
+      const int K4 = K >> 2;
+      int k = lane;
+      // four float4 per lane per iteration (2 KB of each row in flight per warp)
+      constexpr int U = 4;
+      for (; k + 32 * (U - 1) < K4; k += 32 * U) {
+        float4 xa[U], wa[U], va[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          xa[u] = __ldg(x4 + k + 32 * u);
+          wa[u] = __ldcs(a4 + k + 32 * u);
+          if (NMAT > 1) va[u] = __ldcs(b4 + k + 32 * u);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          acc[0][0] = fmaf(wa[u].x, xa[u].x, acc[0][0]);
+          acc[0][1] = fmaf(wa[u].y, xa[u].y, acc[0][1]);
+          acc[0][2] = fmaf(wa[u].z, xa[u].z, acc[0][2]);
+          acc[0][3] = fmaf(wa[u].w, xa[u].w, acc[0][3]);
+          if (NMAT > 1) {
+            acc[NMAT - 1][0] = fmaf(va[u].x, xa[u].x, acc[NMAT - 1][0]);
+            acc[NMAT - 1][1] = fmaf(va[u].y, xa[u].y, acc[NMAT - 1][1]);
+            acc[NMAT - 1][2] = fmaf(va[u].z, xa[u].z, acc[NMAT - 1][2]);
+            acc[NMAT - 1][3] = fmaf(va[u].w, xa[u].w, acc[NMAT - 1][3]);
+          }
+        }
+      }
+      for (; k < K4; k += 32) {
+        const float4 xa = __ldg(x4 + k);
+        const float4 wa = __ldcs(a4 + k);
+        acc[0][0] = fmaf(wa.x, xa.x, acc[0][0]);
+        acc[0][1] = fmaf(wa.y, xa.y, acc[0][1]);
+        acc[0][2] = fmaf(wa.z, xa.z, acc[0][2]);
+        acc[0][3] = fmaf(wa.w, xa.w, acc[0][3]);
+        if (NMAT > 1) {
+          const float4 v1 = __ldcs(b4 + k);
+          acc[NMAT - 1][0] = fmaf(v1.x, xa.x, acc[NMAT - 1][0]);
+          acc[NMAT - 1][1] = fmaf(v1.y, xa.y, acc[NMAT - 1][1]);
+          acc[NMAT - 1][2] = fmaf(v1.z, xa.z, acc[NMAT - 1][2]);
+          acc[NMAT - 1][3] = fmaf(v1.w, xa.w, acc[NMAT - 1][3]);
+        }
+      }
+    } else {
+      for (int k = lane; k < K; k += 32) {
+        const float xv = __ldg(x + k);
+        acc[0][k & 3] = fmaf(r0[k], xv, acc[0][k & 3]);
+        if (NMAT > 1) acc[NMAT - 1][k & 3] = fmaf(r1[k], xv, acc[NMAT - 1][k & 3]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+      float v = (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]);
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) (m == 0 ? out0 : out1)[n] = v;
+    }
+  }
 }
 
 // rmsnorm of one row, written as f16 (the activations of the tensor-core GEMM).
@@ -192,6 +275,19 @@ cudaError_t launch_dequant_int4(const uint8_t* w, const uint16_t* s, const uint8
 cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int rows, int dim,
                            float eps, cudaStream_t st) {
   rmsnorm_kernel<<<rows, 256, 0, st>>>(x, w, out, dim, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_matvec_f32(const float* x, const float* W0, const float* W1, float* out0,
+                              float* out1, int K, int N, int sm_count, cudaStream_t st) {
+  const int vec = (K % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W0) |
+                                    reinterpret_cast<uintptr_t>(W1)) % 16 == 0);
+  // 8 warps (rows) per block; enough blocks to cover the SMs a few times, rows strided
+  const int blocks = std::max(1, std::min((N + 7) / 8, sm_count * 8));
+  if (W1)
+    matvec_f32_kernel<2><<<blocks, 256, 0, st>>>(x, W0, W1, out0, out1, K, N, vec);
+  else
+    matvec_f32_kernel<1><<<blocks, 256, 0, st>>>(x, W0, nullptr, out0, nullptr, K, N, vec);
   return cudaGetLastError();
 }
 

@@ -73,6 +73,10 @@ SIGNATURES = {
                                 C.POINTER(Int4MatrixC), vp, vp, u32, u32, u32, u32, f32, u32,
                                 vp]),
     "tk_dequant_int4": (i32, [vp, vp, vp, vp, vp, u32, u32, u32]),
+    "tk_matvec": (i32, [vp, vp, vp, vp, u32, u32]),
+    "tk_matvec_async": (i32, [vp, vp, vp, vp, u32, u32, vp]),
+    "tk_matvec_dual": (i32, [vp, vp, vp, vp, vp, vp, u32, u32]),
+    "tk_matvec_dual_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, vp]),
     "tk_tp_unique_id": (i32, [vp]),
     "tk_tp_create": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),
     "tk_tp_destroy": (None, [vp]),

@@ -19,6 +19,34 @@ class FusedRMSNormRoPE:
                                x.count // int(dim), dim, head_dim, pos, eps)
 
 
+class Matvec:
+    """Matvec (fused.zig:53-89): out = W x, W f32 [N][K]; K of any size here."""
+
+    def __init__(self, device):
+        self.device = device
+
+    @classmethod
+    def init(cls, device) -> "Matvec":
+        return cls(device)
+
+    def forward(self, x, W, out, K, N):
+        ops.matvec(self.device, x, W, out, K, N)
+
+
+class MatvecDual:
+    """MatvecDual (fused.zig:91-133): out1 = W1 x, out2 = W2 x in one pass over x."""
+
+    def __init__(self, device):
+        self.device = device
+
+    @classmethod
+    def init(cls, device) -> "MatvecDual":
+        return cls(device)
+
+    def forward(self, x, W1, W2, out1, out2, K, N):
+        ops.matvec_dual(self.device, x, W1, W2, out1, out2, K, N)
+
+
 class FusedSiluMul:
     """FusedSiluMul (fused.zig:178-213): out = silu(gate) * up, n = gate.count."""
 

@@ -95,6 +95,30 @@ def silu_mul(device, gate, up, out, n, stream=None, sync=True):
             check(L.tk_device_synchronize(_dev(device)))
 
 
+def matvec(device, x, W, out, K, N, stream=None, sync=True):
+    """out[n] = sum_k W[n][k] x[k], W f32 [N][K] (Matvec, fused.zig:53-89)."""
+    L = _lib.lib()
+    args = (_dev(device), _ptr(x), _ptr(W), _ptr(out), int(K), int(N))
+    if sync and stream is None:
+        check(L.tk_matvec(*args))
+    else:
+        check(L.tk_matvec_async(*args, stream))
+        if sync:
+            check(L.tk_device_synchronize(_dev(device)))
+
+
+def matvec_dual(device, x, W1, W2, out1, out2, K, N, stream=None, sync=True):
+    """Two matvecs sharing x (MatvecDual, fused.zig:91-133)."""
+    L = _lib.lib()
+    args = (_dev(device), _ptr(x), _ptr(W1), _ptr(W2), _ptr(out1), _ptr(out2), int(K), int(N))
+    if sync and stream is None:
+        check(L.tk_matvec_dual(*args))
+    else:
+        check(L.tk_matvec_dual_async(*args, stream))
+        if sync:
+            check(L.tk_device_synchronize(_dev(device)))
+
+
 def dequant_int4(device, w_packed, scales, zeros, out, k, n, group_size):
     check(_lib.lib().tk_dequant_int4(_dev(device), _ptr(w_packed), _ptr(scales), _ptr(zeros),
                                      _ptr(out), int(k), int(n), int(group_size)))
