@@ -208,6 +208,20 @@ int tk_matvec_dual(tk_device *dev, const float *x, const float *W1, const float 
 int tk_matvec_dual_async(tk_device *dev, const float *x, const float *W1, const float *W2,
                          float *out1, float *out2, uint32_t K, uint32_t N, void *stream);
 
+/* ---- GGUF Q4_0 -> qmatmul_int4 layout ---------------------------------------------------
+ * The on-disk format on the path's input side (src/model/gguf.zig, src/model/llama.zig:341-353,
+ * where the reference decodes Q4_0 to f32 instead).  blocks: n_rows x (k/32) Q4_0 blocks of 18
+ * bytes (f16 d, 16 bytes of nibbles), row n = output feature n (the f32 Matvec's [N][K]).  Writes
+ * w_packed [k/2][n_rows], scales [k/32][n_rows] (= d), zeros [k/32][n_rows/2] (= 8): a matrix for
+ * tk_qmatmul_int4 with group_size 32 whose dequantised weights equal d * (q - 8) exactly.
+ * Nibble order inside a block: TK_Q4_0_REFERENCE_ORDER (weight 2i = low nibble of byte i,
+ * 2i+1 = high nibble: llama.zig:347-350) or TK_Q4_0_GGML_ORDER (weight i = low nibble,
+ * i+16 = high nibble).  k % 32 == 0, n_rows even.  Synchronous. */
+#define TK_Q4_0_REFERENCE_ORDER 0
+#define TK_Q4_0_GGML_ORDER 1
+int tk_repack_q4_0(tk_device *dev, const void *blocks, uint8_t *w_packed, uint16_t *scales,
+                   uint8_t *zeros, uint32_t n_rows, uint32_t k, int order);
+
 /* Test hook (bit-exactness of dequantisation, shaders.zig:474-495):
  * out f32 [k][n] = float(scale[g][n]) * (float(q[k][n]) - float(zero[g][n])). */
 int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *scales,

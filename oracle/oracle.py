@@ -130,6 +130,40 @@ def matvec_f32_sequential(x, W, K: int, N: int) -> np.ndarray:
     return out
 
 
+def q4_0_decode_f32(blocks, n_rows: int, k: int, order: int = 0) -> np.ndarray:
+    """GGUF Q4_0 -> dense f32 [n_rows][k] (weight = (q - 8) * d).  order 0 follows the reference
+    loader (src/model/llama.zig:341-353: weight 2i = low nibble of qs[i], 2i+1 = high nibble);
+    order 1 the ggml layout (weight i = low nibble, i + 16 = high nibble)."""
+    b = np.asarray(blocks, dtype=np.uint8).reshape(n_rows, k // 32, 18)
+    d = b[:, :, 0:2].copy().view(np.float16).astype(np.float32)  # [n][k/32][1]
+    qs = b[:, :, 2:]
+    lo, hi = (qs & 0xF).astype(np.float32), (qs >> 4).astype(np.float32)
+    q = np.empty((n_rows, k // 32, 32), dtype=np.float32)
+    if order == 0:
+        q[:, :, 0::2], q[:, :, 1::2] = lo, hi
+    else:
+        q[:, :, :16], q[:, :, 16:] = lo, hi
+    return ((q - 8.0) * d).reshape(n_rows, k).astype(np.float32)
+
+
+def q4_0_repack(blocks, n_rows: int, k: int, order: int = 0):
+    """The qmatmul_int4 layout (group size 32) of GGUF Q4_0 blocks: (w_packed [k/2][n],
+    scales f16 bits [k/32][n], zeros [k/32][n/2] = 0x88), codes and d unchanged."""
+    b = np.asarray(blocks, dtype=np.uint8).reshape(n_rows, k // 32, 18)
+    d = b[:, :, 0:2].copy().view(np.uint16)[:, :, 0]  # [n][k/32]
+    qs = b[:, :, 2:]
+    lo, hi = qs & 0xF, qs >> 4
+    q = np.empty((n_rows, k // 32, 32), dtype=np.uint8)
+    if order == 0:
+        q[:, :, 0::2], q[:, :, 1::2] = lo, hi
+    else:
+        q[:, :, :16], q[:, :, 16:] = lo, hi
+    qk = q.reshape(n_rows, k).T  # [k][n]
+    w = (qk[0::2] | (qk[1::2] << 4)).astype(np.uint8)
+    return (np.ascontiguousarray(w), np.ascontiguousarray(d.T.astype(np.uint16)),
+            np.full((k // 32, n_rows // 2), 0x88, dtype=np.uint8))
+
+
 def normwise_err(y, ref) -> float:
     """max_i |y_i - ref_i| / max_i |ref_i| (the path's error metric)."""
     y = np.asarray(y, dtype=np.float64)

@@ -128,3 +128,37 @@ def test_matvec_oracle_matches_shader_order():
     y32 = oracle.matvec_f32_sequential(x, W, K, N)
     assert np.allclose(y64, W.astype(np.float64) @ x.astype(np.float64))
     assert oracle.normwise_err(y32, y64) < 1e-6
+
+
+def _q4_0_blocks(seed, n_rows, k):
+    rng = np.random.default_rng(seed)
+    b = rng.integers(0, 256, size=(n_rows, k // 32, 18), dtype=np.uint8)
+    d = (rng.uniform(0.005, 0.02, size=(n_rows, k // 32))).astype(np.float16)
+    b[:, :, 0:2] = d.view(np.uint8).reshape(n_rows, k // 32, 2)
+    return b.reshape(-1)
+
+
+def test_q4_0_known_answer():
+    """One block, d = 0.5, qs[i] = (2i+1) << 4 | 2i mod 16: the reference loader's order
+    (src/model/llama.zig:347-350) gives weight j = (j mod 16 - 8) * 0.5 for j < 32 (2i -> low
+    nibble 2i, 2i+1 -> high nibble 2i+1); ggml's order puts the low nibbles first."""
+    blk = np.zeros(18, dtype=np.uint8)
+    blk[0:2] = np.array([0.5], dtype=np.float16).view(np.uint8)
+    for i in range(16):
+        blk[2 + i] = ((2 * i) % 16) | (((2 * i + 1) % 16) << 4)
+    ref = oracle.q4_0_decode_f32(blk, 1, 32, order=0)[0]
+    assert np.array_equal(ref, (np.arange(32) % 16 - 8).astype(np.float32) * 0.5)
+    ggml = oracle.q4_0_decode_f32(blk, 1, 32, order=1)[0]
+    assert np.array_equal(ggml[:16], ((2 * np.arange(16)) % 16 - 8).astype(np.float32) * 0.5)
+    assert np.array_equal(ggml[16:], ((2 * np.arange(16) + 1) % 16 - 8).astype(np.float32) * 0.5)
+
+
+@pytest.mark.parametrize("order", [0, 1])
+def test_q4_0_repack_oracle_exact(order):
+    """The layout restatement dequantises (shaders.zig:474-495 semantics, group 32) to exactly
+    the loader's f32 weights, transposed to [k][n]."""
+    n_rows, k = 6, 96
+    blocks = _q4_0_blocks(11 + order, n_rows, k)
+    w, s, z = oracle.q4_0_repack(blocks, n_rows, k, order)
+    dense = oracle.dequant_f32(w, s, z, k, n_rows, 32)
+    assert np.array_equal(dense, oracle.q4_0_decode_f32(blocks, n_rows, k, order).T)

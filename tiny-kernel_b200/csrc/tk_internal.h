@@ -40,6 +40,8 @@ cudaError_t launch_add(const float* a, const float* b, float* out, int n, cudaSt
 cudaError_t launch_f32_to_f16(const float* x, __half* y, long long n, cudaStream_t st);
 cudaError_t launch_matvec_f32(const float* x, const float* W0, const float* W1, float* out0,
                               float* out1, int K, int N, int sm_count, cudaStream_t st);
+cudaError_t launch_repack_q4_0(const uint8_t* blocks, uint8_t* w, uint16_t* s, uint8_t* z, int N,
+                               int K, int order, cudaStream_t st);
 cudaError_t launch_rmsnorm_f16(const float* x, const float* w, __half* out, int rows, int dim,
                                float eps, cudaStream_t st);
 cudaError_t launch_splitk_reduce(const float* part, int splits, long long mn, const float* residual,

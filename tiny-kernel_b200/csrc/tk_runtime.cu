@@ -890,6 +890,20 @@ int tk_matvec(tk_device* d, const float* x, const float* W, float* out, uint32_t
   return sync_and_check(d, d->stream);
 }
 
+int tk_repack_q4_0(tk_device* d, const void* blocks, uint8_t* w, uint16_t* s, uint8_t* z,
+                   uint32_t n, uint32_t k, int order) {
+  if (!d || !blocks || !w || !s || !z) return fail(TK_ERR_ARG, "NULL argument");
+  if (n == 0 || k == 0 || k % 32 || n % 2)
+    return fail(TK_ERR_ARG, "Q4_0 repack needs k %% 32 == 0 and an even row count (k=%u, n=%u)", k, n);
+  if (order != TK_Q4_0_REFERENCE_ORDER && order != TK_Q4_0_GGML_ORDER)
+    return fail(TK_ERR_ARG, "unknown Q4_0 nibble order %d", order);
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_LAUNCH(d, launch_repack_q4_0(static_cast<const uint8_t*>(blocks), w, s, z, (int)n, (int)k, order,
+                                  d->stream));
+  return sync_and_check(d, d->stream);
+}
+
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
   if (m == 0 || k == 0 || n == 0 || gs == 0 || gs % 8 || k % gs || n % 2) return -1;
   if (!engine_shape(k, n, gs)) return 0;

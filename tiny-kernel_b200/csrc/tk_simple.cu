@@ -164,6 +164,41 @@ __global__ void __launch_bounds__(256) matvec_f32_kernel(const float* __restrict
   }
 }
 
+// GGUF Q4_0 blocks (f16 d, 16 bytes of nibbles; 32 weights of one output row n) -> the
+// qmatmul_int4 layout with group size 32: scale d, zero point 8, codes unchanged, so
+// s * (q - z) = d * (q - 8) exactly.  Thread t of a block handles output column n0 + t of one
+// 32-k block kb: 16 packed bytes at rows 16kb .. 16kb+15 (128 threads -> 128 contiguous bytes
+// per row store).  order 0: weight 2i = low nibble of qs[i], 2i+1 = high nibble (the reference
+// loader, src/model/llama.zig:341-353); order 1: weight i = low nibble, i + 16 = high nibble.
+__global__ void __launch_bounds__(128) repack_q4_0_kernel(const uint8_t* __restrict__ blocks,
+                                                          uint8_t* __restrict__ w,
+                                                          uint16_t* __restrict__ s,
+                                                          uint8_t* __restrict__ z, int N, int K,
+                                                          int order) {
+  const int n = blockIdx.x * 128 + threadIdx.x;
+  const int kb = blockIdx.y;
+  if (n >= N) return;
+  const uint8_t* blk = blocks + ((size_t)n * (K / 32) + kb) * 18;
+  const uint16_t d = (uint16_t)(blk[0] | (blk[1] << 8));
+  uint8_t q[32];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint8_t b = blk[2 + i];
+    if (order == 0) {
+      q[2 * i] = b & 0xF;
+      q[2 * i + 1] = b >> 4;
+    } else {
+      q[i] = b & 0xF;
+      q[i + 16] = b >> 4;
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < 16; ++p)
+    w[(size_t)(16 * kb + p) * N + n] = (uint8_t)(q[2 * p] | (q[2 * p + 1] << 4));
+  s[(size_t)kb * N + n] = d;
+  if ((n & 1) == 0) z[(size_t)kb * (N / 2) + n / 2] = 0x88;
+}
+
 // rmsnorm of one row, written as f16 (the activations of the tensor-core GEMM).
 __global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                    __half* __restrict__ out, int dim, float eps) {
@@ -288,6 +323,13 @@ cudaError_t launch_matvec_f32(const float* x, const float* W0, const float* W1, 
     matvec_f32_kernel<2><<<blocks, 256, 0, st>>>(x, W0, W1, out0, out1, K, N, vec);
   else
     matvec_f32_kernel<1><<<blocks, 256, 0, st>>>(x, W0, nullptr, out0, nullptr, K, N, vec);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_repack_q4_0(const uint8_t* blocks, uint8_t* w, uint16_t* s, uint8_t* z, int N,
+                               int K, int order, cudaStream_t st) {
+  const dim3 grid((unsigned)((N + 127) / 128), (unsigned)(K / 32));
+  repack_q4_0_kernel<<<grid, 128, 0, st>>>(blocks, w, s, z, N, K, order);
   return cudaGetLastError();
 }
 

@@ -27,6 +27,8 @@ TK_MEM_HOST = 2
 
 TK_FFN_RESIDUAL = 1
 TK_TP_UNIQUE_ID_BYTES = 128
+TK_Q4_0_REFERENCE_ORDER = 0
+TK_Q4_0_GGML_ORDER = 1
 
 vp = C.c_void_p
 u32 = C.c_uint32
@@ -77,6 +79,7 @@ SIGNATURES = {
     "tk_matvec_async": (i32, [vp, vp, vp, vp, u32, u32, vp]),
     "tk_matvec_dual": (i32, [vp, vp, vp, vp, vp, vp, u32, u32]),
     "tk_matvec_dual_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, vp]),
+    "tk_repack_q4_0": (i32, [vp, vp, vp, vp, vp, u32, u32, i32]),
     "tk_tp_unique_id": (i32, [vp]),
     "tk_tp_create": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),
     "tk_tp_destroy": (None, [vp]),

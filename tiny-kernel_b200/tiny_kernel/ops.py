@@ -119,6 +119,13 @@ def matvec_dual(device, x, W1, W2, out1, out2, K, N, stream=None, sync=True):
             check(L.tk_device_synchronize(_dev(device)))
 
 
+def repack_q4_0(device, blocks, w_packed, scales, zeros, n_rows, k, order=0):
+    """GGUF Q4_0 blocks [n_rows][k/32] x 18 B -> qmatmul_int4 layout, group size 32
+    (order 0: the reference loader's nibble order, 1: ggml's)."""
+    check(_lib.lib().tk_repack_q4_0(_dev(device), _ptr(blocks), _ptr(w_packed), _ptr(scales),
+                                    _ptr(zeros), int(n_rows), int(k), int(order)))
+
+
 def dequant_int4(device, w_packed, scales, zeros, out, k, n, group_size):
     check(_lib.lib().tk_dequant_int4(_dev(device), _ptr(w_packed), _ptr(scales), _ptr(zeros),
                                      _ptr(out), int(k), int(n), int(group_size)))
