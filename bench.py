@@ -231,6 +231,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--collective", default="nccl", choices=["p2p", "nccl"],
+                    help="tensor-parallel exchange: the library's group (one-shot all-reduce over "
+                         "NVLink peer memory, NCCL beyond its size limit) or torch.distributed NCCL")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -255,6 +258,12 @@ def main():
                                 device_id=torch.device("cuda", local))
         pg = dist
     dev = tk.init(local)
+    group = None
+    if pg is not None and args.collective == "p2p":
+        from tiny_kernel.tp import Group, unique_id
+        box = [unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(box, src=0)
+        group = Group(dev, world, rank, box[0])
     m = args.batch
     L = args.layers
     name, hidden, inter_full = MODELS[args.model]
@@ -299,7 +308,7 @@ def main():
     xb = torch.empty((m, hidden), dtype=torch.float32, device="cuda")
     stream = torch.cuda.Stream()
     # stacks carry the residual (added once, by rank 0's kernel, before the all-reduce)
-    residual = L > 1 and rank == 0
+    residual = L > 1 and (rank == 0 or group is not None)
 
     def run_step(i, x_in, bufs, sync):
         """One step: L blocks; returns the buffer that holds the step's output."""
@@ -307,6 +316,13 @@ def main():
         for l in range(L):
             nw, g, u, d = mats[i % copies][l]
             out = bufs[l % 2]
+            if group is not None:
+                # shard FFN + the exchange, both inside the library
+                group.int4_ffn(cur, nw, g, u, d, out, m, hidden, inter, GS, eps=EPS,
+                               residual=residual, stream=None if sync else stream.cuda_stream,
+                               sync=sync)
+                cur = out
+                continue
             ops.int4_ffn(dev, cur, nw, g, u, d, out, m, hidden, inter, GS, eps=EPS,
                          residual=residual, stream=None if sync else stream.cuda_stream, sync=sync)
             if pg is not None:
@@ -457,6 +473,9 @@ def main():
                 "workload": workload_name(name, m, L),
                 "hidden": hidden, "inter": inter_full, "group_size": GS, "batch": m, "layers": L,
                 "parallelism": f"tp{world}", "weight_copies": copies,
+                "collective": (None if pg is None else
+                               ("peer-memory one-shot all-reduce" if group is not None and group.uses_p2p
+                                else "NCCL all-reduce")),
                 "l2_guard": f"{copies} weight copies x {L} block(s) = "
                             f"{copies * L * shard_w_bytes / 1e6:.0f} MB per GPU (> 3x L2)",
                 "launch": "cuda-graph" if graph is not None else "stream",
@@ -474,6 +493,8 @@ def main():
         print(json.dumps(line), flush=True)
     if graph is not None:
         del graph
+    if group is not None:
+        group.close()
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()

@@ -190,8 +190,14 @@ int tk_int4_ffn_tp_async(tk_tp *tp, const float *x, const float *norm_weight,
                          const tk_int4_matrix *down, float *out, uint32_t m, uint32_t hidden,
                          uint32_t inter_shard, uint32_t group_size, float eps, uint32_t flags,
                          void *stream);
-/* In-place sum of an f32 device buffer across the group (the FFN's exchange step). */
+/* In-place sum of an f32 device buffer across the group (the FFN's exchange step).  Up to
+ * 262144 floats it is a one-shot all-reduce over NVLink peer memory (the ranks map one another's
+ * receive areas at tk_tp_create; sums in rank order, so every rank gets the same bits; bounded
+ * waits report TK_ERR_TIMEOUT through tk_device_check_error); larger buffers, or groups where a
+ * rank could not map its peers, or TK_TP_NCCL=1 in the environment, use NCCL. */
 int tk_tp_allreduce_sum_f32(tk_tp *tp, float *buf, size_t count, void *stream);
+/* 1 when the group uses the peer-memory all-reduce, 0 when NCCL carries every exchange. */
+int tk_tp_uses_p2p(tk_tp *tp);
 
 /* ---- fp32 matvec ---------------------------------------------------------------------
  * Replaces Matvec.forward(x, W, out, K, N) (src/kernels/fused.zig:62-89, shaders.zig:184-226):

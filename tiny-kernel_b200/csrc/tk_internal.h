@@ -40,6 +40,23 @@ cudaError_t launch_add(const float* a, const float* b, float* out, int n, cudaSt
 cudaError_t launch_f32_to_f16(const float* x, __half* y, long long n, cudaStream_t st);
 cudaError_t launch_matvec_f32(const float* x, const float* W0, const float* W1, float* out0,
                               float* out1, int K, int N, int sm_count, cudaStream_t st);
+// One-shot peer-memory all-reduce (tk_allreduce.cu).
+constexpr int kP2PMaxRanks = 8;
+constexpr int kP2PMaxChunks = 512;
+constexpr int kP2PChunkFloats = 512;
+constexpr size_t kP2PMaxFloats = (size_t)kP2PMaxChunks * kP2PChunkFloats;  // 1 MB of f32
+constexpr unsigned kErrP2PWait = 8u;
+struct P2PParams {
+  float* buf;                       // the local vector, summed in place
+  int count, chunk, nranks, rank;
+  size_t slot_floats;               // floats per receive slot (one rank, one parity)
+  float* recv[kP2PMaxRanks];        // rank r's receive area, mapped here: [2][nranks][slot]
+  unsigned* flags[kP2PMaxRanks];    // rank r's flags, mapped here: [nranks][kP2PMaxChunks]
+  unsigned* counters;               // local epoch per chunk [kP2PMaxChunks]
+  unsigned* err;
+  unsigned long long timeout_ns;
+};
+cudaError_t launch_p2p_allreduce(const P2PParams& p, cudaStream_t st);
 cudaError_t launch_repack_q4_0(const uint8_t* blocks, uint8_t* w, uint16_t* s, uint8_t* z, int N,
                                int K, int order, cudaStream_t st);
 cudaError_t launch_rmsnorm_f16(const float* x, const float* w, __half* out, int rows, int dim,

@@ -1271,6 +1271,8 @@ struct NcclApi {
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   bool ok = false;
@@ -1287,10 +1289,11 @@ int nccl_api(const NcclApi** out) {
     g_nccl.get_unique_id = reinterpret_cast<decltype(g_nccl.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
     g_nccl.comm_init_rank = reinterpret_cast<decltype(g_nccl.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     g_nccl.all_reduce = reinterpret_cast<decltype(g_nccl.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(h, "ncclAllGather"));
     g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     g_nccl.error_string = reinterpret_cast<decltype(g_nccl.error_string)>(dlsym(h, "ncclGetErrorString"));
     g_nccl.ok = g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.all_reduce &&
-                g_nccl.comm_destroy && g_nccl.error_string;
+                g_nccl.all_gather && g_nccl.comm_destroy && g_nccl.error_string;
   });
   if (!g_nccl.ok) return fail(TK_ERR_NCCL, "NCCL (libnccl.so.2) could not be loaded");
   *out = &g_nccl;
@@ -1309,7 +1312,103 @@ struct tk_tp {
   tk_device* dev = nullptr;
   ncclComm_t comm = nullptr;
   int nranks = 0, rank = 0;
+  // one-shot peer-memory all-reduce (tk_allreduce.cu); off when any rank could not map its peers
+  bool p2p = false;
+  void* p2p_base = nullptr;              // this rank's receive area + flags + chunk epochs
+  void* p2p_peer[tk::kP2PMaxRanks] = {};  // peers' areas mapped here (CUDA IPC)
+  tk::P2PParams p2p_params{};
 };
+
+namespace {
+
+// Sum of one int across the group (NCCL), for decisions every rank must take alike.
+int tp_sum_int(tk_tp* tp, const NcclApi* n, int v, int* out) {
+  int* dv = nullptr;
+  TK_CUDA_TRY(cudaMalloc(&dv, sizeof(int)));
+  cudaError_t e = cudaMemcpy(dv, &v, sizeof(int), cudaMemcpyHostToDevice);
+  ncclResult_t r = e == cudaSuccess ? n->all_reduce(dv, dv, 1, ncclInt32, ncclSum, tp->comm, tp->dev->stream)
+                                    : ncclSuccess;
+  if (e == cudaSuccess && r == ncclSuccess) e = cudaStreamSynchronize(tp->dev->stream);
+  if (e == cudaSuccess && r == ncclSuccess) e = cudaMemcpy(out, dv, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(dv);
+  if (r != ncclSuccess) return nccl_fail(n, "ncclAllReduce", r);
+  TK_CUDA_TRY(e);
+  return TK_OK;
+}
+
+void tp_p2p_release(tk_tp* tp) {
+  for (int r = 0; r < tk::kP2PMaxRanks; ++r)
+    if (tp->p2p_peer[r]) {
+      cudaIpcCloseMemHandle(tp->p2p_peer[r]);
+      tp->p2p_peer[r] = nullptr;
+    }
+  if (tp->p2p_base) cudaFree(tp->p2p_base);
+  tp->p2p_base = nullptr;
+  tp->p2p = false;
+}
+
+// Receive areas for the peer-memory all-reduce: allocate, zero, exchange IPC handles (NCCL
+// all-gather), map the peers; then every rank learns whether all ranks succeeded.
+int tp_p2p_setup(tk_tp* tp, const NcclApi* n) {
+  using namespace tk;
+  const int R = tp->nranks;
+  const size_t slot = kP2PMaxFloats;
+  const size_t recv_bytes = 2 * (size_t)R * slot * sizeof(float);
+  const size_t flag_bytes = (size_t)R * kP2PMaxChunks * sizeof(unsigned);
+  const size_t bytes = recv_bytes + flag_bytes + kP2PMaxChunks * sizeof(unsigned);
+  int ok = 1;
+  cudaIpcMemHandle_t mine{};
+  if (cudaMalloc(&tp->p2p_base, bytes) != cudaSuccess || cudaMemset(tp->p2p_base, 0, bytes) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&mine, tp->p2p_base) != cudaSuccess)
+    ok = 0;
+  cudaGetLastError();
+  // all ranks take part in the all-gather whatever happened above
+  uint8_t* dh = nullptr;
+  TK_CUDA_TRY(cudaMalloc(&dh, (size_t)R * sizeof(cudaIpcMemHandle_t)));
+  std::vector<cudaIpcMemHandle_t> handles(R);
+  cudaError_t e = cudaMemcpy(dh + (size_t)tp->rank * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+  ncclResult_t r = n->all_gather(dh + (size_t)tp->rank * sizeof(mine), dh, sizeof(mine), ncclUint8, tp->comm,
+                                 tp->dev->stream);
+  if (e == cudaSuccess && r == ncclSuccess) e = cudaStreamSynchronize(tp->dev->stream);
+  if (e == cudaSuccess && r == ncclSuccess)
+    e = cudaMemcpy(handles.data(), dh, (size_t)R * sizeof(mine), cudaMemcpyDeviceToHost);
+  cudaFree(dh);
+  if (r != ncclSuccess) return nccl_fail(n, "ncclAllGather", r);
+  TK_CUDA_TRY(e);
+  P2PParams& P = tp->p2p_params;
+  std::memset(&P, 0, sizeof(P));
+  for (int q = 0; q < R && ok; ++q) {
+    void* base = tp->p2p_base;
+    if (q != tp->rank) {
+      if (cudaIpcOpenMemHandle(&tp->p2p_peer[q], handles[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+        break;
+      }
+      base = tp->p2p_peer[q];
+    }
+    P.recv[q] = static_cast<float*>(base);
+    P.flags[q] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(base) + recv_bytes);
+  }
+  int all = 0;
+  int st = tp_sum_int(tp, n, ok, &all);
+  if (st != TK_OK) return st;
+  if (all != R) {
+    tp_p2p_release(tp);
+    return TK_OK;  // NCCL carries the exchange
+  }
+  P.chunk = kP2PChunkFloats;
+  P.nranks = R;
+  P.rank = tp->rank;
+  P.slot_floats = slot;
+  P.counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(tp->p2p_base) + recv_bytes + flag_bytes);
+  P.err = tp->dev->err;
+  P.timeout_ns = tp->dev->timeout_ns;
+  tp->p2p = true;
+  return TK_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -1346,15 +1445,32 @@ int tk_tp_create(tk_device* d, int nranks, int rank, const uint8_t id[TK_TP_UNIQ
     delete tp;
     return nccl_fail(n, "ncclCommInitRank", r);
   }
+  const char* force_nccl = std::getenv("TK_TP_NCCL");
+  if (nranks > 1 && nranks <= tk::kP2PMaxRanks && !(force_nccl && std::atoi(force_nccl))) {
+    st = tp_p2p_setup(tp, n);
+    if (st != TK_OK) {
+      tk_tp_destroy(tp);
+      return st;
+    }
+  }
   *out = tp;
   return TK_OK;
 }
+
+int tk_tp_uses_p2p(tk_tp* tp) { return tp && tp->p2p ? 1 : 0; }
 
 void tk_tp_destroy(tk_tp* tp) {
   if (!tp) return;
   const NcclApi* n = nullptr;
   if (tp->comm && nccl_api(&n) == TK_OK) {
     cudaSetDevice(tp->dev->ordinal);
+    cudaStreamSynchronize(tp->dev->stream);
+    if (tp->p2p_base) {
+      // no peer may still be writing into this rank's area when it is freed
+      int all = 0;
+      tp_sum_int(tp, n, 1, &all);
+    }
+    tp_p2p_release(tp);
     n->comm_destroy(tp->comm);
   }
   delete tp;
@@ -1362,10 +1478,18 @@ void tk_tp_destroy(tk_tp* tp) {
 
 int tk_tp_allreduce_sum_f32(tk_tp* tp, float* buf, size_t count, void* stream) {
   if (!tp || (!buf && count)) return fail(TK_ERR_ARG, "NULL argument");
-  const NcclApi* n = nullptr;
-  int st = nccl_api(&n);
+  if (count == 0 || tp->nranks == 1) return TK_OK;
+  int st = set_device(tp->dev);
   if (st != TK_OK) return st;
-  if ((st = set_device(tp->dev)) != TK_OK) return st;
+  if (tp->p2p && count <= tk::kP2PMaxFloats) {
+    tk::P2PParams P = tp->p2p_params;
+    P.buf = buf;
+    P.count = (int)count;
+    TK_LAUNCH(tp->dev, tk::launch_p2p_allreduce(P, pick_stream(tp->dev, stream)));
+    return TK_OK;
+  }
+  const NcclApi* n = nullptr;
+  if ((st = nccl_api(&n)) != TK_OK) return st;
   ncclResult_t r = n->all_reduce(buf, buf, count, ncclFloat32, ncclSum, tp->comm,
                                  pick_stream(tp->dev, stream));
   if (r != ncclSuccess) return nccl_fail(n, "ncclAllReduce", r);

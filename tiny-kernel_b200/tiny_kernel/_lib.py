@@ -84,6 +84,7 @@ SIGNATURES = {
     "tk_tp_create": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),
     "tk_tp_destroy": (None, [vp]),
     "tk_tp_allreduce_sum_f32": (i32, [vp, vp, C.c_size_t, vp]),
+    "tk_tp_uses_p2p": (i32, [vp]),
     "tk_int4_ffn_tp": (i32, [vp, vp, vp, C.POINTER(Int4MatrixC), C.POINTER(Int4MatrixC),
                              C.POINTER(Int4MatrixC), vp, u32, u32, u32, u32, f32, u32]),
     "tk_int4_ffn_tp_async": (i32, [vp, vp, vp, C.POINTER(Int4MatrixC), C.POINTER(Int4MatrixC),

@@ -61,10 +61,16 @@ class Group:
         if len(uid) != _lib.TK_TP_UNIQUE_ID_BYTES:
             raise ValueError("group id must be 128 bytes")
         self.rank, self.nranks = rank, nranks
+        self.device = device
         idbuf = (C.c_uint8 * _lib.TK_TP_UNIQUE_ID_BYTES).from_buffer_copy(uid)
         h = C.c_void_p()
         _lib.check(_lib.lib().tk_tp_create(device.handle, nranks, rank, idbuf, C.byref(h)))
         self.handle = h
+
+    @property
+    def uses_p2p(self) -> bool:
+        """True when exchanges go over NVLink peer memory (the one-shot all-reduce)."""
+        return bool(_lib.lib().tk_tp_uses_p2p(self.handle))
 
     def close(self):
         if self.handle:
@@ -90,6 +96,8 @@ class Group:
                                         int(inter_shard), int(group_size), float(eps), flags,
                                         stream)
         _lib.check(st)
+        if sync and stream is not None:
+            self.device.synchronize()
 
 
 def _ptr(v) -> int:
