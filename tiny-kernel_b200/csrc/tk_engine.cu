@@ -943,6 +943,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           W.scales[i] = P.scales[i];
           W.zeros[i] = P.zeros[i];
         }
+        // The items of a phase fed by partial sums wait for those sums (the gate/up -> down
+        // transition) while HBM has nothing to stream: bring all of this CTA's items of the
+        // phase into L2 now, so that their copies into the ring come from L2 afterwards.
+        if (p.prefetch_l2 && !wi.rec_pro && lane == 0) {
+          ItemIter pi = wi;
+          for (int n = 0; pi.ph == wph && n < 64; ++n) {
+            const int mat = pi.cu & (pi.nmat - 1);
+            const int wt = pi.cu >> (pi.nmat - 1);
+            tma_prefetch_2d(&maps.map[W.map_base + 2 * mat], wt * (kWideCols / 8),
+                            pi.grp * pi.spg * kStepRows);
+            iter_next(pi, T, b, Ptot);
+          }
+        }
       }
       if (lane == 0) {
         if (G == 0) trace_event(p, 7);

@@ -142,6 +142,8 @@ struct EngineParams {
   int aux_stage_bytes;
   // segment counters the last CTA to finish returns to zero (the kEpiSiluMul reductions'),
   // and per kEpiSiluMul phase the (segment, slice) pairs it has completed (inside that range)
+  int prefetch_l2;  // 1: at the switch to a phase fed by partial sums (the down projection), the
+                    // weight warp prefetches all of its items of that phase into L2
   unsigned* zero_counters;
   int zero_count;
   unsigned* phase_done;  // [kMaxPhases]

@@ -94,6 +94,7 @@ struct tk_device {
   // batch >= 16 GEMM path: f16 activations, f16 h, split-K partials
   ScratchBuf g_x16, g_h16, g_part;
   int gemm_enabled = 1;  // TK_GEMM=0 routes every batch through the engine
+  int down_prefetch = 1;  // TK_DOWN_PREFETCH=0 turns off the L2 prefetch of the down projection
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   unsigned long long launches = 0;      // kernels enqueued through this device
   std::vector<TmapEntry> tmaps;
@@ -305,6 +306,7 @@ int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, c
   }
   p.stages = stages;
   p.rec0_smem = rec0_smem;
+  p.prefetch_l2 = d->down_prefetch;
   p.trace = d->trace;
   if (d->trace)
     TK_CUDA_TRY(cudaMemsetAsync(d->trace, 0, (size_t)d->sm_count * kTraceEvents * 8, st));
@@ -733,6 +735,7 @@ int tk_device_create(int ordinal, tk_device** out) {
   if (const char* env = std::getenv("TK_ENGINE_STAGES")) d->stages_override = std::atoi(env);
   if (const char* env = std::getenv("TK_FFN_SPLIT")) d->ffn_split = std::atoi(env);
   if (const char* env = std::getenv("TK_GEMM")) d->gemm_enabled = std::atoi(env);
+  if (const char* env = std::getenv("TK_DOWN_PREFETCH")) d->down_prefetch = std::atoi(env);
   if (const char* env = std::getenv("TK_WAIT_TIMEOUT_MS"))
     d->timeout_ns = (unsigned long long)std::atoll(env) * 1000000ull;
   if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
