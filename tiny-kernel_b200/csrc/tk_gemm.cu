@@ -340,15 +340,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //               -> aux ring
 //   warp 1      tensor-memory allocation, MMA issue (A from tensor memory): 2 tiles x 8
 //               tcgen05.mma.kind::f16 (128 x NT x 16) per step
-//   warps 2-9   dequantisers, then the epilogue.  Warp w writes tensor-memory lanes
-//               32(w%4) .. +31 (its lane quarter) of tile (w-2)/4, all 64 columns (packed rows)
-//               of the step.  Lane l (j = l/4, u = l%4) loads the 32-bit words of packed rows
-//               8c + 2u + e (c in 0..7, e in {0,1}) at columns 32q + 4j .. 32q + 4j + 3 (rows 2
-//               apart inside a quad: with the swizzle the warp's loads hit 32 distinct banks)
-//               and stores them with tcgen05.st.16x256b, whose thread layout holds exactly those
-//               cells: column (packed row) 8c + 2u + e of lanes j + 8i' + 16h for byte
-//               i = 2h + i'.  So tensor-memory lane 32q + l holds output column
-//               32q + 4(l%8) + l/8.
+//   warps 2-17  dequantisers, then the epilogue.  Warp w writes tensor-memory lanes
+//               32(w%4) .. +31 (its lane quarter) of tile t, columns 32ch .. 32ch+31 (packed
+//               rows of the step), (t, ch) from (w-2)/4.  Lane l (j = l/4, u = l%4) loads the
+//               32-bit words of packed rows 32ch + 8c + 2u + e (c in 0..3, e in {0,1}) at
+//               columns 32q + 4j .. 32q + 4j + 3 (rows 2 apart inside a quad: with the swizzle
+//               the warp's loads hit 32 distinct banks) and stores them with tcgen05.st.16x256b,
+//               whose thread layout holds exactly those cells: column (packed row)
+//               32ch + 8c + 2u + e of lanes j + 8i' + 16h for byte i = 2h + i'.  So
+//               tensor-memory lane 32q + l holds output column 32q + 4(l%8) + l/8.
 //   A cell is one packed byte: f16 pair (k even, k odd) = (1024 + lo, 64 + hi) by the exponent
 //   constants 0x6400 / 0x5400, minus (1024 + z, 64 + z) (exact), times (s, s) (one rounding).
 // A step's tensor-memory stores complete (tcgen05.wait::st) after the next step's cells are
@@ -500,22 +500,23 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
     }
   } else {
     // --------------------------- dequantisers, then epilogue ------------------------------
-    const int q = warp & 3;         // tensor-memory lane quarter
-    const int t = (warp - 2) >> 2;  // tile
+    const int q = warp & 3;              // tensor-memory lane quarter
+    const int pidx = (warp - 2) >> 2;    // (tile, column half)
+    const int t = pidx >> 1, ch = pidx & 1;
     const int j = lane >> 2, u = lane & 3;
     const int cbase = 32 * q + 4 * j;  // this lane's 4 output columns (within the tile)
-    // swizzled shared-memory offsets (inside a raw stage) of packed rows 8c + 2u + e at columns
-    // cbase .. cbase + 3: chunk (cbase / 16) ^ (row % 8), row % 8 = 2u + e; + c * 1024
+    // swizzled shared-memory offsets (inside a raw stage) of packed rows 32ch + 8c + 2u + e at
+    // columns cbase .. cbase + 3: chunk (cbase / 16) ^ (row % 8), row % 8 = 2u + e; + c * 1024
     uint32_t w_off[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int row = 2 * u + e;
-      w_off[e] = (uint32_t)(kP + t * kGemmTmWeightTile + row * 128 +
+      w_off[e] = (uint32_t)(kP + t * kGemmTmWeightTile + ch * 4096 + row * 128 +
                             (((cbase >> 4) ^ row) << 4) + (cbase & 15));
     }
     const uint32_t rbase = smem_addr(rring), xbase = smem_addr(xring);
-    // tensor-memory address of this warp's block: lanes 32q (+16h), columns of tile t
-    const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + kAcol0 + (uint32_t)(64 * t);
+    // tensor-memory address of this warp's block: lanes 32q (+16h), columns 32ch of tile t
+    const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16) + kAcol0 + (uint32_t)(64 * t + 32 * ch);
     const uint32_t gmask = (uint32_t)p.gs - 1u;
     RingPos rr, ra, rx;
     int gb = 0;
@@ -546,13 +547,13 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
       const uint32_t st = rbase + (uint32_t)rr.s * (uint32_t)kRaw;
       const uint32_t xs = xbase + (uint32_t)rx.s * (uint32_t)kGemmAuxStageBytes;
       const int k0 = (ks0 + i) * kGemmTmKStep;
-      uint32_t h0[32], h1[32];  // the two 16x256b.x8 stores (lane halves h = 0, 1)
+      uint32_t h0[16], h1[16];  // the two 16x256b.x4 stores (lane halves h = 0, 1)
       uint32_t sp[4], zp[4];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         if (c == 0 || ((uint32_t)(16 * c) & gmask) == 0u) {
-          // scales and zero points of this lane's 4 columns in the group of k = k0 + 16c
-          const int g = ((k0 + 16 * c) >> lg) - gb;
+          // scales and zero points of this lane's 4 columns in the group of k = k0 + 64ch + 16c
+          const int g = ((k0 + 64 * ch + 16 * c) >> lg) - gb;
           const uint32_t sx = ld_shared_u32(xs + t * 2048 + g * 256 + cbase * 2);
           const uint32_t sy = ld_shared_u32(xs + t * 2048 + g * 256 + cbase * 2 + 4);
           const uint32_t zw = ld_shared_u32(xs + 4096 + t * 512 + g * 64 + ((cbase >> 1) & ~3));
@@ -585,8 +586,8 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
       t_cells += clock64() - c_cells;
       if (pend_a >= 0) complete_pending();
       const uint32_t ta = tl + kAStageCols * (uint32_t)ra.s;
-      tmem_st_16x256b_x8(ta, h0);
-      tmem_st_16x256b_x8(ta + (16u << 16), h1);
+      tmem_st_16x256b_x4(ta, h0);
+      tmem_st_16x256b_x4(ta + (16u << 16), h1);
       pend_r = rr.s;
       pend_a = ra.s;
       const bool last_of_stage = ia + 1 == spa;
@@ -606,7 +607,7 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
       trace[8] = (unsigned long long)t_comp;
       trace[9] = (unsigned long long)t_cells;
     }
-    // epilogue: lane quarter q, the two warps of a quarter take alternate 8-token chunks
+    // epilogue: lane quarter q, the four warps of a quarter take every fourth 8-token chunk
     bool ok = true;
     if (lane == 0) ok = nsteps > 0 && gemm_wait(&done_bar, 0u, p.err, p.timeout_ns);
     ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -614,7 +615,7 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
       tcgen05_fence_after();
       const int cl = 32 * q + tm_lane_column(lane);
       const uint32_t td = tmem + ((uint32_t)(32 * q) << 16);
-      for (int jj = t; jj < NT / 8; jj += 2) {
+      for (int jj = pidx; jj < NT / 8; jj += 4) {
         uint32_t v0[8], v1[8];
         tmem_ld8(td + (uint32_t)(0 * NT + jj * 8), v0);
         tmem_ld8(td + (uint32_t)(1 * NT + jj * 8), v1);

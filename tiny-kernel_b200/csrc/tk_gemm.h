@@ -65,7 +65,7 @@ struct GemmMaps {
 // own ring.
 constexpr int kGemmTmemMaxNT = 64;   // 128- and 256-token tiles: the shared-memory kernel
 constexpr int kGemmTmKStep = 128;
-constexpr int kGemmTmDequantWarps = 8;  // warp d: tile d/4, tensor-memory lane quarter (d+2)%4
+constexpr int kGemmTmDequantWarps = 16;  // warp d: tile d/8, column half (d/4)%2, lane quarter (d+2)%4
 constexpr int kGemmTmThreads = 64 + 32 * kGemmTmDequantWarps;
 constexpr int kGemmTmWeightTile = kGemmTileCols * kGemmTmKStep / 2;  // 8 KB of packed rows
 constexpr int kGemmAuxGroups = 8;
