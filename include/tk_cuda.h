@@ -228,6 +228,22 @@ int tk_matvec_dual_async(tk_device *dev, const float *x, const float *W1, const 
 int tk_repack_q4_0(tk_device *dev, const void *blocks, uint8_t *w_packed, uint16_t *scales,
                    uint8_t *zeros, uint32_t n_rows, uint32_t k, int order);
 
+/* ---- sampler ----------------------------------------------------------------------------
+ * Replaces the argmax shader (src/kernels/shaders.zig:889-943; the host loop of
+ * src/model/llama.zig:290-303): out[0] = index of the largest of x[0..n).  Ties go to the smallest
+ * index (the shader's tie rule follows its thread layout); all -inf or NaN gives 0. */
+int tk_argmax(tk_device *dev, const float *x, uint32_t n, uint32_t *out);
+int tk_argmax_async(tk_device *dev, const float *x, uint32_t n, uint32_t *out, void *stream);
+/* Replaces softmax_sample (shaders.zig:826-887; llama.zig:305-323): probs = softmax(logits /
+ * temperature) over vocab entries; sampled[0] = the first i whose cumulative probability exceeds
+ * random_val in [0, 1), vocab - 1 if none.  The cumulative sums are computed in a different f32
+ * order than the shader's sequential loop: the index can differ only when random_val lies within
+ * rounding of a cumulative boundary.  temperature > 0. */
+int tk_softmax_sample(tk_device *dev, const float *logits, float *probs, uint32_t *sampled,
+                      uint32_t vocab, float temperature, float random_val);
+int tk_softmax_sample_async(tk_device *dev, const float *logits, float *probs, uint32_t *sampled,
+                            uint32_t vocab, float temperature, float random_val, void *stream);
+
 /* Test hook (bit-exactness of dequantisation, shaders.zig:474-495):
  * out f32 [k][n] = float(scale[g][n]) * (float(q[k][n]) - float(zero[g][n])). */
 int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *scales,

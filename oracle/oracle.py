@@ -164,6 +164,25 @@ def q4_0_repack(blocks, n_rows: int, k: int, order: int = 0):
             np.full((k // 32, n_rows // 2), 0x88, dtype=np.uint8))
 
 
+def argmax_ref(x) -> int:
+    """Index of the largest value, the smallest index on ties (numpy's argmax)."""
+    return int(np.argmax(np.asarray(x, dtype=np.float64)))
+
+
+def softmax_f64(logits, temperature: float) -> np.ndarray:
+    """softmax(logits / temperature) in f64 (shaders.zig:826-873)."""
+    z = np.asarray(logits, dtype=np.float64) / float(temperature)
+    e = np.exp(z - z.max())
+    return e / e.sum()
+
+
+def sample_index(probs, random_val: float) -> int:
+    """The first i with random_val < cumsum(probs)[i], len - 1 if none (shaders.zig:875-886)."""
+    c = np.cumsum(np.asarray(probs, dtype=np.float64))
+    hit = np.nonzero(random_val < c)[0]
+    return int(hit[0]) if len(hit) else len(c) - 1
+
+
 def normwise_err(y, ref) -> float:
     """max_i |y_i - ref_i| / max_i |ref_i| (the path's error metric)."""
     y = np.asarray(y, dtype=np.float64)

@@ -162,3 +162,15 @@ def test_q4_0_repack_oracle_exact(order):
     w, s, z = oracle.q4_0_repack(blocks, n_rows, k, order)
     dense = oracle.dequant_f32(w, s, z, k, n_rows, 32)
     assert np.array_equal(dense, oracle.q4_0_decode_f32(blocks, n_rows, k, order).T)
+
+
+def test_sampler_oracle():
+    """softmax_f64 sums to 1 and sample_index follows the shader's first-exceeding search
+    (shaders.zig:875-886), falling back to the last index."""
+    logits = np.array([1.0, 2.0, 3.0], dtype=np.float32)
+    p = oracle.softmax_f64(logits, 1.0)
+    assert abs(p.sum() - 1.0) < 1e-12 and np.argmax(p) == 2
+    assert oracle.sample_index(p, 0.0) == 0
+    assert oracle.sample_index(p, p[0] + 1e-9) == 1
+    assert oracle.sample_index(p, 1.5) == 2
+    assert oracle.argmax_ref([3.0, 5.0, 5.0, 1.0]) == 1

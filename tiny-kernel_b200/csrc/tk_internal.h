@@ -59,6 +59,9 @@ struct P2PParams {
 cudaError_t launch_p2p_allreduce(const P2PParams& p, cudaStream_t st);
 cudaError_t launch_repack_q4_0(const uint8_t* blocks, uint8_t* w, uint16_t* s, uint8_t* z, int N,
                                int K, int order, cudaStream_t st);
+cudaError_t launch_argmax(const float* x, int n, unsigned* out, cudaStream_t st);
+cudaError_t launch_softmax_sample(const float* logits, float* probs, unsigned* sampled, int n,
+                                  float temperature, float random_val, cudaStream_t st);
 cudaError_t launch_rmsnorm_f16(const float* x, const float* w, __half* out, int rows, int dim,
                                float eps, cudaStream_t st);
 cudaError_t launch_splitk_reduce(const float* part, int splits, long long mn, const float* residual,

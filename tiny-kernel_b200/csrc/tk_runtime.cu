@@ -907,6 +907,40 @@ int tk_repack_q4_0(tk_device* d, const void* blocks, uint8_t* w, uint16_t* s, ui
   return sync_and_check(d, d->stream);
 }
 
+int tk_argmax_async(tk_device* d, const float* x, uint32_t n, uint32_t* out, void* stream) {
+  if (!d || !x || !out) return fail(TK_ERR_ARG, "NULL argument");
+  if (n == 0 || n > (1u << 30)) return fail(TK_ERR_ARG, "argmax length %u out of range", n);
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_LAUNCH(d, launch_argmax(x, (int)n, out, pick_stream(d, stream)));
+  return TK_OK;
+}
+
+int tk_argmax(tk_device* d, const float* x, uint32_t n, uint32_t* out) {
+  int st = tk_argmax_async(d, x, n, out, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
+int tk_softmax_sample_async(tk_device* d, const float* logits, float* probs, uint32_t* sampled,
+                            uint32_t vocab, float temperature, float random_val, void* stream) {
+  if (!d || !logits || !probs || !sampled) return fail(TK_ERR_ARG, "NULL argument");
+  if (vocab == 0 || vocab > (1u << 30)) return fail(TK_ERR_ARG, "vocabulary size %u out of range", vocab);
+  if (!(temperature > 0.f)) return fail(TK_ERR_ARG, "temperature must be positive");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_LAUNCH(d, launch_softmax_sample(logits, probs, sampled, (int)vocab, temperature, random_val,
+                                     pick_stream(d, stream)));
+  return TK_OK;
+}
+
+int tk_softmax_sample(tk_device* d, const float* logits, float* probs, uint32_t* sampled,
+                      uint32_t vocab, float temperature, float random_val) {
+  int st = tk_softmax_sample_async(d, logits, probs, sampled, vocab, temperature, random_val, nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
   if (m == 0 || k == 0 || n == 0 || gs == 0 || gs % 8 || k % gs || n % 2) return -1;
   if (!engine_shape(k, n, gs)) return 0;

@@ -199,6 +199,112 @@ __global__ void __launch_bounds__(128) repack_q4_0_kernel(const uint8_t* __restr
   if ((n & 1) == 0) z[(size_t)kb * (N / 2) + n / 2] = 0x88;
 }
 
+// ---- sampler (src/kernels/shaders.zig:826-943) -------------------------------------------
+// One CTA of 1024 threads; vocabularies are small next to the weights (128K f32 = 512 KB).
+constexpr int kSampleThreads = 1024;
+
+// (value, index) pair that wins: the larger value, the smaller index on ties.
+__device__ __forceinline__ void argmax_merge(float& v, unsigned& i, float ov, unsigned oi) {
+  if (ov > v || (ov == v && oi < i)) {
+    v = ov;
+    i = oi;
+  }
+}
+
+__global__ void __launch_bounds__(kSampleThreads) argmax_kernel(const float* __restrict__ x, int n,
+                                                                unsigned* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ unsigned si[32];
+  float v = -INFINITY;
+  unsigned idx = 0xFFFFFFFFu;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) argmax_merge(v, idx, x[i], (unsigned)i);
+  for (int off = 16; off > 0; off >>= 1)
+    argmax_merge(v, idx, __shfl_xor_sync(0xffffffffu, v, off), __shfl_xor_sync(0xffffffffu, idx, off));
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[w] = v;
+    si[w] = idx;
+  }
+  __syncthreads();
+  if (w == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+    idx = lane < (int)(blockDim.x >> 5) ? si[lane] : 0xFFFFFFFFu;
+    for (int off = 16; off > 0; off >>= 1)
+      argmax_merge(v, idx, __shfl_xor_sync(0xffffffffu, v, off), __shfl_xor_sync(0xffffffffu, idx, off));
+    if (lane == 0) out[0] = idx == 0xFFFFFFFFu ? 0u : idx;  // all -inf / NaN: index 0
+  }
+}
+
+// Block-wide reduction of one float (op 0: max, op 1: sum); every thread gets the result.
+__device__ __forceinline__ float block_reduce(float v, int op, float* red) {
+  for (int off = 16; off > 0; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, v, off);
+    v = op == 0 ? fmaxf(v, o) : v + o;
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  v = lane < nw ? red[lane] : (op == 0 ? -INFINITY : 0.f);
+  for (int off = 16; off > 0; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, v, off);
+    v = op == 0 ? fmaxf(v, o) : v + o;
+  }
+  return v;
+}
+
+// probs = softmax(logits / temperature); sampled = the first i whose cumulative probability
+// exceeds random_val (vocab - 1 if none).  The cumulative sums are a block scan over contiguous
+// per-thread chunks, so the chosen index can differ from a sequential f32 sum only when
+// random_val lies within rounding of a boundary.
+__global__ void __launch_bounds__(kSampleThreads) softmax_sample_kernel(
+    const float* __restrict__ logits, float* __restrict__ probs, unsigned* __restrict__ sampled,
+    int n, float temperature, float random_val) {
+  __shared__ float red[32];
+  __shared__ float scan[kSampleThreads];
+  __shared__ unsigned s_pick;
+  const float inv_t = 1.0f / temperature;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) mx = fmaxf(mx, logits[i] * inv_t);
+  mx = block_reduce(mx, 0, red);
+  float sum = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sum += expf(logits[i] * inv_t - mx);
+  sum = block_reduce(sum, 1, red);
+  const float inv_sum = 1.0f / sum;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) probs[i] = expf(logits[i] * inv_t - mx) * inv_sum;
+  __syncthreads();
+  // contiguous chunk of this thread, its probability mass, an inclusive block scan
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int c0 = min(n, (int)threadIdx.x * per), c1 = min(n, c0 + per);
+  float part = 0.f;
+  for (int i = c0; i < c1; ++i) part += probs[i];
+  scan[threadIdx.x] = part;
+  if (threadIdx.x == 0) s_pick = (unsigned)(n - 1);
+  __syncthreads();
+  for (int off = 1; off < (int)blockDim.x; off <<= 1) {
+    const float add = threadIdx.x >= (unsigned)off ? scan[threadIdx.x - off] : 0.f;
+    __syncthreads();
+    scan[threadIdx.x] += add;
+    __syncthreads();
+  }
+  const float before = threadIdx.x ? scan[threadIdx.x - 1] : 0.f;
+  if (c0 < c1 && random_val >= before && random_val < scan[threadIdx.x]) {
+    float cum = before;
+    unsigned pick = (unsigned)(c1 - 1);
+    for (int i = c0; i < c1; ++i) {
+      cum += probs[i];
+      if (random_val < cum) {
+        pick = (unsigned)i;
+        break;
+      }
+    }
+    atomicMin(&s_pick, pick);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) sampled[0] = s_pick;
+}
+
 // rmsnorm of one row, written as f16 (the activations of the tensor-core GEMM).
 __global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                    __half* __restrict__ out, int dim, float eps) {
@@ -330,6 +436,18 @@ cudaError_t launch_repack_q4_0(const uint8_t* blocks, uint8_t* w, uint16_t* s, u
                                int K, int order, cudaStream_t st) {
   const dim3 grid((unsigned)((N + 127) / 128), (unsigned)(K / 32));
   repack_q4_0_kernel<<<grid, 128, 0, st>>>(blocks, w, s, z, N, K, order);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float* x, int n, unsigned* out, cudaStream_t st) {
+  argmax_kernel<<<1, kSampleThreads, 0, st>>>(x, n, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_softmax_sample(const float* logits, float* probs, unsigned* sampled, int n,
+                                  float temperature, float random_val, cudaStream_t st) {
+  softmax_sample_kernel<<<1, kSampleThreads, 0, st>>>(logits, probs, sampled, n, temperature,
+                                                      random_val);
   return cudaGetLastError();
 }
 

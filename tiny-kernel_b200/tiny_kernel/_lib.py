@@ -80,6 +80,10 @@ SIGNATURES = {
     "tk_matvec_dual": (i32, [vp, vp, vp, vp, vp, vp, u32, u32]),
     "tk_matvec_dual_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, vp]),
     "tk_repack_q4_0": (i32, [vp, vp, vp, vp, vp, u32, u32, i32]),
+    "tk_argmax": (i32, [vp, vp, u32, vp]),
+    "tk_argmax_async": (i32, [vp, vp, u32, vp, vp]),
+    "tk_softmax_sample": (i32, [vp, vp, vp, vp, u32, f32, f32]),
+    "tk_softmax_sample_async": (i32, [vp, vp, vp, vp, u32, f32, f32, vp]),
     "tk_tp_unique_id": (i32, [vp]),
     "tk_tp_create": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),
     "tk_tp_destroy": (None, [vp]),

@@ -126,6 +126,18 @@ def repack_q4_0(device, blocks, w_packed, scales, zeros, n_rows, k, order=0):
                                     _ptr(zeros), int(n_rows), int(k), int(order)))
 
 
+def argmax(device, x, n, out):
+    """out[0] = index of the largest of x[0..n) (ties: the smallest index)."""
+    check(_lib.lib().tk_argmax(_dev(device), _ptr(x), int(n), _ptr(out)))
+
+
+def softmax_sample(device, logits, probs, sampled, vocab, temperature, random_val):
+    """probs = softmax(logits / temperature); sampled[0] = first index whose cumulative
+    probability exceeds random_val (shaders.zig:826-887)."""
+    check(_lib.lib().tk_softmax_sample(_dev(device), _ptr(logits), _ptr(probs), _ptr(sampled),
+                                       int(vocab), float(temperature), float(random_val)))
+
+
 def dequant_int4(device, w_packed, scales, zeros, out, k, n, group_size):
     check(_lib.lib().tk_dequant_int4(_dev(device), _ptr(w_packed), _ptr(scales), _ptr(zeros),
                                      _ptr(out), int(k), int(n), int(group_size)))
