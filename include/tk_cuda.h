@@ -228,6 +228,24 @@ int tk_matvec_dual_async(tk_device *dev, const float *x, const float *W1, const 
 int tk_repack_q4_0(tk_device *dev, const void *blocks, uint8_t *w_packed, uint16_t *scales,
                    uint8_t *zeros, uint32_t n_rows, uint32_t k, int order);
 
+/* ---- paged decode attention ---------------------------------------------------------------
+ * Replaces PagedAttention.forward(q, k_cache, v_cache, block_tables, context_lens, o, batch_size,
+ * num_heads, head_dim, max_blocks) (src/kernels/attention.zig:51-100, shaders.zig:503-587):
+ * for sequence b and head h, o = softmax(q . K^T / sqrt(head_dim)) V over the sequence's first
+ * context_lens[b] tokens; token t lives in physical block block_tables[b * max_blocks + t / 16]
+ * of k_cache / v_cache laid out [block][num_heads][16][head_dim].  q, o: [batch][num_heads]
+ * [head_dim] f32; head_dim <= 128 (the shader's limit).  A sequence with no tokens gives zeros
+ * (the shader divides by a zero sum); a context longer than max_blocks * 16 is cut there (the
+ * shader would read past its table row). */
+int tk_paged_attention(tk_device *dev, const float *q, const float *k_cache, const float *v_cache,
+                       const int32_t *block_tables, const int32_t *context_lens, float *o,
+                       uint32_t batch, uint32_t num_heads, uint32_t head_dim, uint32_t max_blocks);
+int tk_paged_attention_async(tk_device *dev, const float *q, const float *k_cache,
+                             const float *v_cache, const int32_t *block_tables,
+                             const int32_t *context_lens, float *o, uint32_t batch,
+                             uint32_t num_heads, uint32_t head_dim, uint32_t max_blocks,
+                             void *stream);
+
 /* ---- sampler ----------------------------------------------------------------------------
  * Replaces the argmax shader (src/kernels/shaders.zig:889-943; the host loop of
  * src/model/llama.zig:290-303): out[0] = index of the largest of x[0..n).  Ties go to the smallest

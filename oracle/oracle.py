@@ -164,6 +164,34 @@ def q4_0_repack(blocks, n_rows: int, k: int, order: int = 0):
             np.full((k // 32, n_rows // 2), 0x88, dtype=np.uint8))
 
 
+def paged_attention_f64(q, k_cache, v_cache, block_tables, context_lens, batch: int,
+                        num_heads: int, head_dim: int, max_blocks: int) -> np.ndarray:
+    """paged_attention (src/kernels/shaders.zig:503-587) in f64: for sequence b, head h,
+    softmax(q . k_t * head_dim^-1/2) over tokens t < context_lens[b], weighting v_t; token t is
+    row t % 16 of physical block block_tables[b][t / 16] in caches [block][heads][16][head_dim].
+    An empty sequence gives zeros."""
+    B = 16
+    q = np.asarray(q, dtype=np.float64).reshape(batch, num_heads, head_dim)
+    kc = np.asarray(k_cache, dtype=np.float64).reshape(-1, num_heads, B, head_dim)
+    vc = np.asarray(v_cache, dtype=np.float64).reshape(-1, num_heads, B, head_dim)
+    bt = np.asarray(block_tables).reshape(batch, max_blocks)
+    out = np.zeros((batch, num_heads, head_dim))
+    scale = 1.0 / np.sqrt(head_dim)
+    for b in range(batch):
+        n = int(context_lens[b])
+        if n <= 0:
+            continue
+        t = np.arange(n)
+        phys = bt[b, t // B]
+        for h in range(num_heads):
+            K = kc[phys, h, t % B]
+            V = vc[phys, h, t % B]
+            s = K @ q[b, h] * scale
+            p = np.exp(s - s.max())
+            out[b, h] = (p / p.sum()) @ V
+    return out
+
+
 def argmax_ref(x) -> int:
     """Index of the largest value, the smallest index on ties (numpy's argmax)."""
     return int(np.argmax(np.asarray(x, dtype=np.float64)))

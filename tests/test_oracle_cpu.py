@@ -174,3 +174,21 @@ def test_sampler_oracle():
     assert oracle.sample_index(p, p[0] + 1e-9) == 1
     assert oracle.sample_index(p, 1.5) == 2
     assert oracle.argmax_ref([3.0, 5.0, 5.0, 1.0]) == 1
+
+
+def test_paged_attention_oracle_small():
+    """The f64 restatement against a direct loop over tokens on a tiny case."""
+    rng = np.random.default_rng(9)
+    H, D, MB = 2, 4, 3
+    q = rng.standard_normal((1, H, D))
+    kc = rng.standard_normal((MB, H, 16, D))
+    vc = rng.standard_normal((MB, H, 16, D))
+    bt = np.array([[2, 0, 1]], dtype=np.int32)
+    n = 20
+    got = oracle.paged_attention_f64(q, kc, vc, bt, [n], 1, H, D, MB)
+    for h in range(H):
+        ks = np.array([kc[bt[0, t // 16], h, t % 16] for t in range(n)])
+        vs = np.array([vc[bt[0, t // 16], h, t % 16] for t in range(n)])
+        s = ks @ q[0, h] / np.sqrt(D)
+        w = np.exp(s - s.max())
+        assert np.allclose(got[0, h], (w / w.sum()) @ vs)

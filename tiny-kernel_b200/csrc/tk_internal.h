@@ -59,6 +59,10 @@ struct P2PParams {
 cudaError_t launch_p2p_allreduce(const P2PParams& p, cudaStream_t st);
 cudaError_t launch_repack_q4_0(const uint8_t* blocks, uint8_t* w, uint16_t* s, uint8_t* z, int N,
                                int K, int order, cudaStream_t st);
+cudaError_t launch_paged_attention(const float* q, const float* kc, const float* vc,
+                                   const int* block_tables, const int* context_lens, float* o,
+                                   int batch, int num_heads, int head_dim, int max_blocks,
+                                   float scale, cudaStream_t st);
 cudaError_t launch_argmax(const float* x, int n, unsigned* out, cudaStream_t st);
 cudaError_t launch_softmax_sample(const float* logits, float* probs, unsigned* sampled, int n,
                                   float temperature, float random_val, cudaStream_t st);

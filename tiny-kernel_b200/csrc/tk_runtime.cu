@@ -907,6 +907,30 @@ int tk_repack_q4_0(tk_device* d, const void* blocks, uint8_t* w, uint16_t* s, ui
   return sync_and_check(d, d->stream);
 }
 
+int tk_paged_attention_async(tk_device* d, const float* q, const float* kc, const float* vc,
+                             const int32_t* bt, const int32_t* cl, float* o, uint32_t batch,
+                             uint32_t heads, uint32_t head_dim, uint32_t max_blocks, void* stream) {
+  if (!d || !q || !kc || !vc || !bt || !cl || !o) return fail(TK_ERR_ARG, "NULL argument");
+  if (batch == 0 || heads == 0 || head_dim == 0 || head_dim > 128 || max_blocks == 0 ||
+      batch > 65535 || heads > (1u << 20))
+    return fail(TK_ERR_ARG, "paged attention needs batch, heads, max_blocks > 0 and head_dim <= 128");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_LAUNCH(d, launch_paged_attention(q, kc, vc, bt, cl, o, (int)batch, (int)heads, (int)head_dim,
+                                      (int)max_blocks, 1.0f / sqrtf((float)head_dim),
+                                      pick_stream(d, stream)));
+  return TK_OK;
+}
+
+int tk_paged_attention(tk_device* d, const float* q, const float* kc, const float* vc,
+                       const int32_t* bt, const int32_t* cl, float* o, uint32_t batch,
+                       uint32_t heads, uint32_t head_dim, uint32_t max_blocks) {
+  int st = tk_paged_attention_async(d, q, kc, vc, bt, cl, o, batch, heads, head_dim, max_blocks,
+                                    nullptr);
+  if (st != TK_OK) return st;
+  return sync_and_check(d, d->stream);
+}
+
 int tk_argmax_async(tk_device* d, const float* x, uint32_t n, uint32_t* out, void* stream) {
   if (!d || !x || !out) return fail(TK_ERR_ARG, "NULL argument");
   if (n == 0 || n > (1u << 30)) return fail(TK_ERR_ARG, "argmax length %u out of range", n);

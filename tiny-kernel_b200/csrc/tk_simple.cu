@@ -199,6 +199,84 @@ __global__ void __launch_bounds__(128) repack_q4_0_kernel(const uint8_t* __restr
   if ((n & 1) == 0) z[(size_t)kb * (N / 2) + n / 2] = 0x88;
 }
 
+// ---- paged decode attention (src/kernels/shaders.zig:503-587) -----------------------------
+// One CTA per (head, sequence), 8 warps; warp w takes the KV blocks w, w+8, ... of the sequence
+// (16 tokens each, through the block table) and keeps its own online softmax (running max, sum
+// of exponentials, 4 output dims per lane: d = lane + 32i); the CTA merges the 8 states.
+// Layout as the shader: q/o [batch][heads][head_dim], caches [block][heads][16][head_dim].
+constexpr int kKvBlock = 16;
+
+__global__ void __launch_bounds__(256) paged_attention_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    const int* __restrict__ block_tables, const int* __restrict__ context_lens,
+    float* __restrict__ o, int num_heads, int head_dim, int max_blocks, float scale) {
+  __shared__ float s_m[8], s_s[8];
+  __shared__ float s_acc[8][128];
+  const int head = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ctx = min(max(context_lens[b], 0), max_blocks * kKvBlock);  // the table's reach
+  const int nblocks = (ctx + kKvBlock - 1) / kKvBlock;
+  float qv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = lane + 32 * i;
+    qv[i] = d < head_dim ? q[((size_t)b * num_heads + head) * head_dim + d] : 0.f;
+  }
+  float m = -INFINITY, sum = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int blk = warp; blk < nblocks; blk += 8) {
+    const int phys = block_tables[(size_t)b * max_blocks + blk];
+    const size_t base = ((size_t)phys * num_heads + head) * kKvBlock * head_dim;
+    const int ntok = min(kKvBlock, ctx - blk * kKvBlock);
+    for (int t0 = 0; t0 < ntok; t0 += 4) {
+      float kv[4][4], vv[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int d = lane + 32 * i;
+          const bool in = t0 + j < ntok && d < head_dim;
+          const size_t off = base + (size_t)(t0 + j) * head_dim + d;
+          kv[j][i] = in ? kc[off] : 0.f;
+          vv[j][i] = in ? vc[off] : 0.f;
+        }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (t0 + j >= ntok) break;
+        float sc = qv[0] * kv[j][0] + qv[1] * kv[j][1] + qv[2] * kv[j][2] + qv[3] * kv[j][3];
+        for (int off = 16; off > 0; off >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+        sc *= scale;
+        const float nm = fmaxf(m, sc);
+        const float f = expf(m - nm), pr = expf(sc - nm);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] = acc[i] * f + pr * vv[j][i];
+        sum = sum * f + pr;
+        m = nm;
+      }
+    }
+  }
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_s[warp] = sum;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (lane + 32 * i < 128) s_acc[warp][lane + 32 * i] = acc[i];
+  __syncthreads();
+  if (threadIdx.x < head_dim) {
+    const int d = threadIdx.x;
+    float M = -INFINITY;
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, s_m[w]);
+    float S = 0.f, A = 0.f;
+    if (M != -INFINITY)
+      for (int w = 0; w < 8; ++w) {
+        const float f = s_m[w] == -INFINITY ? 0.f : expf(s_m[w] - M);
+        S += s_s[w] * f;
+        A += s_acc[w][d] * f;
+      }
+    o[((size_t)b * num_heads + head) * head_dim + d] = S > 0.f ? A / S : 0.f;  // empty context: 0
+  }
+}
+
 // ---- sampler (src/kernels/shaders.zig:826-943) -------------------------------------------
 // One CTA of 1024 threads; vocabularies are small next to the weights (128K f32 = 512 KB).
 constexpr int kSampleThreads = 1024;
@@ -436,6 +514,15 @@ cudaError_t launch_repack_q4_0(const uint8_t* blocks, uint8_t* w, uint16_t* s, u
                                int K, int order, cudaStream_t st) {
   const dim3 grid((unsigned)((N + 127) / 128), (unsigned)(K / 32));
   repack_q4_0_kernel<<<grid, 128, 0, st>>>(blocks, w, s, z, N, K, order);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_attention(const float* q, const float* kc, const float* vc,
+                                   const int* block_tables, const int* context_lens, float* o,
+                                   int batch, int num_heads, int head_dim, int max_blocks,
+                                   float scale, cudaStream_t st) {
+  paged_attention_kernel<<<dim3((unsigned)num_heads, (unsigned)batch), 256, 0, st>>>(
+      q, kc, vc, block_tables, context_lens, o, num_heads, head_dim, max_blocks, scale);
   return cudaGetLastError();
 }
 

@@ -80,6 +80,8 @@ SIGNATURES = {
     "tk_matvec_dual": (i32, [vp, vp, vp, vp, vp, vp, u32, u32]),
     "tk_matvec_dual_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, vp]),
     "tk_repack_q4_0": (i32, [vp, vp, vp, vp, vp, u32, u32, i32]),
+    "tk_paged_attention": (i32, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),
+    "tk_paged_attention_async": (i32, [vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
     "tk_argmax": (i32, [vp, vp, u32, vp]),
     "tk_argmax_async": (i32, [vp, vp, u32, vp, vp]),
     "tk_softmax_sample": (i32, [vp, vp, vp, vp, u32, f32, f32]),

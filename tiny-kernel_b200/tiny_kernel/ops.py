@@ -126,6 +126,15 @@ def repack_q4_0(device, blocks, w_packed, scales, zeros, n_rows, k, order=0):
                                     _ptr(zeros), int(n_rows), int(k), int(order)))
 
 
+def paged_attention(device, q, k_cache, v_cache, block_tables, context_lens, o, batch,
+                    num_heads, head_dim, max_blocks):
+    """PagedAttention.forward (attention.zig:51-100): decode attention over block-tabled caches."""
+    check(_lib.lib().tk_paged_attention(_dev(device), _ptr(q), _ptr(k_cache), _ptr(v_cache),
+                                        _ptr(block_tables), _ptr(context_lens), _ptr(o),
+                                        int(batch), int(num_heads), int(head_dim),
+                                        int(max_blocks)))
+
+
 def argmax(device, x, n, out):
     """out[0] = index of the largest of x[0..n) (ties: the smallest index)."""
     check(_lib.lib().tk_argmax(_dev(device), _ptr(x), int(n), _ptr(out)))
