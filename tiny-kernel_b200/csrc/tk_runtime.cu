@@ -94,6 +94,7 @@ struct tk_device {
   // batch >= 16 GEMM path: f16 activations, f16 h, split-K partials
   ScratchBuf g_x16, g_h16, g_part;
   int gemm_enabled = 1;  // TK_GEMM=0 routes every batch through the engine
+  int engine_ctas = 0;    // TK_ENGINE_CTAS: CTAs of the engine's launches (0: one per SM)
   int down_prefetch = 1;  // TK_DOWN_PREFETCH=0 turns off the L2 prefetch of the down projection
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   unsigned long long launches = 0;      // kernels enqueued through this device
@@ -101,6 +102,27 @@ struct tk_device {
 };
 
 namespace {
+
+// CTAs of an engine launch: one per SM unless overridden (TK_ENGINE_CTAS).
+int engine_grid(const tk_device* d) {
+  return d->engine_ctas > 0 && d->engine_ctas < d->sm_count ? d->engine_ctas : d->sm_count;
+}
+
+// CTAs of an FFN launch.  A small FFN (a tensor-parallel shard: under ~60 MB of packed weights)
+// is bound by its split-K reduction chains rather than by streaming; there, the largest CTA count
+// (>= 60 % of the SMs) that divides the down projection's (column tile, group) items gives every
+// CTA whole groups, so no group's item is split between CTAs -- measured per FFN step at hidden
+// 4096 on B200: inter 7168 36.1 -> 33.5 us, 3584 31.2 -> 27.9 us, 1792 30.8 -> 24.4 us (112 CTAs);
+// the whole 8B FFN keeps one CTA per SM.
+int ffn_engine_ctas(const tk_device* d, int hidden, int inter, int gs) {
+  if (d->engine_ctas > 0) return engine_grid(d);
+  const int sm = d->sm_count;
+  if (1.5 * (double)hidden * (double)inter >= 60e6) return sm;
+  const long long items = (long long)((hidden + kWideCols - 1) / kWideCols) * (inter / gs);
+  for (int c = sm; c * 10 >= sm * 6; --c)
+    if (items % c == 0) return c;
+  return sm;
+}
 
 int set_device(tk_device* d) {
   TK_CUDA_TRY(cudaSetDevice(d->ordinal));
@@ -281,11 +303,12 @@ int bind_partials(tk_device* d, EngineParams& p, int first, int count, int idx, 
   return TK_OK;
 }
 
-int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, cudaStream_t st) {
+int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, cudaStream_t st,
+                  int ctas) {
   int spg_max = 0, fb_max = 0;
   for (int q = 0; q < p.nphases; ++q) {
     // the kernel's stream-K arithmetic is 32-bit
-    if (p.ph[q].units * (long long)d->sm_count >= (1LL << 31))
+    if (p.ph[q].units * (long long)ctas >= (1LL << 31))
       return fail(TK_ERR_UNSUPPORTED, "phase of %lld work units is too large for one launch",
                   p.ph[q].units);
     spg_max = std::max(spg_max, p.ph[q].spg);
@@ -316,7 +339,7 @@ int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, c
   int blocks = 0;
   TK_CUDA_TRY(engine_occupancy(mt, p.gs0, smem, &blocks));
   if (blocks < 1) return fail(TK_ERR_UNSUPPORTED, "engine kernel cannot be resident");
-  TK_LAUNCH(d, engine_launch(mt, p.gs0, maps, p, d->sm_count, smem, st));
+  TK_LAUNCH(d, engine_launch(mt, p.gs0, maps, p, ctas, smem, st));
   return TK_OK;
 }
 
@@ -330,7 +353,7 @@ int qmatmul_engine_chunk(tk_device* d, const float* x, const uint8_t* w, const u
                          const uint8_t* z, float* out, int m, int k, int n, int gs,
                          cudaStream_t st) {
   const int mt = mt_for(m);
-  const long long Wtot = d->sm_count;  // one CTA per SM; stream-K ranges are per CTA
+  const long long Wtot = engine_grid(d);  // one CTA per SM; stream-K ranges are per CTA
   EngineParams p;
   std::memset(&p, 0, sizeof(p));
   p.m = m;
@@ -362,7 +385,7 @@ int qmatmul_engine_chunk(tk_device* d, const float* x, const uint8_t* w, const u
   std::memset(&maps, 0, sizeof(maps));
   stt = matrix_tmaps(d, w, n, k, gs, maps, 0);
   if (stt != TK_OK) return stt;
-  return launch_engine(d, mt, maps, p, st);
+  return launch_engine(d, mt, maps, p, st, (int)Wtot);
 }
 
 int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk_int4_matrix* gate,
@@ -370,7 +393,7 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
                      float* h_out, int m, int hidden, int inter, int gs, float eps, bool residual,
                      cudaStream_t st) {
   const int mt = mt_for(m);
-  const long long Wtot = d->sm_count;  // one CTA per SM; stream-K ranges are per CTA
+  const long long Wtot = ffn_engine_ctas(d, hidden, inter, gs);  // stream-K ranges are per CTA
   EngineParams p;
   std::memset(&p, 0, sizeof(p));
   p.m = m;
@@ -439,7 +462,7 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   if (stt != TK_OK) return stt;
   stt = matrix_tmaps(d, down->w_packed, hidden, inter, gs, maps, 4);
   if (stt != TK_OK) return stt;
-  return launch_engine(d, mt, maps, p, st);
+  return launch_engine(d, mt, maps, p, st, (int)Wtot);
 }
 
 // ---- batch >= 16: the tcgen05 GEMM path (tk_gemm.cu) ----------------------------------------
@@ -736,6 +759,7 @@ int tk_device_create(int ordinal, tk_device** out) {
   if (const char* env = std::getenv("TK_FFN_SPLIT")) d->ffn_split = std::atoi(env);
   if (const char* env = std::getenv("TK_GEMM")) d->gemm_enabled = std::atoi(env);
   if (const char* env = std::getenv("TK_DOWN_PREFETCH")) d->down_prefetch = std::atoi(env);
+  if (const char* env = std::getenv("TK_ENGINE_CTAS")) d->engine_ctas = std::atoi(env);
   if (const char* env = std::getenv("TK_WAIT_TIMEOUT_MS"))
     d->timeout_ns = (unsigned long long)std::atoll(env) * 1000000ull;
   if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
