@@ -75,3 +75,22 @@ def test_tp_group_id_and_argument_checks():
         == _lib.TK_ERR_ARG
     assert L.tk_tp_allreduce_sum_f32(None, None, 0, None) == _lib.TK_ERR_ARG
     L.tk_tp_destroy(None)  # no-op
+
+
+def test_tp_id_before_torch_import_keeps_torch_loadable():
+    """NCCL loaded by the tensor-parallel entry points before ``import torch`` is the copy torch
+    links against, so torch still imports (an older system libnccl.so.2 loaded first would leave
+    torch's libtorch_cuda.so with unresolved NCCL symbols)."""
+    import subprocess
+    import sys
+
+    pkg = os.path.dirname(os.path.dirname(os.path.abspath(_lib.__file__)))
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "from tiny_kernel import tp\n"
+            "assert len(tp.unique_id()) == 128\n"
+            "import torch\n"
+            "print('ok', torch.__version__)\n") % pkg
+    env = {k: v for k, v in os.environ.items() if k != "TK_NCCL_LIB"}
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
+                       timeout=600)
+    assert r.returncode == 0 and r.stdout.startswith("ok"), r.stderr[-2000:]

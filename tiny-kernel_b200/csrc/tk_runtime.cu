@@ -1367,8 +1367,15 @@ std::once_flag g_nccl_once;
 NcclApi g_nccl;
 
 int nccl_api(const NcclApi** out) {
+  // Which NCCL: TK_NCCL_LIB (a path) first, then a libnccl.so.2 the process already holds (a
+  // framework's own), then the loader's search.  All other code in the process that links
+  // libnccl.so.2 binds to whichever copy is loaded first, so an older system NCCL loaded here
+  // ahead of a framework's newer one would leave the framework's symbols unresolved.
   std::call_once(g_nccl_once, [] {
-    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    void* h = nullptr;
+    if (const char* lib = getenv("TK_NCCL_LIB"); lib && *lib) h = dlopen(lib, RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
     if (!h) return;
     g_nccl.get_unique_id = reinterpret_cast<decltype(g_nccl.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));

@@ -112,12 +112,36 @@ class TKError(RuntimeError):
 _lib = None
 
 
+def bundled_nccl() -> str | None:
+    """The libnccl.so.2 of the ``nvidia-nccl`` wheel that torch links against, if installed.
+
+    The tensor-parallel entry points load NCCL at their first call; a process holds one
+    libnccl.so.2, so loading an older system copy before ``import torch`` would leave torch's
+    newer NCCL symbols unresolved.  Pointing TK_NCCL_LIB at the wheel's copy keeps both on one.
+    """
+    import importlib.util
+
+    try:
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return None
+    for root in (spec.submodule_search_locations or []) if spec else []:
+        path = os.path.join(root, "lib", "libnccl.so.2")
+        if os.path.exists(path):
+            return path
+    return None
+
+
 def lib() -> C.CDLL:
     """The loaded library (raises OSError if it has not been built)."""
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise OSError(f"libtkcuda is not built: {LIB_PATH} (run `make -C tiny-kernel_b200`)")
+        if not os.environ.get("TK_NCCL_LIB"):
+            nccl = bundled_nccl()
+            if nccl:
+                os.environ["TK_NCCL_LIB"] = nccl
         handle = C.CDLL(LIB_PATH)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(handle, name)
