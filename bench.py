@@ -14,8 +14,9 @@ once: by rank 0's kernel, before the all-reduce).
 value     whole-job algorithmic GB/s: FFN bytes (weights + x + norm weight + out) per step
           x steps / max-over-ranks device time; inputs resident in HBM; L2 defeated by
           rotating several weight copies whose total exceeds 3x the L2 size.
-e2e       the same metric through the synchronous C ABI (tk_int4_ffn) with the activation
-          copied from pinned host memory and the output read back every step.
+e2e       the same metric through the C ABI with host buffers: every step queues the
+          activation's upload from pinned host memory, the FFN and the output's download on
+          the device's stream and waits once for the result (tk_device_synchronize).
 --impl reference  times the CPU transcription of the reference shaders (oracle/), all host
           threads, on the same workload (the reference itself is Zig + Metal and cannot run
           on this Linux host).
@@ -310,8 +311,10 @@ def main():
     # stacks carry the residual (added once, by rank 0's kernel, before the all-reduce)
     residual = L > 1 and (rank == 0 or group is not None)
 
-    def run_step(i, x_in, bufs, sync):
-        """One step: L blocks; returns the buffer that holds the step's output."""
+    def run_step(i, x_in, bufs, sync, on=None):
+        """One step: L blocks; returns the buffer that holds the step's output.  Without sync
+        the blocks are queued on `on` (a torch stream; default the bench's own stream)."""
+        on = stream if on is None else on
         cur = x_in
         for l in range(L):
             nw, g, u, d = mats[i % copies][l]
@@ -319,18 +322,18 @@ def main():
             if group is not None:
                 # shard FFN + the exchange, both inside the library
                 group.int4_ffn(cur, nw, g, u, d, out, m, hidden, inter, GS, eps=EPS,
-                               residual=residual, stream=None if sync else stream.cuda_stream,
+                               residual=residual, stream=None if sync else on.cuda_stream,
                                sync=sync)
                 cur = out
                 continue
             ops.int4_ffn(dev, cur, nw, g, u, d, out, m, hidden, inter, GS, eps=EPS,
-                         residual=residual, stream=None if sync else stream.cuda_stream, sync=sync)
+                         residual=residual, stream=None if sync else on.cuda_stream, sync=sync)
             if pg is not None:
                 if sync:
                     pg.all_reduce(out)
                     torch.cuda.current_stream().synchronize()
                 else:
-                    with torch.cuda.stream(stream):
+                    with torch.cuda.stream(on):
                         pg.all_reduce(out)
             cur = out
         return cur
@@ -400,7 +403,9 @@ def main():
     # the bound of the step: whichever of HBM bytes and tensor FLOPs takes longer at peak
     tensor_bound = per_gpu_flops / (peak_tc * 1e12) > per_gpu_bytes / (peak * 1e9)
 
-    # ---- end to end through the synchronous C ABI with host buffers -------------------
+    # ---- end to end through the C ABI with host buffers -------------------------------
+    # A user's step: the activation's upload, the FFN and the output's download queued on the
+    # device's stream, then one wait for the result (tk_device_synchronize), every step.
     import ctypes as C
     Lb = lib()
     xb_host = tk.Buffer(dev, "f32", m * hidden, kind=2)   # pinned host
@@ -409,20 +414,25 @@ def main():
               x_host.reshape(-1))
     xd = torch.empty((m, hidden), dtype=torch.float32, device="cuda")
     e2e_steps = max(1, min(steps_timed, 2000 // L))
+    devstream = torch.cuda.ExternalStream(dev.stream())
+
+    def e2e_step(i):
+        check(Lb.tk_buffer_upload_async(dev.handle, xd.data_ptr(), xb_host.ptr, xb_host.nbytes,
+                                        None))
+        res = run_step(i, xd, (xa, xb), False, on=devstream)
+        check(Lb.tk_buffer_download_async(dev.handle, ob_host.ptr, res.data_ptr(),
+                                          ob_host.nbytes, None))
+        check(Lb.tk_device_synchronize(dev.handle))
+
     for i in range(3):
-        check(Lb.tk_buffer_upload(dev.handle, xd.data_ptr(), xb_host.ptr, xb_host.nbytes))
-        res = run_step(i, xd, (xa, xb), True)
-        check(Lb.tk_buffer_download(dev.handle, ob_host.ptr, res.data_ptr(), ob_host.nbytes))
+        e2e_step(i)
     if pg is not None:
         pg.barrier()
     torch.cuda.synchronize()
-    devstream = torch.cuda.ExternalStream(dev.stream())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(devstream)
     for i in range(e2e_steps):
-        check(Lb.tk_buffer_upload(dev.handle, xd.data_ptr(), xb_host.ptr, xb_host.nbytes))
-        res = run_step(i, xd, (xa, xb), True)
-        check(Lb.tk_buffer_download(dev.handle, ob_host.ptr, res.data_ptr(), ob_host.nbytes))
+        e2e_step(i)
     e1.record(devstream)
     e1.synchronize()
     e2e_ms = e0.elapsed_time(e1)

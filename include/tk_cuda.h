@@ -104,6 +104,16 @@ int tk_buffer_free(tk_device *dev, void *ptr);
 /* Synchronous host<->device copies on the device's stream. */
 int tk_buffer_upload(tk_device *dev, void *dst_device, const void *src_host, size_t bytes);
 int tk_buffer_download(tk_device *dev, void *dst_host, const void *src_device, size_t bytes);
+/* The same copies queued on `stream` (NULL: the device's stream) without waiting, so a step can
+ * queue its upload, its kernels and its download and wait once (tk_device_synchronize): the
+ * reference encodes a step into one command buffer, commits it and waits once
+ * (CommandBuffer.commit / waitUntilCompleted, src/metal/device.zig:137-153).
+ * The host memory must stay valid until the copy has run; with pageable host memory the copy
+ * may be partly synchronous, with pinned memory (TK_MEM_HOST) it is not. */
+int tk_buffer_upload_async(tk_device *dev, void *dst_device, const void *src_host, size_t bytes,
+                           void *stream);
+int tk_buffer_download_async(tk_device *dev, void *dst_host, const void *src_device, size_t bytes,
+                             void *stream);
 
 /* ---- kernels --------------------------------------------------------------------- */
 

@@ -1,10 +1,11 @@
-"""GPU tests of the one-shot peer-memory all-reduce (tk_tp_allreduce_sum_f32), 2 GPUs.
+"""GPU tests of the one-shot peer-memory all-reduce (tk_tp_allreduce_sum_f32), 2 and 4 GPUs.
 
 Every rank generates every rank's input from the seed, so each can check the sum bit-exactly
 against the f32 sum in rank order (the order the kernel uses).  Covered: ragged and vector sizes
 up to the peer path's limit and one beyond it (NCCL), repeated calls (both buffer parities), a
 CUDA graph replayed with new inputs (the epochs live on the device), and a wait that runs out:
-rank 0 calls alone with a short bound and gets TK_ERR_TIMEOUT, no GPU fault.  Needs >= 2 GPUs.
+rank 0 calls alone with a short bound and gets TK_ERR_TIMEOUT, no GPU fault.  A case skips
+when the box has fewer GPUs than its ranks.
 """
 import os
 import sys
@@ -88,7 +89,7 @@ def _run(fn, world, *args):
     mp.start_processes(fn, args=(world,) + args, nprocs=world, join=True, start_method="spawn")
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_p2p_allreduce_bit_exact(torch_cuda, tmp_path, world):
     if torch_cuda.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")

@@ -67,3 +67,37 @@ def test_mirror_api_fused(tkdev):
     bo = tkdev.create_buffer("f32", n)
     tk.kernels.fused.FusedSiluMul.init(tkdev).forward(bg, bu, bo)
     assert oracle.normwise_err(bo.slice(), oracle.silu_mul_f64(g, u)) <= TOL
+
+
+@pytest.mark.parametrize("nbytes", [0, 4, 4096 + 12, 1 << 20])
+def test_async_buffer_copies_round_trip(torch_cuda, tkdev, nbytes):
+    """tk_buffer_upload_async / tk_buffer_download_async: bytes queued on the device's stream
+    (NULL) and on a caller's stream come back unchanged after one wait."""
+    import ctypes as C
+
+    import tiny_kernel as tk
+    from tiny_kernel import _lib
+    L = _lib.lib()
+    torch = torch_cuda
+    src = np.random.default_rng(nbytes).integers(0, 256, size=max(nbytes, 1), dtype=np.uint8)
+    hin = tk.Buffer(tkdev, "u8", max(nbytes, 1), kind=_lib.TK_MEM_HOST)
+    hout = tk.Buffer(tkdev, "u8", max(nbytes, 1), kind=_lib.TK_MEM_HOST)
+    view_in = np.frombuffer((C.c_char * hin.nbytes).from_address(hin.ptr), np.uint8)
+    view_out = np.frombuffer((C.c_char * hout.nbytes).from_address(hout.ptr), np.uint8)
+    view_in[:] = src
+    d = torch.empty(max(nbytes, 1), dtype=torch.uint8, device="cuda")
+    side = torch.cuda.Stream()
+    try:
+        for stream in (None, side.cuda_stream):
+            view_out[:] = 0
+            _lib.check(L.tk_buffer_upload_async(tkdev.handle, d.data_ptr(), hin.ptr, nbytes, stream))
+            _lib.check(L.tk_buffer_download_async(tkdev.handle, hout.ptr, d.data_ptr(), nbytes,
+                                                  stream))
+            if stream is None:
+                _lib.check(L.tk_device_synchronize(tkdev.handle))
+            else:
+                side.synchronize()
+            assert np.array_equal(view_out[:nbytes], src[:nbytes])
+    finally:
+        hin.deinit()
+        hout.deinit()

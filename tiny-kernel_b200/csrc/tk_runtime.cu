@@ -886,6 +886,22 @@ int tk_buffer_download(tk_device* d, void* dst, const void* src, size_t bytes) {
   return TK_OK;
 }
 
+int tk_buffer_upload_async(tk_device* d, void* dst, const void* src, size_t bytes, void* stream) {
+  if (!d || (!dst && bytes) || (!src && bytes)) return fail(TK_ERR_ARG, "NULL argument");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, pick_stream(d, stream)));
+  return TK_OK;
+}
+
+int tk_buffer_download_async(tk_device* d, void* dst, const void* src, size_t bytes, void* stream) {
+  if (!d || (!dst && bytes) || (!src && bytes)) return fail(TK_ERR_ARG, "NULL argument");
+  int st = set_device(d);
+  if (st != TK_OK) return st;
+  TK_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, pick_stream(d, stream)));
+  return TK_OK;
+}
+
 int tk_matvec_dual_async(tk_device* d, const float* x, const float* W1, const float* W2, float* out1,
                          float* out2, uint32_t K, uint32_t N, void* stream) {
   if (!d || !x || !W1 || !out1) return fail(TK_ERR_ARG, "NULL argument");

@@ -58,6 +58,8 @@ SIGNATURES = {
     "tk_buffer_free": (i32, [vp, vp]),
     "tk_buffer_upload": (i32, [vp, vp, vp, C.c_size_t]),
     "tk_buffer_download": (i32, [vp, vp, vp, C.c_size_t]),
+    "tk_buffer_upload_async": (i32, [vp, vp, vp, C.c_size_t, vp]),
+    "tk_buffer_download_async": (i32, [vp, vp, vp, C.c_size_t, vp]),
     "tk_qmatmul_int4": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32]),
     "tk_qmatmul_int4_async": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
     "tk_qmatmul_int4_path": (i32, [u32, u32, u32, u32]),
