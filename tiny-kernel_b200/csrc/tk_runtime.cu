@@ -12,6 +12,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -71,6 +72,7 @@ struct TmapEntry {
 };
 
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // 2 s per bounded wait
+constexpr unsigned kErrHostSlots = 64;  // synchronising calls in flight at once on one device
 // shared memory the engine kernel declares statically (phase table, job queues, barriers)
 constexpr int kStaticSmemReserve = 4096;
 
@@ -88,6 +90,10 @@ struct tk_device {
   int ffn_split = 1;  // gate/up tile ranges of the FFN (TK_FFN_SPLIT, 1..4)
   SyncState* sync = nullptr;
   unsigned* err = nullptr;
+  // Pinned host copies of the error word, one slot per synchronising call (a ring), so that the
+  // word's read is queued behind the call's work and one wait covers both.
+  unsigned* err_host = nullptr;
+  std::atomic<unsigned> err_slot{0};
   ScratchBuf frag[1];      // per-CTA prologue records when they do not fit in shared memory
   ScratchBuf partials[2];  // split-K partial sums: [0] first reduction, [1] second
   ScratchBuf counters[2];  // segment counters per 128-column sub-tile of each
@@ -344,8 +350,14 @@ int launch_engine(tk_device* d, int mt, const TmapPack& maps, EngineParams& p, c
 }
 
 int sync_and_check(tk_device* d, cudaStream_t st) {
+  // The error word is copied on `st` behind the work, so the one wait also brings the word back
+  // (a separate synchronous read would be a second round trip on every synchronous call).
+  volatile unsigned* slot = d->err_host + d->err_slot.fetch_add(1u) % kErrHostSlots;
+  TK_CUDA_TRY(cudaMemcpyAsync(const_cast<unsigned*>(slot), d->err, sizeof(unsigned),
+                              cudaMemcpyDeviceToHost, st));
   TK_CUDA_TRY(cudaStreamSynchronize(st));
-  return tk_device_check_error(d);
+  if (*slot == 0) return TK_OK;
+  return tk_device_check_error(d);  // reads the word again, reports it and clears the state
 }
 
 // One engine launch for <= 4 rows of qmatmul_int4.
@@ -765,7 +777,9 @@ int tk_device_create(int ordinal, tk_device** out) {
   if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
     return cleanup(fail(TK_ERR_CUDA, "cudaStreamCreate failed"));
   if (cudaMalloc(&d->sync, sizeof(SyncState)) != cudaSuccess ||
-      cudaMalloc(&d->err, 256) != cudaSuccess)
+      cudaMalloc(&d->err, 256) != cudaSuccess ||
+      cudaHostAlloc(&d->err_host, kErrHostSlots * sizeof(unsigned), cudaHostAllocDefault) !=
+          cudaSuccess)
     return cleanup(fail(TK_ERR_NOMEM, "scratch allocation failed"));
   if (cudaMemset(d->sync, 0, sizeof(SyncState)) != cudaSuccess || cudaMemset(d->err, 0, 256) != cudaSuccess)
     return cleanup(fail(TK_ERR_CUDA, "scratch init failed"));
@@ -782,6 +796,7 @@ void tk_device_destroy(tk_device* d) {
     if (b->ptr) cudaFree(b->ptr);
   if (d->sync) cudaFree(d->sync);
   if (d->err) cudaFree(d->err);
+  if (d->err_host) cudaFreeHost(d->err_host);
   if (d->trace) cudaFree(d->trace);
   if (d->stream) cudaStreamDestroy(d->stream);
   delete d;
