@@ -1,7 +1,8 @@
 """GPU tests of the one-shot peer-memory all-reduce (tk_tp_allreduce_sum_f32), 2 and 4 GPUs.
 
 Every rank generates every rank's input from the seed, so each can check the sum bit-exactly
-against the f32 sum in rank order (the order the kernel uses).  Covered: ragged and vector sizes
+against the f32 sum in rank order (the order the kernel uses); the size beyond the peer path's
+limit goes to NCCL, checked bit-exactly at 2 ranks and within f32 rounding from 3 on.  Covered: ragged and vector sizes
 up to the peer path's limit and one beyond it (NCCL), repeated calls (both buffer parities), a
 CUDA graph replayed with new inputs (the epochs live on the device), and a wait that runs out:
 rank 0 calls alone with a short bound and gets TK_ERR_TIMEOUT, no GPU fault.  A case skips
@@ -16,6 +17,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 SIZES = [1, 3, 4, 511, 512, 513, 4096, 65536 + 7, 262144, 262144 + 4]
+PEER_MAX_FLOATS = 512 * 512  # the peer path's limit (512 chunks of 512 floats); NCCL beyond it
 
 
 def _setup(rank):
@@ -38,6 +40,17 @@ def _expect(xs):
     return v
 
 
+def _matches(got, xs):
+    """The peer path sums in rank order: bit-exact.  Beyond its limit NCCL reduces, whose order
+    is its own from 3 ranks on (with 2, a + b is the same either way): within the f32 rounding
+    of a sum in any order, (ranks - 1) * eps * sum |x_r| per element."""
+    exp = _expect(xs)
+    if len(xs) <= 2 or got.size <= PEER_MAX_FLOATS:
+        return np.array_equal(got, exp)
+    bound = (len(xs) - 1) * np.finfo(np.float32).eps * np.sum(np.abs(np.stack(xs)), axis=0)
+    return bool(np.all(np.abs(got.astype(np.float64) - exp) <= bound))
+
+
 def _rank_sum(rank, world, uid, result_path):
     _setup(rank)
     import torch
@@ -57,7 +70,7 @@ def _rank_sum(rank, world, uid, result_path):
                 buf = torch.from_numpy(xs[rank]).cuda()
                 g.allreduce_sum(buf, n)
                 dev.synchronize()
-                if not np.array_equal(buf.cpu().numpy(), _expect(xs)):
+                if not _matches(buf.cpu().numpy(), xs):
                     bad.append((it, n))
         # CUDA graph: the all-reduce captured once, replayed with new inputs
         n = 4096
