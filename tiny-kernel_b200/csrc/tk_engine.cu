@@ -45,6 +45,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "tk_engine.h"
 #include "tk_ptx.cuh"
 
@@ -1528,13 +1530,36 @@ bool engine_plan_smem(int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes,
   return false;
 }
 
+// The shared-memory attribute and the occupancy query cost host time ahead of every launch, so
+// they are redone only when an instantiation is launched on a device with another shared-memory
+// size than its last one (the attribute always holds the size of the latest launch).
 cudaError_t engine_occupancy(int mt, int gs, size_t smem, int* blocks) {
-  switch (mt) {
-    case 1: return occupancy_gs<1>(gs, smem, blocks);
-    case 2: return occupancy_gs<2>(gs, smem, blocks);
-    case 4: return occupancy_gs<4>(gs, smem, blocks);
-    default: return cudaErrorInvalidValue;
+  constexpr int kMaxDevices = 64;
+  struct Last {
+    size_t smem;
+    int blocks;
+  };
+  static std::mutex mu;
+  static Last last[kMaxDevices][3][4] = {};  // [device][MT 1, 2, 4][GS 16, 32, 64, 128]
+  const int mi = mt == 1 ? 0 : mt == 2 ? 1 : mt == 4 ? 2 : -1;
+  const int gi = gs == 16 ? 0 : gs == 32 ? 1 : gs == 64 ? 2 : gs == 128 ? 3 : -1;
+  if (mi < 0 || gi < 0) return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  Last* L = dev >= 0 && dev < kMaxDevices ? &last[dev][mi][gi] : nullptr;
+  if (L && L->blocks > 0 && L->smem == smem) {
+    *blocks = L->blocks;
+    return cudaSuccess;
   }
+  switch (mt) {
+    case 1: e = occupancy_gs<1>(gs, smem, blocks); break;
+    case 2: e = occupancy_gs<2>(gs, smem, blocks); break;
+    default: e = occupancy_gs<4>(gs, smem, blocks); break;
+  }
+  if (L) *L = (e == cudaSuccess) ? Last{smem, *blocks} : Last{0, 0};
+  return e;
 }
 
 cudaError_t engine_launch(int mt, int gs, const TmapPack& maps, const EngineParams& p, int grid,
