@@ -29,6 +29,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "tk_engine.h"
 #include "tk_gemm.h"
 #include "tk_ptx.cuh"
@@ -648,11 +650,31 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// The dynamic shared-memory attribute of instantiation `slot` (0-2: tensor-memory kernel at 16,
+// 32, 64 tokens; 3-4: shared-memory kernel at 128, 256), set again only when it is launched on a
+// device with another size than its last launch there: the call costs host time ahead of every
+// launch otherwise.
+cudaError_t set_smem_attr(const void* kern, int slot, size_t smem) {
+  constexpr int kMaxDevices = 64, kSlots = 5;
+  static std::mutex mu;
+  static size_t last[kMaxDevices][kSlots] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t* L = dev >= 0 && dev < kMaxDevices ? &last[dev][slot] : nullptr;
+  if (L && *L == smem) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (L) *L = e == cudaSuccess ? smem : 0;
+  return e;
+}
+
 template <int NT>
 cudaError_t launch_tm(const GemmMaps& maps, const GemmParams& p, dim3 grid, size_t smem,
                       cudaStream_t st) {
   auto kern = int4_gemm_tm_kernel<NT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = set_smem_attr(reinterpret_cast<const void*>(kern), NT == 16 ? 0 : NT == 32 ? 1 : 2,
+                                smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kGemmTmThreads, smem, st>>>(maps, p);
   return cudaGetLastError();
@@ -662,7 +684,7 @@ template <int NT>
 cudaError_t launch_nt(const GemmMaps& maps, const GemmParams& p, dim3 grid, size_t smem,
                       cudaStream_t st) {
   auto kern = int4_gemm_kernel<NT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = set_smem_attr(reinterpret_cast<const void*>(kern), NT == 128 ? 3 : 4, smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kGemmThreads, smem, st>>>(maps, p);
   return cudaGetLastError();
