@@ -27,6 +27,21 @@
  *    The *_async variants enqueue on the given CUDA stream (NULL = the device's
  *    stream) and return immediately.
  *  - f16 scales are passed as raw IEEE binary16 bit patterns (uint16_t).
+ *  - The library caches per-device state for the life of the process (kernel attributes, the
+ *    allocation-free entry point's scratch address): cudaDeviceReset while it is loaded is not
+ *    supported.
+ *
+ * Environment (read once, at tk_device_create; for tuning and tests, none is needed):
+ *   TK_WAIT_TIMEOUT_MS  bound of every device-side wait (default 2000); a wait that runs out
+ *                       reports TK_ERR_TIMEOUT
+ *   TK_GEMM=0           route every batch through the streaming engine (no tcgen05 GEMM)
+ *   TK_ENGINE_CTAS      CTAs of the streaming engine's launches (default: one per SM; smaller
+ *                       FFN shards take a divisor of their work, see tk_int4_ffn)
+ *   TK_ENGINE_STAGES    cap on the engine's shared-memory ring depth (default: deepest fit)
+ *   TK_FFN_SPLIT        gate/up tile ranges of the engine's FFN, 1..4 (default 1)
+ *   TK_DOWN_PREFETCH=0  no L2 prefetch of the down projection at the gate/up -> down switch
+ *   TK_TP_NCCL=1        tk_tp groups use NCCL for every exchange (read at tk_tp_create)
+ *   TK_NCCL_LIB         path of the libnccl.so.2 the tk_tp_* calls load
  *
  * INT4 weight layout (identical to qmatmul_int4, src/kernels/shaders.zig:442-501):
  *   w_packed u8 [K/2][N]          byte (k/2)*N + n; even k = low nibble, odd k = high nibble
@@ -121,8 +136,11 @@ int tk_buffer_download_async(tk_device *dev, void *dst_host, const void *src_dev
  * x f32 [m][k], out f32 [m][n].  The reference computes row 0 only and requires
  * k <= 4096; this entry point computes all m rows and any k with k % group_size == 0,
  * group_size % 8 == 0, n even.  Shapes with n % 128 == 0, k % 128 == 0 and
- * group_size in {16, 32, 64, 128} run the TMA-fed tensor-core GEMV engine; other
- * legal shapes run a plain CUDA-core kernel. */
+ * group_size in {16, 32, 64, 128} (16-byte aligned pointers) run the TMA-fed streaming
+ * engine up to 15 rows -- dp2a on the CUDA cores against activations quantised to int16 per
+ * group at 1-2 rows, int8 tensor-core MMAs (mma.sync) against int8 hi/lo activation parts at
+ * 3-4 rows, chunks of 4 rows beyond -- and the tcgen05 dequant-to-f16 GEMM from 16 rows
+ * (tk_qmatmul_int4_path); other legal shapes run a plain CUDA-core kernel. */
 int tk_qmatmul_int4(tk_device *dev, const float *x, const uint8_t *w_packed,
                     const uint16_t *scales, const uint8_t *zeros, float *out, uint32_t m,
                     uint32_t k, uint32_t n, uint32_t group_size);
@@ -204,7 +222,10 @@ int tk_int4_ffn_tp_async(tk_tp *tp, const float *x, const float *norm_weight,
  * 262144 floats it is a one-shot all-reduce over NVLink peer memory (the ranks map one another's
  * receive areas at tk_tp_create; sums in rank order, so every rank gets the same bits; bounded
  * waits report TK_ERR_TIMEOUT through tk_device_check_error); larger buffers, or groups where a
- * rank could not map its peers, or TK_TP_NCCL=1 in the environment, use NCCL. */
+ * rank could not map its peers, or TK_TP_NCCL=1 in the environment, use NCCL.  Once a peer wait
+ * of the device has run out (reported by tk_device_check_error or a synchronous call), a group
+ * using peer memory refuses further exchanges with TK_ERR_TIMEOUT: its ranks' chunk epochs are
+ * out of step, so it must be destroyed and created again. */
 int tk_tp_allreduce_sum_f32(tk_tp *tp, float *buf, size_t count, void *stream);
 /* 1 when the group uses the peer-memory all-reduce, 0 when NCCL carries every exchange. */
 int tk_tp_uses_p2p(tk_tp *tp);
@@ -298,15 +319,21 @@ int tk_device_trace_read(tk_device *dev, uint64_t *out, size_t max_values, size_
  *
  * For callers that cannot call cudaMalloc: a process whose device memory is reserved up
  * front by its own allocator, a latency-critical loop that must not take cudaMalloc's
- * device-wide synchronisation, or a binding that cannot own a tk_device.  Same contract
- * as tk_qmatmul_int4 (same layout, shapes, errors and results), on the calling thread's
- * current CUDA device and on `stream` (NULL = the legacy default stream), synchronous.
+ * device-wide synchronisation, or a binding that cannot own a tk_device.  Same layout, shapes
+ * and errors as tk_qmatmul_int4, on the calling thread's current CUDA device and on `stream`
+ * (NULL = the legacy default stream).
+ *  - Synchronous: it waits for its work and reads the error word back before it returns, so
+ *    it cannot be recorded into a CUDA graph.
+ *  - Results are within the path's tolerance of tk_qmatmul_int4's, not always identical: every
+ *    row count runs the streaming engine in chunks of 4 rows (m >= 16 does not take the
+ *    tensor-core GEMM), and shapes the engine does not take run the CUDA-core kernel.
+ *  - Its bounded device-side waits give up after a fixed 2 s (TK_WAIT_TIMEOUT_MS is not read).
  * It allocates nothing: the engine's scratch is one static device array of
  * TK_NOALLOC_SCRATCH_BYTES per GPU that loads the library, held until the process exits.
  *  - A shape whose scratch would exceed that size fails with TK_ERR_ARG (config 0,
  *    m=1 k=4096 n=14336 group 64, needs about 3.5 MB); use tk_qmatmul_int4 for those.
- *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
- *    make that first call before any stream capture.
+ *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *    and keeps it for the life of the process (cudaDeviceReset is not supported afterwards).
  *  - Every call shares the one array and clears its counters on entry: calls that overlap
  *    on the GPU (other threads, other streams) race and must be serialised by the caller. */
 #define TK_NOALLOC_SCRATCH_BYTES (4u << 20)

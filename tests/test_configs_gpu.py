@@ -1,0 +1,125 @@
+"""GPU parity at the shapes of the larger workloads: the Llama-3-70B FFN (hidden 8192,
+intermediate 28672, the down projection's K = 28672) and decode stacks of residual FFN blocks.
+
+Reference semantics: qmatmul_int4 (src/kernels/shaders.zig:442-501) composed into the FFN as in
+src/bench.zig:266-341 plus the down projection, and the decode layer loop of
+src/model/llama.zig:220-231 (x <- x + FFN(rmsnorm(x))) over several blocks with their own weights.
+Every case is compared with the f64 oracle; the bar is the path's contract, normwise max error
+1e-3 (TOL), and the precision each path holds (ENGINE_PRECISION for the streaming engine at 1-4
+rows, GEMM_PRECISION for the tcgen05 GEMM from 16 rows).
+"""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import dev, host, mat_dev
+from tiny_kernel import data, ops
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+ENGINE_PRECISION = 7e-4
+GEMM_PRECISION = 8e-4
+EPS = 1e-5
+
+
+def _bar(path):
+    return GEMM_PRECISION if path == 2 else ENGINE_PRECISION
+
+
+@pytest.mark.parametrize("m,K,N", [
+    (1, 8192, 28672),    # 70B gate/up, batch 1: streaming engine
+    (32, 8192, 28672),   # 70B gate/up, batch 32: tcgen05 GEMM
+    (1, 28672, 8192),    # 70B down (K = 28672), batch 1
+    (32, 28672, 8192),   # 70B down, batch 32
+])
+def test_qmatmul_70b_shapes(torch_cuda, tkdev, m, K, N):
+    torch = torch_cuda
+    gs = 64
+    path = ops.path(m, K, N, gs)
+    assert path == (2 if m >= 16 else 1)
+    M = data.make_int4_matrix(301, f"q70b{K}x{N}", K, N, gs)
+    x = data.make_x(302, f"q70bx{m}x{K}", m, K)
+    w, s, z = mat_dev(torch, M)
+    out = torch.empty((m, N), dtype=torch.float32, device="cuda")
+    ops.qmatmul_int4(tkdev, dev(torch, x), w, s, z, out, m, K, N, gs)
+    ref = oracle.qmatmul_f64(x, M.w, M.s, M.z, K, N, gs)
+    e = oracle.normwise_err(host(out), ref)
+    print(f"qmatmul m={m} K={K} N={N}: normwise err {e:.2e}")
+    assert e <= TOL and e <= _bar(path), e
+
+
+def _ffn(torch, tkdev, x, W, residual=False):
+    m = x.shape[0]
+    out = torch.empty((m, W.hidden), dtype=torch.float32, device="cuda")
+    h = torch.empty((m, W.inter), dtype=torch.float32, device="cuda")
+    ops.int4_ffn(tkdev, dev(torch, x), dev(torch, W.norm_w), mat_dev(torch, W.gate),
+                 mat_dev(torch, W.up), mat_dev(torch, W.down), out, m, W.hidden, W.inter, W.gs,
+                 eps=EPS, h_out=h, residual=residual)
+    return host(out), host(h)
+
+
+@pytest.mark.parametrize("m,inter", [
+    (1, 28672),   # the whole 70B FFN on one GPU, batch 1
+    (32, 28672),  # batch 32 (the GEMM path; down K = 28672)
+    (1, 3584),    # one rank's shard of the 70B FFN at TP8, batch 1
+    (32, 3584),   # the TP8 shard at batch 32
+])
+def test_ffn_70b(torch_cuda, tkdev, m, inter):
+    hidden, gs = 8192, 64
+    path = ops.ffn_path(m, hidden, inter, gs)
+    W = data.make_ffn(311, hidden, inter, gs)
+    x = data.make_x(312, f"f70bx{m}", m, hidden)
+    y, h = _ffn(torch_cuda, tkdev, x, W)
+    ref, ref_h = oracle.ffn_f64(x, W.norm_w, W.gate, W.up, W.down, EPS, return_h=True)
+    ey, eh = oracle.normwise_err(y, ref), oracle.normwise_err(h, ref_h)
+    print(f"70B FFN m={m} inter={inter}: normwise err y {ey:.2e} h {eh:.2e}")
+    assert ey <= TOL and eh <= TOL, (ey, eh)
+    assert ey <= _bar(path) and eh <= _bar(path), (ey, eh)
+
+
+def _stack(torch, tkdev, x, blocks):
+    """x <- x + FFN_l(x) for each block, through tk_int4_ffn with TK_FFN_RESIDUAL (ping-pong
+    buffers on the device; nothing returns to the host between blocks)."""
+    m, hidden = x.shape
+    bufs = [dev(torch, x), torch.empty((m, hidden), dtype=torch.float32, device="cuda")]
+    for l, W in enumerate(blocks):
+        src, dst = bufs[l % 2], bufs[(l + 1) % 2]
+        ops.int4_ffn(tkdev, src, dev(torch, W.norm_w), mat_dev(torch, W.gate),
+                     mat_dev(torch, W.up), mat_dev(torch, W.down), dst, m, W.hidden, W.inter,
+                     W.gs, eps=EPS, residual=True)
+    return host(bufs[len(blocks) % 2])
+
+
+def _stack_ref(x, blocks):
+    y = np.asarray(x, dtype=np.float64)
+    for W in blocks:
+        y = oracle.ffn_f64(y, W.norm_w, W.gate, W.up, W.down, EPS, residual=True)
+    return y
+
+
+@pytest.mark.parametrize("m", [1, 4])
+def test_stack_8b_four_blocks(torch_cuda, tkdev, m):
+    """Four full-size Llama-3-8B blocks (4096 -> 14336 -> 4096) with the residual."""
+    blocks = [data.make_ffn(321, 4096, 14336, 64, layer=l) for l in range(4)]
+    x = data.make_x(322, f"st8bx{m}", m, 4096)
+    y = _stack(torch_cuda, tkdev, x, blocks)
+    ref = _stack_ref(x, blocks)
+    e = oracle.normwise_err(y, ref)
+    print(f"8B stack of 4, m={m}: normwise err {e:.2e}")
+    assert e <= TOL and e <= ENGINE_PRECISION, e
+
+
+@pytest.mark.parametrize("m", [1, 2, 4, 16, 64])
+def test_stack_32_blocks_reduced_width(torch_cuda, tkdev, m):
+    """32 blocks (the 8B model's depth) at hidden 512, intermediate 1024, batch sweep of the
+    decode-stack workload: errors of every block feed the next one's rmsnorm."""
+    hidden, inter, gs = 512, 1024, 64
+    blocks = [data.make_ffn(331, hidden, inter, gs, layer=l) for l in range(32)]
+    x = data.make_x(332, f"st32x{m}", m, hidden)
+    y = _stack(torch_cuda, tkdev, x, blocks)
+    ref = _stack_ref(x, blocks)
+    e = oracle.normwise_err(y, ref)
+    path = ops.ffn_path(m, hidden, inter, gs)
+    print(f"32-block stack hidden {hidden}, m={m} (path {path}): normwise err {e:.2e}")
+    assert e <= TOL and e <= _bar(path), e

@@ -113,6 +113,8 @@ def test_p2p_allreduce_bit_exact(torch_cuda, tmp_path, world):
 
 
 def _rank_timeout(rank, world, uid, result_path):
+    import ctypes as C
+
     _setup(rank)
     os.environ["TK_WAIT_TIMEOUT_MS"] = "200"
     import torch
@@ -132,6 +134,11 @@ def _rank_timeout(rank, world, uid, result_path):
             g.allreduce_sum(buf, 1024)
             torch.cuda.synchronize()
             status = _lib.lib().tk_device_check_error(dev.handle)
+            # the group is now out of step with its peer: a further exchange is refused on
+            # the host, before any launch
+            again = _lib.lib().tk_tp_allreduce_sum_f32(g.handle, C.c_void_p(buf.data_ptr()), 1024,
+                                                       None)
+            status = status if again == _lib.TK_ERR_TIMEOUT else -100
     finally:
         g.close()  # a group that saw a timeout is not reused
         dev.deinit()

@@ -104,6 +104,9 @@ struct tk_device {
   int down_prefetch = 1;  // TK_DOWN_PREFETCH=0 turns off the L2 prefetch of the down projection
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   unsigned long long launches = 0;      // kernels enqueued through this device
+  // timed-out peer-memory exchanges seen by tk_device_check_error: a tk_tp group created before
+  // the latest one is out of step with its peers and refuses further exchanges
+  unsigned p2p_timeouts = 0;
   std::vector<TmapEntry> tmaps;
 };
 
@@ -819,6 +822,7 @@ int tk_device_check_error(tk_device* d) {
   unsigned h = 0;
   TK_CUDA_TRY(cudaMemcpy(&h, d->err, sizeof(h), cudaMemcpyDeviceToHost));
   if (h == 0) return TK_OK;
+  if (h & tk::kErrP2PWait) ++d->p2p_timeouts;
   // Clear the error word and return the engine's scratch to its launch-ready state.
   TK_CUDA_TRY(cudaDeviceSynchronize());
   TK_CUDA_TRY(cudaMemset(d->err, 0, 256));
@@ -1216,6 +1220,7 @@ int tk_int4_ffn(tk_device* d, const float* x, const float* norm_w, const tk_int4
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // TK_NOALLOC_SCRATCH_BYTES
+constexpr size_t kNoAllocErrBytes = 256;  // the error word's slot at the start of the array
 constexpr int kNoAllocMaxDevices = 64;
 
 // One copy per GPU that loads this library, held until the process exits.  In host code
@@ -1275,9 +1280,11 @@ int noalloc_engine_chunk(unsigned char* scratch, int sm_count, int smem_optin, c
   P.maxseg = max_segments(P, Wtot);
   P.red_first = 0;
   P.red_count = 1;
-  // layout: launch state | error word | tile counters | partials | per-CTA records
-  const size_t off_err = align256(sizeof(SyncState));
-  const size_t off_cnt = off_err + 256;
+  // layout: error word | launch state | tile counters | partials | per-CTA records.  The error
+  // word is cleared once per call (tk_qmatmul_int4_noalloc), before the first chunk, so that a
+  // timed-out wait in any chunk is still set when the word is read after the last one.
+  const size_t off_sync = kNoAllocErrBytes;
+  const size_t off_cnt = off_sync + align256(sizeof(SyncState));
   const size_t off_part = off_cnt + align256((size_t)(n / kTileCols) * sizeof(unsigned));
   const size_t part_bytes =
       (size_t)P.tiles * P.nmat * P.maxseg * kSlices * mt * kTileCols * sizeof(float);
@@ -1289,9 +1296,9 @@ int noalloc_engine_chunk(unsigned char* scratch, int sm_count, int smem_optin, c
                 "m=%d k=%d n=%d group_size=%d needs %zu bytes of scratch; the allocation-free "
                 "entry point has %zu (use tk_qmatmul_int4)",
                 m, k, n, gs, need, kNoAllocScratchBytes);
-  // the launch state, error word and tile counters must start at zero; the partials and
-  // records are written before they are read
-  TK_CUDA_TRY(cudaMemsetAsync(scratch, 0, off_part, st));
+  // the launch state and tile counters must start at zero; the partials and records are
+  // written before they are read
+  TK_CUDA_TRY(cudaMemsetAsync(scratch + off_sync, 0, off_part - off_sync, st));
   P.map_base = 0;
   P.scales[0] = s;
   P.zeros[0] = z;
@@ -1326,8 +1333,8 @@ int noalloc_engine_chunk(unsigned char* scratch, int sm_count, int smem_optin, c
   p.stages = stages;
   p.rec0_smem = rec0_smem;
   p.trace = nullptr;
-  p.sync = reinterpret_cast<SyncState*>(scratch);
-  p.err = reinterpret_cast<unsigned*>(scratch + off_err);
+  p.sync = reinterpret_cast<SyncState*>(scratch + off_sync);
+  p.err = reinterpret_cast<unsigned*>(scratch);
   p.timeout_ns = kDefaultTimeoutNs;
   int blocks = 0;
   TK_CUDA_TRY(engine_occupancy(mt, p.gs0, smem, &blocks));
@@ -1363,6 +1370,9 @@ extern "C" int tk_qmatmul_int4_noalloc(const float* x, const uint8_t* w, const u
   if (major < 10) return fail(TK_ERR_UNSUPPORTED, "device %d is not sm_100a", ordinal);
   TK_CUDA_TRY(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, ordinal));
   TK_CUDA_TRY(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ordinal));
+  // the error word (the array's first bytes) starts at zero once per call and collects the
+  // error bits of every chunk
+  TK_CUDA_TRY(cudaMemsetAsync(scratch, 0, kNoAllocErrBytes, cs));
   for (uint32_t r = 0; r < m; r += 4) {
     const uint32_t mm = std::min<uint32_t>(4, m - r);
     st = noalloc_engine_chunk(scratch, sm_count, smem_optin, x + (size_t)r * k, w, s, z,
@@ -1370,10 +1380,8 @@ extern "C" int tk_qmatmul_int4_noalloc(const float* x, const uint8_t* w, const u
     if (st != TK_OK) return st;
   }
   TK_CUDA_TRY(cudaStreamSynchronize(cs));
-  // the error word sits right after the launch state (see noalloc_engine_chunk)
   unsigned h = 0;
-  TK_CUDA_TRY(cudaMemcpy(&h, scratch + align256(sizeof(SyncState)), sizeof(h),
-                         cudaMemcpyDeviceToHost));
+  TK_CUDA_TRY(cudaMemcpy(&h, scratch, sizeof(h), cudaMemcpyDeviceToHost));
   if (h != 0) return fail(TK_ERR_TIMEOUT, "device-side bounded wait gave up (error bits 0x%x)", h);
   return TK_OK;
 }
@@ -1440,6 +1448,9 @@ struct tk_tp {
   void* p2p_base = nullptr;              // this rank's receive area + flags + chunk epochs
   void* p2p_peer[tk::kP2PMaxRanks] = {};  // peers' areas mapped here (CUDA IPC)
   tk::P2PParams p2p_params{};
+  // the device's p2p_timeouts when the group was made: a wait of this group that ran out leaves
+  // the ranks' chunk epochs out of step, so the group takes no further exchange after one
+  unsigned p2p_timeouts_at_create = 0;
 };
 
 namespace {
@@ -1563,6 +1574,7 @@ int tk_tp_create(tk_device* d, int nranks, int rank, const uint8_t id[TK_TP_UNIQ
   tp->dev = d;
   tp->nranks = nranks;
   tp->rank = rank;
+  tp->p2p_timeouts_at_create = d->p2p_timeouts;
   ncclResult_t r = n->comm_init_rank(&tp->comm, nranks, u, rank);
   if (r != ncclSuccess) {
     delete tp;
@@ -1602,6 +1614,10 @@ void tk_tp_destroy(tk_tp* tp) {
 int tk_tp_allreduce_sum_f32(tk_tp* tp, float* buf, size_t count, void* stream) {
   if (!tp || (!buf && count)) return fail(TK_ERR_ARG, "NULL argument");
   if (count == 0 || tp->nranks == 1) return TK_OK;
+  if (tp->p2p && tp->dev->p2p_timeouts != tp->p2p_timeouts_at_create)
+    return fail(TK_ERR_TIMEOUT,
+                "a peer-memory exchange on this device timed out; the group's ranks are out of "
+                "step: destroy it (tk_tp_destroy) and create a new one");
   int st = set_device(tp->dev);
   if (st != TK_OK) return st;
   if (tp->p2p && count <= tk::kP2PMaxFloats) {
