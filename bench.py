@@ -73,7 +73,7 @@ def arithmetic(path, m):
         return ("int4->f16 x f16 -> f32",
                 "INT4 weights dequantised to f16, f16 activations (and f16 h between the GEMMs), "
                 "tcgen05 MMA with f32 accumulation, f32 output")
-    if path == 1:
+    if path in (1, 3):
         if m <= 2:
             return ("int4 x int16 -> int32 -> f32",
                     "INT4 weights x activations quantised to int16 per group (one power-of-two "
@@ -619,7 +619,10 @@ def main():
                             "sample": f"unavailable: {e}"}
         traffic = (load_traffic(m, world) if (args.model == "8b" and L == 1 and not matvec)
                    else None)
-        if matvec:
+        if path == 3:
+            kern = ("tk::int4_decode_kernel (qmatmul_int4, one phase)" if matvec else
+                    "tk::int4_decode_kernel (FFN: gate/up, h, down, y in one launch)")
+        elif matvec:
             kern = "tk::int4_engine_kernel (qmatmul_int4, one phase)"
         elif path == 2:
             kern = ("tk::int4_gemm_kernel x2 (gate/up with silu*up, down split-K) + rmsnorm, "
@@ -666,7 +669,8 @@ def main():
                 "l2_guard": f"{copies} weight copies x {L} block(s) = "
                             f"{copies * L * shard_w_bytes / 1e6:.0f} MB per GPU (> 3x L2)",
                 "launch": "cuda-graph" if graph is not None else "stream",
-                "path": {2: "tcgen05 GEMM", 1: "streaming engine"}.get(path, "CUDA-core"),
+                "path": {3: "decode kernel (batch 1-2)", 2: "tcgen05 GEMM",
+                         1: "streaming engine"}.get(path, "CUDA-core"),
                 "arithmetic": arith,
                 "bytes_per_step": step_bytes_total,
                 "rank_ms_per_step": [round(v / steps_timed, 6) for v in rank_ms],

@@ -342,8 +342,10 @@ int tk_qmatmul_int4_noalloc(const float *x, const uint8_t *w_packed, const uint1
                             uint32_t n, uint32_t group_size, void *stream);
 
 /* Which path tk_qmatmul_int4 would take for a shape with 16-byte aligned buffers and the
- * default device settings: 2 = tcgen05 GEMM (m >= 16), 1 = streaming engine (m < 16, or a
- * shape the GEMM does not tile), 0 = CUDA-core fallback, <0 = invalid shape.
+ * default device settings (148 SMs, 227 KB of shared memory per block): 3 = the batch 1-2 decode
+ * kernel (m <= 2 whose records and ring fit shared memory), 2 = tcgen05 GEMM (m >= 16),
+ * 1 = streaming engine (other m < 16, or a shape the GEMM does not tile), 0 = CUDA-core fallback,
+ * <0 = invalid shape.
  * No counterpart in the reference (one shader serves every shape there). */
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t group_size);
 

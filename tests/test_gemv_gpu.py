@@ -75,7 +75,7 @@ ENGINE_CASES = [
 
 @pytest.mark.parametrize("m,K,N,gs", ENGINE_CASES)
 def test_qmatmul_engine_vs_oracle(torch_cuda, tkdev, m, K, N, gs):
-    assert ops.path(m, K, N, gs) == 1
+    assert ops.path(m, K, N, gs) in (1, 3)
     M = data.make_int4_matrix(1000 + m, f"q{K}x{N}", K, N, gs)
     x = data.make_x(7, f"x{m}x{K}", m, K)
     y = run_qmatmul(torch_cuda, tkdev, x, M)

@@ -1,0 +1,784 @@
+// tk_decode.cu -- the batch 1-2 decode kernel: qmatmul_int4 and the INT4 Llama FFN in one
+// persistent launch per call, with a counter-free split-K exchange (tk_decode.h).
+//
+// Warp roles (one CTA per SM, 288 threads):
+//   warp 8 (producer)   lane 0 issues every copy of the CTA: first the prologue data (x rows and
+//                       the norm weight, 1-D bulk copies into the first ring stages), then per
+//                       work item the packed rows (2-D TMA box of 1040-byte rows), the f16 scales
+//                       and the packed zero points of a 1024-column tile and one group.  Items of
+//                       phase B are copied as soon as a stage is free: their weights do not
+//                       depend on h, so they land while phase A finishes and h is assembled.
+//   warps 0-7 (consumers) slice w = 128 columns of every item, dp2a arithmetic (tk_dp2a.cuh).
+//                       prologue: rmsnorm + the int16 records of every group of x, in smem;
+//                       phase A, then (FFN) the phase-B records: h = silu(gate) * up summed from
+//                       the tagged gate/up partials of the other CTAs, one item per warp, in
+//                       parallel; phase B; finally the y reduction tasks of this CTA.
+// Split-K exchange: a segment (one CTA's contiguous k range of one column unit) stores its
+// partial sums as 64-bit words (tag << 32 | float bits) with plain stores; a reader loads the
+// words of every segment it needs and retries until all carry this launch's tag, then sums them
+// in segment order (deterministic: every reader gets the same bits).  The tag is the launch's
+// epoch + 1: CTA b reads epoch[b] at its start and, at its end, writes epoch[b + k * grid] for
+// every k, so every slot advances once per launch whatever the grid size, and no CTA writes a
+// slot another CTA of the same launch reads.
+// Every wait is bounded by a global-timer timeout and reports through p.err.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "tk_decode.h"
+#include "tk_dp2a.cuh"
+#include "tk_ptx.cuh"
+
+namespace tk {
+
+namespace {
+
+constexpr int kNC = kDecConsumers;
+constexpr int kProducerWarp = kNC;
+
+// CTA whose stream-K range holds unit u (ranges [U*b/W, U*(b+1)/W))
+__device__ __forceinline__ int dec_cta_of_unit(unsigned u, unsigned units, unsigned W) {
+  return (int)(((u + 1) * W - 1) / units);
+}
+
+// Segments (CTA ranges) of column unit cu, and the first one's CTA.
+__device__ __forceinline__ int dec_nseg(const DecPhase& P, int cu, int* first) {
+  const unsigned per = (unsigned)(P.groups * P.spg);
+  const unsigned a = (unsigned)cu * per;
+  const int c0 = dec_cta_of_unit(a, P.units, P.ctas);
+  if (first) *first = c0;
+  return dec_cta_of_unit(a + per - 1, P.units, P.ctas) - c0 + 1;
+}
+
+// One CTA's walk over its items (one group of one column unit each) of phase A, then B.
+struct It {
+  int ph;       // 0: phase A, 1: phase B, 2: done
+  int i, n;     // item index within the phase, the CTA's items in the phase
+  int cu, grp;  // column unit (tile * nmat + matrix) and group
+  int s0, s1;   // k-steps [s0, s1) of the group
+  int last_s1;
+  int groups, spg, nmat, N;
+};
+
+__device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned b) {
+  while (it.ph < 2) {
+    if (it.ph == 1 && !p.ffn) {
+      it.ph = 2;
+      return;
+    }
+    const DecPhase& P = it.ph == 0 ? p.A : p.B;
+    if (b < P.ctas) {
+      const unsigned U = P.units, W = P.ctas;
+      const unsigned beg = U * b / W, end = U * (b + 1) / W;
+      const unsigned fg0 = beg / (unsigned)P.spg, fgl = (end - 1) / (unsigned)P.spg;
+      const unsigned cl = fg0 / (unsigned)P.groups;
+      it.groups = P.groups;
+      it.spg = P.spg;
+      it.nmat = P.nmat;
+      it.N = P.N;
+      it.i = 0;
+      it.n = (int)(fgl - fg0 + 1);
+      it.cu = (int)cl;
+      it.grp = (int)(fg0 - cl * (unsigned)P.groups);
+      it.s0 = (int)(beg - fg0 * (unsigned)P.spg);
+      it.last_s1 = (int)(end - fgl * (unsigned)P.spg);
+      it.s1 = it.n == 1 ? it.last_s1 : P.spg;
+      return;
+    }
+    ++it.ph;
+  }
+}
+
+__device__ __forceinline__ void it_start(It& it, const DecodeParams& p, unsigned b) {
+  it.ph = 0;
+  it.i = it.n = it.cu = it.grp = it.s0 = it.s1 = it.last_s1 = 0;
+  it.groups = it.spg = it.nmat = 1;
+  it.N = 0;
+  it_seek(it, p, b);
+}
+
+__device__ __forceinline__ void it_next(It& it, const DecodeParams& p, unsigned b) {
+  if (++it.i < it.n) {
+    if (++it.grp == it.groups) {
+      it.grp = 0;
+      ++it.cu;
+    }
+    it.s0 = 0;
+    it.s1 = it.i == it.n - 1 ? it.last_s1 : it.spg;
+    return;
+  }
+  ++it.ph;
+  it_seek(it, p, b);
+}
+
+__device__ __forceinline__ int it_tile(const It& it) { return it.cu >> (it.nmat - 1); }
+
+// 128-column slices of the item's tile that hold columns (8 except in a ragged last tile).
+__device__ __forceinline__ int it_slices(const It& it) {
+  const int rem = (it.N - it_tile(it) * kWideCols) / kTileCols;
+  return rem < kSlices ? rem : kSlices;
+}
+
+__device__ __forceinline__ bool it_seg_end(const It& it) {
+  return it.grp == it.groups - 1 || it.i == it.n - 1;
+}
+
+__device__ __forceinline__ void dec_trace(const DecodeParams& p, int ev) {
+  if (p.trace) p.trace[(size_t)blockIdx.x * kTraceEvents + ev] = global_timer_ns();
+}
+
+// Packed rows + scales + zero points of item `it` into one stage (producer lane 0).
+__device__ __forceinline__ void issue_item(const TmapPack& maps, const DecPhase& P, const It& it,
+                                           uint8_t* tile, uint8_t* aux, uint64_t* bar,
+                                           uint64_t pol) {
+  const int mat = it.cu & (it.nmat - 1);
+  const int wt = it_tile(it);
+  const int ns = it_slices(it);
+  const uint32_t bytes = (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes +
+                                    ns * (kScaleBytes + kZeroBytes));
+  mbar_arrive_expect_tx(bar, bytes);
+  const int row0 = it.grp * it.spg * kStepRows;
+  const int x = wt * (kWideCols / 8);  // u64 element of the tile's first byte
+  if (it.s0 == 0 && it.s1 == it.spg) {
+    tma_load_2d(tile, &maps.map[P.map_base + 2 * mat], bar, x, row0, pol);
+  } else {
+    for (int s = it.s0; s < it.s1; ++s)
+      tma_load_2d(tile + s * kStepRows * kRowBytes, &maps.map[P.map_base + 2 * mat + 1], bar, x,
+                  row0 + s * kStepRows, pol);
+  }
+  const int col0 = wt * kWideCols;
+  bulk_load(aux, P.scales[mat] + (size_t)it.grp * P.N + col0, (uint32_t)(ns * kScaleBytes), bar, pol);
+  bulk_load(aux + kSlices * kScaleBytes, P.zeros[mat] + (size_t)it.grp * (P.N / 2) + col0 / 2,
+            (uint32_t)(ns * kZeroBytes), bar, pol);
+}
+
+__device__ __forceinline__ unsigned long long tagged(float v, unsigned tag) {
+  return ((unsigned long long)tag << 32) | __float_as_uint(v);
+}
+
+__device__ __forceinline__ void st_cg_u64x2(unsigned long long* p, unsigned long long a,
+                                            unsigned long long b) {
+  asm volatile("st.global.cg.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ ulonglong2 ld_cg_u64x2(const unsigned long long* p) {
+  ulonglong2 v;
+  asm volatile("ld.global.cg.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_cg_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Tagged partial words of segment `seg` of column unit cu, token tok: 1024 columns.
+template <int MT>
+__device__ __forceinline__ unsigned long long* dec_part(const DecPhase& P, int cu, int seg, int tok) {
+  return P.part + (((size_t)cu * P.maxseg + seg) * MT + tok) * kWideCols;
+}
+
+// Bounded wait for a stage; false on an abort or a timeout.
+__device__ __forceinline__ bool dec_wait_full(uint64_t* bar, uint32_t par, volatile int* abort,
+                                              unsigned* err, unsigned long long timeout_ns,
+                                              int lane) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, par))) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    if (__all_sync(0xffffffffu, mbar_try_wait_hint(bar, par, 1000))) return true;
+    int st = 0;
+    if (lane == 0) {
+      if (*abort) st = 1;
+      else if (global_timer_ns() - t0 > timeout_ns) {
+        atomicOr(err, kErrTmaWait);
+        st = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, st, 0)) return false;
+  }
+}
+
+// Consumer warp `slice`: all of this CTA's items of phase `ph` (it.ph == ph on entry), dp2a
+// arithmetic; each finished segment's partial sums are stored as tagged words.  Records: the
+// group's (rec_by_item == 0: rec + grp * frag_bytes) or the item's (rec + i * frag_bytes).
+// Returns false on an abort.
+template <int MT, int GS>
+__device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, It& it,
+                              unsigned b, int slice, int lane, uint8_t* tiles, uint8_t* auxs,
+                              uint64_t* full, uint64_t* empty, int& slot, uint32_t& parity,
+                              long long& consumed, const uint8_t* rec, bool rec_by_item,
+                              unsigned tag, volatile int* abort) {
+  constexpr int R = GS / 2;                 // packed rows per group
+  constexpr int HB = R <= 32 ? R / 2 : 16;  // rows per chunk
+  constexpr int NCH = R / HB;               // chunks per item (2 or 4)
+  constexpr int tok_stride = dp_tok_stride(GS);
+  const int S = p.stages;
+  const int fb = p.frag_bytes;
+  auto stage_tile = [&](int sl) { return tiles + (size_t)sl * p.tile_stage_bytes + slice * kTileCols; };
+  auto stage_aux = [&](int sl) { return auxs + (size_t)sl * p.aux_stage_bytes; };
+  auto item_rec = [&](const It& x) { return rec + (size_t)(rec_by_item ? x.i : x.grp) * fb; };
+  if (it.ph != ph) return true;
+  uint32_t wA[HB], wB[HB];
+  uint4 XA[MT][HB / 4], XB[MT][HB / 4];
+  DpMeta<MT> Mc, Mn;
+  float y[4 * MT];
+#pragma unroll
+  for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+  if (!dec_wait_full(&full[slot], parity, abort, p.err, p.timeout_ns, lane)) return false;
+  {
+    const uint8_t* r = item_rec(it);
+    dp_load_meta<MT, GS>(stage_aux(slot), r, slice, lane, it.s0, it.s1, Mc);
+    dp_load_rows<HB>(stage_tile(slot), 0, it.s0 * kStepRows, it.s1 * kStepRows, lane, wA);
+    dp_load_x<MT, HB>(r, tok_stride, 0, XA);
+  }
+  for (;;) {
+    const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
+    const uint8_t* tl = stage_tile(slot);
+    const uint8_t* r = item_rec(it);
+    const bool seg_end = it_seg_end(it);
+    It nx = it;
+    it_next(nx, p, b);
+    const int nslot = slot + 1 == S ? 0 : slot + 1;
+    const uint32_t npar = slot + 1 == S ? parity ^ 1u : parity;
+    const bool more = nx.ph == ph;
+    const bool prefetch = !seg_end && more;
+    bool next_loaded = false, ok = true;
+    int aL[MT][4], aH[MT][4];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) aL[m][i] = aH[m][i] = 0;
+#pragma unroll
+    for (int c = 0; c < NCH; c += 2) {
+      dp_load_rows<HB>(tl, (c + 1) * HB, r0, r1, lane, wB);
+      dp_load_x<MT, HB>(r, tok_stride, (c + 1) * HB, XB);
+      bool nready = false;
+      if (c + 2 == NCH) {
+        // every byte of this stage is loaded (in issue order before the arrival)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (prefetch) nready = mbar_test_wait(&full[nslot], npar);
+      }
+      dp_compute<MT, HB>(wA, XA, aL, aH);
+      if (c + 2 < NCH) {
+        dp_load_rows<HB>(tl, (c + 2) * HB, r0, r1, lane, wA);
+        dp_load_x<MT, HB>(r, tok_stride, (c + 2) * HB, XA);
+      } else if (prefetch) {
+        // the next item's first chunk while this item's last chunk computes
+        if (!__all_sync(0xffffffffu, nready) &&
+            !dec_wait_full(&full[nslot], npar, abort, p.err, p.timeout_ns, lane)) {
+          ok = false;
+        } else {
+          const uint8_t* nr = item_rec(nx);
+          dp_load_meta<MT, GS>(stage_aux(nslot), nr, slice, lane, nx.s0, nx.s1, Mn);
+          dp_load_rows<HB>(stage_tile(nslot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
+          dp_load_x<MT, HB>(nr, tok_stride, 0, XA);
+          next_loaded = true;
+        }
+      }
+      dp_compute<MT, HB>(wB, XB, aL, aH);
+    }
+    dp_epilogue<MT>(Mc, aL, aH, y);
+    ++consumed;
+    slot = nslot;
+    parity = npar;
+    if (seg_end) {
+      if (slice < it_slices(it)) {
+        int c0 = 0;
+        dec_nseg(P, it.cu, &c0);
+        const int seg = (int)b - c0;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          unsigned long long* dst = dec_part<MT>(P, it.cu, seg, m) + slice * kTileCols + 4 * lane;
+          st_cg_u64x2(dst, tagged(y[4 * m], tag), tagged(y[4 * m + 1], tag));
+          st_cg_u64x2(dst + 2, tagged(y[4 * m + 2], tag), tagged(y[4 * m + 3], tag));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+    }
+    if (!ok) return false;
+    if (!more) {
+      it = nx;
+      return true;
+    }
+    if (!next_loaded) {
+      if (!dec_wait_full(&full[slot], parity, abort, p.err, p.timeout_ns, lane)) return false;
+      const uint8_t* nr = item_rec(nx);
+      dp_load_meta<MT, GS>(stage_aux(slot), nr, slice, lane, nx.s0, nx.s1, Mn);
+      dp_load_rows<HB>(stage_tile(slot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
+      dp_load_x<MT, HB>(nr, tok_stride, 0, XA);
+    }
+    it = nx;
+    Mc = Mn;
+  }
+}
+
+// Bounded poll step shared by the readers of tagged partials: returns 1 to retry, 0 to give up
+// (timeout -> error bit and abort, or another warp aborted).  t0 = 0 starts the clock.
+__device__ __forceinline__ bool dec_poll_again(uint64_t& t0, volatile int* abort, unsigned* err,
+                                               unsigned long long timeout_ns, int lane) {
+  const uint64_t now = global_timer_ns();
+  if (t0 == 0) t0 = now;
+  int st = 0;
+  if (lane == 0) {
+    if (*abort) st = 1;
+    else if (now - t0 > timeout_ns) {
+      atomicOr(err, kErrDecPoll);
+      *abort = 1;
+      st = 1;
+    }
+  }
+  if (__shfl_sync(0xffffffffu, st, 0)) return false;
+  __nanosleep(64);
+  return true;
+}
+
+// One reduction task of the last phase: 8 output columns, 4 lanes per column; lane (c, j) sums
+// the segments j, j + 4, j + 8, ... of column c in order, then the four lanes combine their sums
+// in a fixed tree, so the result's bits do not depend on timing.  Returns false on an abort.
+template <int MT>
+__device__ bool reduce_task(const DecodeParams& p, const DecPhase& L, int task, unsigned tag,
+                            int lane, volatile int* abort) {
+  constexpr int B = kDecReduceBatch;  // segments per lane per batch
+  const int col = task * 8 + (lane >> 2), j = lane & 3;
+  const int cu = col / kWideCols, cl = col % kWideCols;
+  const int ns = dec_nseg(L, cu, nullptr);
+#pragma unroll 1
+  for (int m = 0; m < MT; ++m) {
+    float acc = 0.f;
+    for (int base = 0; base < ns; base += 4 * B) {
+      uint64_t t0 = 0;
+      for (;;) {
+        unsigned long long v[B];
+#pragma unroll
+        for (int i = 0; i < B; ++i) {
+          const int s = base + j + 4 * i;
+          v[i] = s < ns ? ld_cg_u64(dec_part<MT>(L, cu, s, m) + cl) : ((unsigned long long)tag << 32);
+        }
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < B; ++i) ok = ok && (unsigned)(v[i] >> 32) == tag;
+        if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll
+          for (int i = 0; i < B; ++i) acc += __uint_as_float((unsigned)v[i]);
+          break;
+        }
+        if (!dec_poll_again(t0, abort, p.err, p.timeout_ns, lane)) return false;
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (j == 0 && m < p.m) {
+      if (p.residual) acc = p.residual[(size_t)m * p.ldr + col] + acc;
+      p.out[(size_t)m * p.ldo + col] = acc;
+    }
+  }
+  return true;
+}
+
+// The record of one phase-B item (h group `grp`), built by one warp from the gate/up partials:
+// h = silu(sum of the gate segments) * (sum of the up segments) over the group's GS columns,
+// quantised into the dp2a record at `rec`; write_h: also store h to h_out.  Lanes: li = lane & 15
+// owns columns 4 li .. 4 li + 3 of the group; for GS <= 64 lanes 0-15 sum the gate segments and
+// lanes 16-31 the up segments at the same time, for GS = 128 every lane sums both.  Segments are
+// loaded 8 at a time, all of a batch in flight, and summed in segment order.
+template <int MT, int GS>
+__device__ bool build_h_record(const DecodeParams& p, int grp, bool write_h, uint8_t* rec,
+                               unsigned tag, int lane, volatile int* abort) {
+  constexpr int kSB = 8;
+  constexpr bool kSplit = GS / 4 <= 16;  // a half warp per matrix
+  constexpr int kMats = kSplit ? 1 : 2;  // matrices summed per lane
+  const DecPhase& A = p.A;
+  const int c0 = grp * GS;  // first h column of the group
+  const int ta = c0 / kWideCols, cl = c0 % kWideCols;
+  const int li = kSplit ? (lane & 15) : lane;
+  const bool owner = li < GS / 4;
+  float acc[kMats][MT][4];
+#pragma unroll
+  for (int q = 0; q < kMats; ++q)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[q][m][0] = acc[q][m][1] = acc[q][m][2] = acc[q][m][3] = 0.f;
+#pragma unroll
+  for (int q = 0; q < kMats; ++q) {
+    const int mat = kSplit ? (lane >> 4) : q;
+    const int cu = ta * 2 + mat;
+    const int ns = dec_nseg(A, cu, nullptr);
+    // warp-uniform batch count: the larger of the two matrices' segment counts
+    const int nsw = kSplit ? max(ns, __shfl_xor_sync(0xffffffffu, ns, 16)) : ns;
+    for (int base = 0; base < nsw; base += kSB) {
+      uint64_t t0 = 0;
+      for (;;) {
+        ulonglong2 va[kSB][MT], vb[kSB][MT];
+#pragma unroll
+        for (int i = 0; i < kSB; ++i)
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            if (owner && base + i < ns) {
+              const unsigned long long* src = dec_part<MT>(A, cu, base + i, m) + cl + 4 * li;
+              va[i][m] = ld_cg_u64x2(src);
+              vb[i][m] = ld_cg_u64x2(src + 2);
+            } else {
+              const unsigned long long t = (unsigned long long)tag << 32;
+              va[i][m] = vb[i][m] = make_ulonglong2(t, t);
+            }
+          }
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < kSB; ++i)
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            ok = ok && (unsigned)(va[i][m].x >> 32) == tag && (unsigned)(va[i][m].y >> 32) == tag &&
+                 (unsigned)(vb[i][m].x >> 32) == tag && (unsigned)(vb[i][m].y >> 32) == tag;
+        if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll
+          for (int i = 0; i < kSB; ++i)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              acc[q][m][0] += __uint_as_float((unsigned)va[i][m].x);
+              acc[q][m][1] += __uint_as_float((unsigned)va[i][m].y);
+              acc[q][m][2] += __uint_as_float((unsigned)vb[i][m].x);
+              acc[q][m][3] += __uint_as_float((unsigned)vb[i][m].y);
+            }
+          break;
+        }
+        if (!dec_poll_again(t0, abort, p.err, p.timeout_ns, lane)) return false;
+      }
+    }
+  }
+  const bool holder = lane < GS / 4;  // lanes 0 .. GS/4 - 1 hold the group's h
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    float h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float g = acc[0][m][i];
+      // GS <= 64: the up sums live in lanes 16-31
+      const float u = kSplit ? __shfl_down_sync(0xffffffffu, acc[0][m][i], 16) : acc[kMats - 1][m][i];
+      h[i] = (holder && m < p.m) ? g / (1.0f + expf(-g)) * u : 0.f;
+    }
+    build_records_dp<MT>(h, m, GS, rec, p.frag_bytes, lane, 0);
+    if (write_h && holder && m < p.m)
+      *reinterpret_cast<float4*>(p.h_out + (size_t)m * p.ldh + c0 + 4 * lane) =
+          make_float4(h[0], h[1], h[2], h[3]);
+  }
+  return true;
+}
+
+template <int MT, int GS>
+__global__ void __launch_bounds__(kDecThreads, 1)
+    int4_decode_kernel(const __grid_constant__ TmapPack maps, const __grid_constant__ DecodeParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ float s_red[MT * kNC];
+  __shared__ float s_rms[MT];
+  __shared__ volatile long long s_armed;  // items (prologue stages included) armed by the producer
+  __shared__ volatile int s_abort;
+  __shared__ volatile int s_never;
+  __shared__ unsigned s_tag;
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.stages;
+  uint8_t* tiles = smem;
+  uint8_t* auxs = smem + (size_t)S * p.tile_stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(auxs + (size_t)S * p.aux_stage_bytes);
+  uint64_t* empty = full + S;
+  uint8_t* rec0 = reinterpret_cast<uint8_t*>(empty + S);  // 16-byte aligned (S barriers each)
+  uint8_t* recb = rec0 + (size_t)p.A.groups * p.frag_bytes;
+  const unsigned b = blockIdx.x;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kNC);
+    }
+    fence_mbar_init();
+    s_armed = 0;
+    s_abort = 0;
+    s_never = 0;
+    s_tag = p.epoch[b] + 1u;
+    dec_trace(p, 0);
+  }
+  __syncthreads();
+  const unsigned tag = s_tag;
+  int slot = 0;
+  uint32_t parity = 0;
+  long long consumed = 0;
+
+  if (warp == kProducerWarp) {
+    // ------------------------------- producer ---------------------------------------------
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first();
+      const int P0 = p.pro_stages;
+      // prologue: x rows then the norm weight, contiguous over the first P0 stages' tiles
+      {
+        const uint32_t xrow = (uint32_t)p.A.K * 4u;
+        const uint32_t total = xrow * (uint32_t)p.m + (p.norm_w ? xrow : 0u);
+        mbar_arrive_expect_tx(&full[0], total);
+        for (int m = 0; m < p.m; ++m)
+          bulk_load(tiles + (size_t)m * xrow, p.x + (size_t)m * p.ldx, xrow, &full[0], pol);
+        if (p.norm_w) bulk_load(tiles + (size_t)p.m * xrow, p.norm_w, xrow, &full[0], pol);
+        for (int i = 1; i < P0; ++i) mbar_arrive(&full[i]);
+        s_armed = P0;
+      }
+      long long G = P0;
+      int ws = P0 % S;
+      uint32_t wround = (uint32_t)(P0 / S);
+      It it;
+      it_start(it, p, b);
+      dec_trace(p, 7);
+      while (it.ph < 2) {
+        if (wround > 0) {
+          // bounded wait for the consumers to free the slot
+          bool ok = mbar_try_wait(&empty[ws], (wround - 1) & 1);
+          if (!ok) {
+            const uint64_t t0 = global_timer_ns();
+            while (!(ok = mbar_try_wait(&empty[ws], (wround - 1) & 1))) {
+              if (s_abort) break;
+              if (global_timer_ns() - t0 > p.timeout_ns) {
+                atomicOr(p.err, kErrTmaWait);
+                s_abort = 1;
+                break;
+              }
+            }
+          }
+          if (!ok) break;
+        }
+        if (s_abort) break;
+        const DecPhase& P = it.ph == 0 ? p.A : p.B;
+        issue_item(maps, P, it, tiles + (size_t)ws * p.tile_stage_bytes,
+                   auxs + (size_t)ws * p.aux_stage_bytes, &full[ws], pol);
+        s_armed = ++G;
+        it_next(it, p, b);
+        if (++ws == S) {
+          ws = 0;
+          ++wround;
+        }
+      }
+      s_armed = G;
+      dec_trace(p, 8);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------- consumers --------------------------------------------
+    const int slice = warp;
+    volatile int* abort = &s_abort;
+    // prologue: wait for x (and the norm weight), then the records of every group of x; the
+    // consumer warps take the same branch (an abort is published before the barrier)
+    if (!dec_wait_full(&full[0], 0, abort, p.err, p.timeout_ns, lane) && lane == 0) *abort = 1;
+    named_barrier(1, kNC * 32);
+    bool ok = *abort == 0;
+    const bool pro_landed = ok;
+    if (ok) {
+      const float* xs = reinterpret_cast<const float*>(tiles);
+      const float* ws = xs + (size_t)p.m * p.A.K;
+      const int nchunks = p.A.K / kTileCols;
+      float rms[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) rms[m] = 1.f;
+      if (p.norm_w) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float v = 0.f;
+          if (m < p.m)
+            for (int ch = warp; ch < nchunks; ch += kNC) {
+              const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.A.K + ch * kTileCols + 4 * lane);
+              v = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, v))));
+            }
+          for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+          if (lane == 0) s_red[m * kNC + warp] = v;
+        }
+        named_barrier(1, kNC * 32);
+        if (threadIdx.x < MT) {
+          float tot = 0.f;
+          for (int i = 0; i < kNC; ++i) tot += s_red[threadIdx.x * kNC + i];
+          s_rms[threadIdx.x] = rsqrtf(tot / (float)p.A.K + p.eps);
+        }
+        named_barrier(1, kNC * 32);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) rms[m] = s_rms[m];
+      }
+      for (int ch = warp; ch < nchunks; ch += kNC) {
+        float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (p.norm_w) w4 = *reinterpret_cast<const float4*>(ws + ch * kTileCols + 4 * lane);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+          if (m < p.m) {
+            const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.A.K + ch * kTileCols + 4 * lane);
+            if (p.norm_w) {
+              v[0] = a.x * rms[m] * w4.x;
+              v[1] = a.y * rms[m] * w4.y;
+              v[2] = a.z * rms[m] * w4.z;
+              v[3] = a.w * rms[m] * w4.w;
+            } else {
+              v[0] = a.x;
+              v[1] = a.y;
+              v[2] = a.z;
+              v[3] = a.w;
+            }
+          }
+          build_records_dp<MT>(v, m, GS, rec0 + (size_t)(ch * kTileCols / GS) * p.frag_bytes,
+                               p.frag_bytes, lane, -1);
+        }
+      }
+    }
+    // every consumer has read the prologue data and written its records: free the stages
+    named_barrier(1, kNC * 32);
+    __syncwarp();
+    if (lane == 0)
+      for (int i = 0; i < p.pro_stages; ++i) mbar_arrive(&empty[i]);
+    if (pro_landed) {
+      slot = p.pro_stages % S;
+      parity = (uint32_t)((p.pro_stages / S) & 1);
+      consumed = p.pro_stages;
+    }
+    if (threadIdx.x == 0) dec_trace(p, 1);
+    if (s_abort) ok = false;
+
+    It it;
+    it_start(it, p, b);
+    if (ok)
+      ok = consume_phase<MT, GS>(p, p.A, 0, it, b, slice, lane, tiles, auxs, full, empty, slot,
+                                 parity, consumed, rec0, false, tag, abort);
+    if (threadIdx.x == 0) dec_trace(p, 2);
+    if (p.ffn) {
+      // the records of this CTA's phase-B items: warp w builds items w, w + 8, ...
+      if (ok && b < p.B.ctas) {
+        It bi;
+        bi.ph = 1;
+        it_seek(bi, p, b);
+        for (int i = 0; bi.ph == 1 && ok; ++i) {
+          if (i % kNC == warp)
+            ok = build_h_record<MT, GS>(p, bi.grp, p.h_out && bi.cu == 0 && bi.s0 == 0,
+                                        recb + (size_t)i * p.frag_bytes, tag, lane, abort);
+          it_next(bi, p, b);
+        }
+      }
+      if (!ok) *abort = 1;
+      named_barrier(1, kNC * 32);
+      if (*abort) ok = false;
+      if (threadIdx.x == 0) dec_trace(p, 3);
+      if (ok)
+        ok = consume_phase<MT, GS>(p, p.B, 1, it, b, slice, lane, tiles, auxs, full, empty, slot,
+                                   parity, consumed, recb, true, tag, abort);
+      if (threadIdx.x == 0) dec_trace(p, 4);
+    }
+    if (!ok) *abort = 1;
+    // the y reduction tasks of this CTA (8 columns each)
+    const DecPhase& L = p.ffn ? p.B : p.A;
+    for (int t = (int)b + (int)gridDim.x * warp; ok && t < p.red_tasks; t += (int)gridDim.x * kNC)
+      ok = reduce_task<MT>(p, L, t, tag, lane, abort);
+    if (threadIdx.x == 0) dec_trace(p, 5);
+  }
+  __syncthreads();
+  if (warp < kNC) {
+    // after an abort: wait for the stages armed but not consumed, so no copy is in flight when
+    // the CTA exits
+    const long long armed = s_armed;
+    for (long long G = consumed; G < armed; ++G) {
+      dec_wait_full(&full[slot], parity, &s_never, p.err, p.timeout_ns, lane);
+      if (++slot == S) {
+        slot = 0;
+        parity ^= 1u;
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (unsigned j = b; j < (unsigned)kDecEpochSlots; j += gridDim.x) p.epoch[j] = tag;
+    dec_trace(p, 6);
+  }
+}
+
+template <int MT, int GS>
+cudaError_t dec_launch_mt(const TmapPack& maps, const DecodeParams& p, int grid, size_t smem,
+                          cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, int4_decode_kernel<MT, GS>, maps, p);
+}
+
+template <int MT, int GS>
+cudaError_t dec_prepare_mt(size_t smem, int* blocks) {
+  auto kern = int4_decode_kernel<MT, GS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kern, kDecThreads, smem);
+}
+
+template <int MT>
+cudaError_t dec_occupancy_gs(int gs, size_t smem, int* blocks) {
+  switch (gs) {
+    case 16: return dec_prepare_mt<MT, 16>(smem, blocks);
+    case 32: return dec_prepare_mt<MT, 32>(smem, blocks);
+    case 64: return dec_prepare_mt<MT, 64>(smem, blocks);
+    case 128: return dec_prepare_mt<MT, 128>(smem, blocks);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int MT>
+cudaError_t dec_launch_gs(int gs, const TmapPack& maps, const DecodeParams& p, int grid,
+                          size_t smem, cudaStream_t stream) {
+  switch (gs) {
+    case 16: return dec_launch_mt<MT, 16>(maps, p, grid, smem, stream);
+    case 32: return dec_launch_mt<MT, 32>(maps, p, grid, smem, stream);
+    case 64: return dec_launch_mt<MT, 64>(maps, p, grid, smem, stream);
+    case 128: return dec_launch_mt<MT, 128>(maps, p, grid, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+size_t decode_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes,
+                         int recb_bytes) {
+  return 1024 + (size_t)stages * ((size_t)tile_stage_bytes + aux_stage_bytes + 16) +
+         (size_t)rec0_bytes + (size_t)recb_bytes;
+}
+
+// The attribute and occupancy query are redone only when an instantiation is launched with
+// another shared-memory size than its last one on a device.
+cudaError_t decode_occupancy(int mt, int gs, size_t smem, int* blocks) {
+  constexpr int kMaxDevices = 64;
+  struct Last {
+    size_t smem;
+    int blocks;
+  };
+  static Last last[kMaxDevices][2][4] = {};
+  const int mi = mt == 1 ? 0 : mt == 2 ? 1 : -1;
+  const int gi = gs == 16 ? 0 : gs == 32 ? 1 : gs == 64 ? 2 : gs == 128 ? 3 : -1;
+  if (mi < 0 || gi < 0) return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  Last* L = dev >= 0 && dev < kMaxDevices ? &last[dev][mi][gi] : nullptr;
+  if (L && L->blocks > 0 && L->smem == smem) {
+    *blocks = L->blocks;
+    return cudaSuccess;
+  }
+  e = mt == 1 ? dec_occupancy_gs<1>(gs, smem, blocks) : dec_occupancy_gs<2>(gs, smem, blocks);
+  if (L) *L = (e == cudaSuccess) ? Last{smem, *blocks} : Last{0, 0};
+  return e;
+}
+
+cudaError_t decode_launch(int mt, int gs, const TmapPack& maps, const DecodeParams& p, int grid,
+                          size_t smem, cudaStream_t stream) {
+  switch (mt) {
+    case 1: return dec_launch_gs<1>(gs, maps, p, grid, smem, stream);
+    case 2: return dec_launch_gs<2>(gs, maps, p, grid, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace tk

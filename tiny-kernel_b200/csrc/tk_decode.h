@@ -1,0 +1,81 @@
+// tk_decode.h -- parameters of the batch 1-2 decode kernel (tk_decode.cu).
+//
+// One persistent, cooperative launch (one CTA per SM) computes either
+//   qmatmul_int4 (src/kernels/shaders.zig:442-501):  phase A = y[m][N] = x . W
+// or the INT4 Llama FFN (src/bench.zig:266-341 + the down projection and residual of
+// src/model/llama.zig:220-231):
+//   prologue rmsnorm(x) -> phase A gate/up -> h = silu(gate) * up -> phase B down (+ x).
+// Work is split stream-K over k-steps (16 k values) of 1024-column tiles, as in the streaming
+// engine (tk_engine.h), but the split-K exchange is counter-free: every segment of partial sums
+// is stored as (value, tag) pairs in one 64-bit word, the tag being the launch's epoch, so a
+// reader knows a value is this launch's by looking at the value itself -- no counters, fences
+// or flags between the producer of a partial and its reader, and nothing to reset between
+// launches.  The phase-B records (h) are built by the consumer warps of every CTA straight from
+// the gate/up partials; the output y is reduced by 32-column tasks spread over all CTAs.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "tk_engine.h"
+
+namespace tk {
+
+constexpr int kDecConsumers = 8;                      // consumer warps (one per 128-col slice)
+constexpr int kDecThreads = (kDecConsumers + 1) * 32;  // + the producer warp
+constexpr int kDecEpochSlots = 1024;  // launch counters: CTA b reads slot b, writes b + k*grid
+constexpr int kDecMaxItemsB = 64;     // phase-B items of one CTA whose records live in smem
+constexpr int kDecReduceBatch = 16;   // partials loaded per batch by a reduction task
+
+// error bits of the device error word (shared with the engine's)
+constexpr unsigned kErrDecPoll = 16u;  // a tagged partial never arrived
+
+struct DecPhase {
+  int K, N;           // contraction size and output columns
+  int nmat;           // 1, or 2 (gate and up at the same columns)
+  int tiles;          // ceil(N / 1024)
+  int groups, spg;    // K / group size, k-steps per group
+  unsigned units;     // tiles * nmat * groups * spg
+  unsigned ctas;      // min(grid, units): CTAs that hold a range of this phase
+  int map_base;       // tensor maps of matrix i: map[map_base + 2i] (group box), +1 (k-step box)
+  const uint16_t* scales[2];
+  const uint8_t* zeros[2];
+  unsigned long long* part;  // tagged partial sums [tiles * nmat][maxseg][MT][1024]
+  int maxseg;
+};
+
+struct DecodeParams {
+  int m;     // live rows (<= MT)
+  int ffn;   // 1: A is gate/up and B the down projection; 0: A only (qmatmul_int4)
+  DecPhase A, B;
+  const float* x;  // [m][ldx], K = A.K
+  int ldx;
+  const float* norm_w;  // non-null: rmsnorm(x) with eps first (the FFN)
+  float eps;
+  float* out;  // y [m][ldo] of the last phase
+  int ldo;
+  const float* residual;  // optional, added to y
+  int ldr;
+  float* h_out;  // optional f32 h [m][ldh]
+  int ldh;
+  // shared memory: S stages of (tile | aux), then the records
+  int stages, tile_stage_bytes, aux_stage_bytes;
+  int pro_stages;  // the first stages hold the prologue copies: x rows, then the norm weight
+  int frag_bytes;  // record bytes per group
+  int recb_items;  // phase-B records per CTA (the largest item count of a CTA's range)
+  int red_tasks;   // 32-column reduction tasks of the last phase
+  unsigned* epoch;  // [kDecEpochSlots]
+  unsigned* err;
+  unsigned long long timeout_ns;
+  unsigned long long* trace;  // optional [grid][kTraceEvents] global-timer stamps
+};
+
+// Dynamic shared memory of a launch with these sizes (1024-byte alignment slack included).
+size_t decode_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes,
+                         int recb_bytes);
+cudaError_t decode_occupancy(int mt, int gs, size_t smem, int* blocks);
+cudaError_t decode_launch(int mt, int gs, const TmapPack& maps, const DecodeParams& p, int grid,
+                          size_t smem, cudaStream_t stream);
+
+}  // namespace tk

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "../../include/tk_cuda.h"
+#include "tk_decode.h"
 #include "tk_engine.h"
 #include "tk_internal.h"
 
@@ -102,6 +103,8 @@ struct tk_device {
   int gemm_enabled = 1;  // TK_GEMM=0 routes every batch through the engine
   int engine_ctas = 0;    // TK_ENGINE_CTAS: CTAs of the engine's launches (0: one per SM)
   int down_prefetch = 1;  // TK_DOWN_PREFETCH=0 turns off the L2 prefetch of the down projection
+  int decode_enabled = 1;  // TK_DECODE=0 routes batch 1-2 through the streaming engine instead
+  ScratchBuf dec;          // decode kernel: launch epochs + tagged partial sums of both phases
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   unsigned long long launches = 0;      // kernels enqueued through this device
   // timed-out peer-memory exchanges seen by tk_device_check_error: a tk_tp group created before
@@ -480,6 +483,174 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
   return launch_engine(d, mt, maps, p, st, (int)Wtot);
 }
 
+// ---- batch 1-2: the decode kernel (tk_decode.cu) ---------------------------------------------
+
+constexpr int kDecSmemLimit = 227 * 1024;  // B200 opt-in shared memory per block
+constexpr int kDefaultGrid = 148;          // B200 SMs (the path queries assume the full device)
+
+// One phase of the decode kernel over K x N with nmat matrices on `grid` CTAs.
+void dec_fill(DecPhase& P, int K, int N, int gs, int nmat, int grid) {
+  std::memset(&P, 0, sizeof(P));
+  P.K = K;
+  P.N = N;
+  P.nmat = nmat;
+  P.tiles = (N + kWideCols - 1) / kWideCols;
+  P.groups = K / gs;
+  P.spg = gs / 16;
+  P.units = (unsigned)((long long)P.tiles * nmat * P.groups * P.spg);
+  P.ctas = std::min<unsigned>((unsigned)grid, P.units);
+  const long long per = (long long)P.groups * P.spg;
+  int mx = 1;
+  for (long long cu = 0; cu < (long long)P.tiles * nmat; ++cu) {
+    const long long a = cu * per;
+    const int ns = (int)(warp_of_unit_h(a + per - 1, P.units, P.ctas) - warp_of_unit_h(a, P.units, P.ctas) + 1);
+    mx = std::max(mx, ns);
+  }
+  P.maxseg = mx;
+}
+
+// The most items (groups) any CTA's range of phase P touches.
+int dec_max_items(const DecPhase& P) {
+  int mx = 0;
+  for (unsigned b = 0; b < P.ctas; ++b) {
+    const unsigned long long beg = (unsigned long long)P.units * b / P.ctas;
+    const unsigned long long end = (unsigned long long)P.units * (b + 1) / P.ctas;
+    mx = std::max(mx, (int)((end - 1) / P.spg - beg / P.spg + 1));
+  }
+  return mx;
+}
+
+struct DecPlan {
+  int stages = 0, pro_stages = 0, tile_stage_bytes = 0, aux_stage_bytes = 0;
+  int recb_items = 0, frag_bytes = 0;
+  size_t smem = 0;
+};
+
+// Shared-memory plan of a decode launch; false when the shape does not fit (the caller then takes
+// the streaming engine).
+bool dec_plan(const DecPhase& A, const DecPhase* B, int m, int mt, int gs, bool norm, int smem_limit,
+              DecPlan* out) {
+  DecPlan pl;
+  pl.tile_stage_bytes = ((gs / 16) * kStepRows * kRowBytes + 127) & ~127;
+  pl.aux_stage_bytes = kSlices * (kScaleBytes + kZeroBytes);
+  pl.frag_bytes = record_bytes(gs, mt);
+  pl.recb_items = B ? dec_max_items(*B) : 0;
+  if (pl.recb_items > kDecMaxItemsB) return false;
+  const long long pro = (long long)A.K * 4 * (m + (norm ? 1 : 0));
+  pl.pro_stages = (int)((pro + pl.tile_stage_bytes - 1) / pl.tile_stage_bytes);
+  const int rec0 = A.groups * pl.frag_bytes, recb = pl.recb_items * pl.frag_bytes;
+  for (int s = kMaxStages; s >= 2; --s) {
+    const size_t need = decode_smem_bytes(s, pl.tile_stage_bytes, pl.aux_stage_bytes, rec0, recb);
+    if (need <= (size_t)smem_limit) {
+      pl.stages = s;
+      pl.smem = need;
+      break;
+    }
+  }
+  if (pl.stages < 2 || pl.pro_stages >= pl.stages) return false;
+  // 32-bit stream-K arithmetic in the kernel
+  if ((long long)A.units * A.ctas >= (1LL << 31)) return false;
+  if (B && (long long)B->units * B->ctas >= (1LL << 31)) return false;
+  *out = pl;
+  return true;
+}
+
+// Can the decode kernel take this call (default device settings)?
+bool decode_shape(int m, int k, int n, int inter, int gs, int grid, bool ffn) {
+  if (m < 1 || m > 2 || !(gs == 16 || gs == 32 || gs == 64 || gs == 128)) return false;
+  DecPhase A, B;
+  DecPlan pl;
+  if (ffn) {
+    dec_fill(A, k, inter, gs, 2, grid);
+    dec_fill(B, inter, k, gs, 1, grid);
+    return dec_plan(A, &B, m, m, gs, true, kDecSmemLimit - kStaticSmemReserve, &pl);
+  }
+  dec_fill(A, k, n, gs, 1, grid);
+  return dec_plan(A, nullptr, m, m, gs, false, kDecSmemLimit - kStaticSmemReserve, &pl);
+}
+
+// One decode launch for m <= 2 rows: qmatmul_int4 (gate == nullptr) or the FFN.  Returns
+// TK_ERR_UNSUPPORTED, before enqueuing anything, when the shape does not fit the kernel.
+int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
+               const tk_int4_matrix* a0, const tk_int4_matrix* a1, const tk_int4_matrix* down,
+               float* out, float* h_out, int m, int k, int n, int inter, int gs, bool residual,
+               cudaStream_t st) {
+  const bool ffn = down != nullptr;
+  const int mt = m;  // instantiations for 1 and 2 rows
+  const int grid = engine_grid(d);
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.m = m;
+  p.ffn = ffn ? 1 : 0;
+  if (ffn) {
+    dec_fill(p.A, k, inter, gs, 2, grid);
+    dec_fill(p.B, inter, k, gs, 1, grid);
+  } else {
+    dec_fill(p.A, k, n, gs, 1, grid);
+  }
+  DecPlan pl;
+  if (!dec_plan(p.A, ffn ? &p.B : nullptr, m, mt, gs, ffn, d->smem_optin - kStaticSmemReserve, &pl))
+    return fail(TK_ERR_UNSUPPORTED, "shape does not fit the decode kernel");
+  if (d->stages_override > 0 && d->stages_override < pl.stages && d->stages_override > pl.pro_stages) {
+    pl.stages = d->stages_override;
+    pl.smem = decode_smem_bytes(pl.stages, pl.tile_stage_bytes, pl.aux_stage_bytes,
+                                p.A.groups * pl.frag_bytes, pl.recb_items * pl.frag_bytes);
+  }
+  // scratch: epochs, then the tagged partials of A and of B
+  const size_t epoch_bytes = kDecEpochSlots * sizeof(unsigned);
+  const size_t partA = (size_t)p.A.tiles * p.A.nmat * p.A.maxseg * mt * kWideCols * 8;
+  const size_t partB = ffn ? (size_t)p.B.tiles * p.B.maxseg * mt * kWideCols * 8 : 0;
+  int stt = scratch_ensure(d, d->dec, epoch_bytes + partA + partB);
+  if (stt != TK_OK) return stt;
+  uint8_t* base = static_cast<uint8_t*>(d->dec.ptr);
+  p.epoch = reinterpret_cast<unsigned*>(base);
+  p.A.part = reinterpret_cast<unsigned long long*>(base + epoch_bytes);
+  p.B.part = ffn ? reinterpret_cast<unsigned long long*>(base + epoch_bytes + partA) : nullptr;
+  TmapPack maps;
+  std::memset(&maps, 0, sizeof(maps));
+  p.A.map_base = 0;
+  p.A.scales[0] = a0->scales;
+  p.A.zeros[0] = a0->zeros;
+  if ((stt = matrix_tmaps(d, a0->w_packed, ffn ? inter : n, k, gs, maps, 0)) != TK_OK) return stt;
+  if (ffn) {
+    p.A.scales[1] = a1->scales;
+    p.A.zeros[1] = a1->zeros;
+    if ((stt = matrix_tmaps(d, a1->w_packed, inter, k, gs, maps, 2)) != TK_OK) return stt;
+    p.B.map_base = 4;
+    p.B.scales[0] = down->scales;
+    p.B.zeros[0] = down->zeros;
+    if ((stt = matrix_tmaps(d, down->w_packed, k, inter, gs, maps, 4)) != TK_OK) return stt;
+  }
+  p.x = x;
+  p.ldx = k;
+  p.norm_w = ffn ? norm_w : nullptr;
+  p.eps = eps;
+  const int n_out = ffn ? k : n;
+  p.out = out;
+  p.ldo = n_out;
+  p.residual = residual ? x : nullptr;
+  p.ldr = k;
+  p.h_out = ffn ? h_out : nullptr;
+  p.ldh = inter;
+  p.stages = pl.stages;
+  p.tile_stage_bytes = pl.tile_stage_bytes;
+  p.aux_stage_bytes = pl.aux_stage_bytes;
+  p.pro_stages = pl.pro_stages;
+  p.frag_bytes = pl.frag_bytes;
+  p.recb_items = pl.recb_items;
+  p.red_tasks = n_out / 8;
+  p.err = d->err;
+  p.timeout_ns = d->timeout_ns;
+  p.trace = d->trace;
+  if (d->trace)
+    TK_CUDA_TRY(cudaMemsetAsync(d->trace, 0, (size_t)d->sm_count * kTraceEvents * 8, st));
+  int blocks = 0;
+  TK_CUDA_TRY(decode_occupancy(mt, gs, pl.smem, &blocks));
+  if (blocks < 1) return fail(TK_ERR_UNSUPPORTED, "decode kernel cannot be resident");
+  TK_LAUNCH(d, decode_launch(mt, gs, maps, p, grid, pl.smem, st));
+  return TK_OK;
+}
+
 // ---- batch >= 16: the tcgen05 GEMM path (tk_gemm.cu) ----------------------------------------
 
 constexpr int kGemmMinRows = 16;
@@ -775,6 +946,7 @@ int tk_device_create(int ordinal, tk_device** out) {
   if (const char* env = std::getenv("TK_GEMM")) d->gemm_enabled = std::atoi(env);
   if (const char* env = std::getenv("TK_DOWN_PREFETCH")) d->down_prefetch = std::atoi(env);
   if (const char* env = std::getenv("TK_ENGINE_CTAS")) d->engine_ctas = std::atoi(env);
+  if (const char* env = std::getenv("TK_DECODE")) d->decode_enabled = std::atoi(env);
   if (const char* env = std::getenv("TK_WAIT_TIMEOUT_MS"))
     d->timeout_ns = (unsigned long long)std::atoll(env) * 1000000ull;
   if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -795,7 +967,7 @@ void tk_device_destroy(tk_device* d) {
   cudaSetDevice(d->ordinal);
   if (d->stream) cudaStreamSynchronize(d->stream);
   for (auto* b : {&d->frag[0], &d->partials[0], &d->partials[1], &d->counters[0],
-                  &d->counters[1], &d->g_x16, &d->g_h16, &d->g_part})
+                  &d->counters[1], &d->g_x16, &d->g_h16, &d->g_part, &d->dec})
     if (b->ptr) cudaFree(b->ptr);
   if (d->sync) cudaFree(d->sync);
   if (d->err) cudaFree(d->err);
@@ -827,7 +999,7 @@ int tk_device_check_error(tk_device* d) {
   TK_CUDA_TRY(cudaDeviceSynchronize());
   TK_CUDA_TRY(cudaMemset(d->err, 0, 256));
   TK_CUDA_TRY(cudaMemset(d->sync, 0, sizeof(SyncState)));
-  for (auto* b : {&d->counters[0], &d->counters[1]})
+  for (auto* b : {&d->counters[0], &d->counters[1], &d->dec})
     if (b->ptr) TK_CUDA_TRY(cudaMemset(b->ptr, 0, b->cap));
   return fail(TK_ERR_TIMEOUT, "device-side bounded wait gave up (error bits 0x%x)", h);
 }
@@ -1027,7 +1199,8 @@ int tk_softmax_sample(tk_device* d, const float* logits, float* probs, uint32_t*
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
   if (m == 0 || k == 0 || n == 0 || gs == 0 || gs % 8 || k % gs || n % 2) return -1;
   if (!engine_shape(k, n, gs)) return 0;
-  return m >= kGemmMinRows && gemm_shape(k, n, gs, false) ? 2 : 1;
+  if (m >= kGemmMinRows && gemm_shape(k, n, gs, false)) return 2;
+  return decode_shape((int)m, (int)k, (int)n, 0, (int)gs, kDefaultGrid, false) ? 3 : 1;
 }
 
 int tk_int4_ffn_path(uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs) {
@@ -1035,10 +1208,9 @@ int tk_int4_ffn_path(uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs) {
       hidden % 2 || inter % 2)
     return -1;
   if (!engine_shape(hidden, inter, gs) || !engine_shape(inter, hidden, gs)) return 0;
-  return m >= kGemmMinRows && gemm_shape(hidden, inter, gs, true) &&
-                 gemm_shape(inter, hidden, gs, false)
-             ? 2
-             : 1;
+  if (m >= kGemmMinRows && gemm_shape(hidden, inter, gs, true) && gemm_shape(inter, hidden, gs, false))
+    return 2;
+  return decode_shape((int)m, (int)hidden, 0, (int)inter, (int)gs, kDefaultGrid, true) ? 3 : 1;
 }
 
 int tk_qmatmul_int4_async(tk_device* d, const float* x, const uint8_t* w, const uint16_t* s,
@@ -1060,6 +1232,13 @@ int tk_qmatmul_int4_async(tk_device* d, const float* x, const uint8_t* w, const 
     return qmatmul_gemm(d, x, w, s, z, out, (int)m, (int)k, (int)n, (int)gs, cs);
   for (uint32_t r = 0; r < m; r += 4) {
     const uint32_t mm = std::min<uint32_t>(4, m - r);
+    if (mm <= 2 && d->decode_enabled) {
+      const tk_int4_matrix a{w, s, z};
+      st = decode_run(d, x + (size_t)r * k, nullptr, 0.f, &a, nullptr, nullptr, out + (size_t)r * n,
+                      nullptr, (int)mm, (int)k, (int)n, 0, (int)gs, false, cs);
+      if (st == TK_OK) continue;
+      if (st != TK_ERR_UNSUPPORTED) return st;
+    }
     st = qmatmul_engine_chunk(d, x + (size_t)r * k, w, s, z, out + (size_t)r * n, (int)mm, (int)k,
                               (int)n, (int)gs, cs);
     if (st != TK_OK) return st;
@@ -1166,6 +1345,13 @@ int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const t
   if (fast) {
     for (uint32_t r = 0; r < m; r += 4) {
       const uint32_t mm = std::min<uint32_t>(4, m - r);
+      if (mm <= 2 && d->decode_enabled) {
+        st = decode_run(d, x + (size_t)r * hidden, norm_w, eps, gate, up, down,
+                        out + (size_t)r * hidden, h_out ? h_out + (size_t)r * inter : nullptr,
+                        (int)mm, (int)hidden, 0, (int)inter, (int)gs, residual, cs);
+        if (st == TK_OK) continue;
+        if (st != TK_ERR_UNSUPPORTED) return st;
+      }
       st = ffn_engine_chunk(d, x + (size_t)r * hidden, norm_w, gate, up, down,
                             out + (size_t)r * hidden, h_out ? h_out + (size_t)r * inter : nullptr,
                             (int)mm, (int)hidden, (int)inter, (int)gs, eps, residual, cs);

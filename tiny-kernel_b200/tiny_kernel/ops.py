@@ -153,8 +153,8 @@ def dequant_int4(device, w_packed, scales, zeros, out, k, n, group_size):
 
 
 def path(m, k, n, group_size) -> int:
-    """qmatmul_int4's path: 2 = tcgen05 GEMM, 1 = streaming engine, 0 = CUDA-core fallback,
-    -1 = invalid shape."""
+    """qmatmul_int4's path: 3 = batch 1-2 decode kernel, 2 = tcgen05 GEMM, 1 = streaming engine,
+    0 = CUDA-core fallback, -1 = invalid shape."""
     return _lib.lib().tk_qmatmul_int4_path(int(m), int(k), int(n), int(group_size))
 
 
