@@ -97,3 +97,29 @@ def test_tp_id_before_torch_import_keeps_torch_loadable():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
                        timeout=600)
     assert r.returncode == 0 and r.stdout.startswith("ok"), r.stderr[-2000:]
+
+
+def test_zig_shims_call_only_exported_symbols():
+    """The Zig kernel API files (tiny-kernel_b200/zig, not compiled here: no Zig toolchain) call
+    only entry points that include/tk_cuda.h declares and libtkcuda exports, and keep the
+    reference's struct names and forward() methods."""
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    zdir = os.path.join(root, "tiny-kernel_b200", "zig", "src")
+    header = open(os.path.join(root, "include", "tk_cuda.h")).read()
+    L = _lib.lib()
+    called = set()
+    text = ""
+    for dirpath, _, files in os.walk(zdir):
+        for f in files:
+            if f.endswith(".zig"):
+                t = open(os.path.join(dirpath, f)).read()
+                text += t
+                called |= set(re.findall(r"\bc\.(tk_[a-z0-9_]+)\(", t))
+    assert len(called) >= 12
+    for name in sorted(called):
+        assert re.search(rf"\b{name}\s*\(", header), name
+        assert hasattr(L, name), name
+    for struct in ("QMatMulInt4", "RMSNorm", "FusedRMSNormRoPE", "FusedSiluMul", "Matvec",
+                   "MatvecDual", "FusedInt4FFN"):
+        assert re.search(rf"pub const {struct} = struct", text), struct
