@@ -305,11 +305,16 @@ int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *sca
  * sm_count * TK_TRACE_EVENTS global-timer stamps (ns) per CTA: start, prologue done,
  * phase-0 barrier passed, phase-0 items done, phase-1 barrier passed, phase-1 items done,
  * end, producer first issue, producer last issue, first stage landed (0 = not reached).
+ * A launch of the batch 1-2 decode kernel uses the slots as: start, prologue records done, phase A
+ * done, phase-B records done, phase B done, reduction tasks done, end, producer first issue,
+ * producer last issue, first phase-B stage in hand (all ns), then consumer warp 0's ns spent
+ * waiting for stages in phase A and in phase B, the CTA's phase-A and phase-B item counts, and the
+ * ns at which the last phase-B stage was in hand.
  * A launch of the batch >= 16 GEMM overwrites the buffer with SM-clock cycle counts instead,
  * for CTAs x + X * (y + Y * z) below sm_count: TMA producer waiting for free ring stages,
  * producer total, MMA issuer waiting for dequantised tiles, MMA waiting for TMA stages, MMA
  * total, first dequantiser warp waiting for TMA stages, waiting for free A stages, its total. */
-#define TK_TRACE_EVENTS 10
+#define TK_TRACE_EVENTS 16
 int tk_device_trace_enable(tk_device *dev, int enable);
 int tk_device_trace_read(tk_device *dev, uint64_t *out, size_t max_values, size_t *n_values);
 

@@ -209,7 +209,8 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
                               unsigned b, int slice, int lane, uint8_t* tiles, uint8_t* auxs,
                               uint64_t* full, uint64_t* empty, int& slot, uint32_t& parity,
                               long long& consumed, const uint8_t* rec, bool rec_by_item,
-                              unsigned tag, volatile int* abort) {
+                              unsigned tag, volatile int* abort, unsigned long long* wait_ns,
+                              unsigned long long* first_ns, unsigned long long* last_ns) {
   constexpr int R = GS / 2;                 // packed rows per group
   constexpr int HB = R <= 32 ? R / 2 : 16;  // rows per chunk
   constexpr int NCH = R / HB;               // chunks per item (2 or 4)
@@ -226,7 +227,18 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
   float y[4 * MT];
 #pragma unroll
   for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
-  if (!dec_wait_full(&full[slot], parity, abort, p.err, p.timeout_ns, lane)) return false;
+  // stage waits, timed for the trace (consumer warp 0 when tracing)
+  auto wait_stage = [&](int sl, uint32_t par) -> bool {
+    if (!wait_ns) return dec_wait_full(&full[sl], par, abort, p.err, p.timeout_ns, lane);
+    const unsigned long long t0 = global_timer_ns();
+    const bool r = dec_wait_full(&full[sl], par, abort, p.err, p.timeout_ns, lane);
+    const unsigned long long t1 = global_timer_ns();
+    *wait_ns += t1 - t0;
+    *last_ns = t1;
+    return r;
+  };
+  if (!wait_stage(slot, parity)) return false;
+  if (wait_ns) *first_ns = global_timer_ns();
   {
     const uint8_t* r = item_rec(it);
     dp_load_meta<MT, GS>(stage_aux(slot), r, slice, lane, it.s0, it.s1, Mc);
@@ -267,8 +279,7 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
         dp_load_x<MT, HB>(r, tok_stride, (c + 2) * HB, XA);
       } else if (prefetch) {
         // the next item's first chunk while this item's last chunk computes
-        if (!__all_sync(0xffffffffu, nready) &&
-            !dec_wait_full(&full[nslot], npar, abort, p.err, p.timeout_ns, lane)) {
+        if (!__all_sync(0xffffffffu, nready) && !wait_stage(nslot, npar)) {
           ok = false;
         } else {
           const uint8_t* nr = item_rec(nx);
@@ -305,7 +316,7 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
       return true;
     }
     if (!next_loaded) {
-      if (!dec_wait_full(&full[slot], parity, abort, p.err, p.timeout_ns, lane)) return false;
+      if (!wait_stage(slot, parity)) return false;
       const uint8_t* nr = item_rec(nx);
       dp_load_meta<MT, GS>(stage_aux(slot), nr, slice, lane, nx.s0, nx.s1, Mn);
       dp_load_rows<HB>(stage_tile(slot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
@@ -638,10 +649,21 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
     It it;
     it_start(it, p, b);
+    // trace of consumer warp 0: stage waits per phase, item counts, first / last phase-B stage
+    const bool tw = p.trace && warp == 0;
+    unsigned long long wA = 0, wB = 0, fB = 0, lB = 0, lA = 0, fA = 0;
+    const int nA = it.ph == 0 ? it.n : 0;
     if (ok)
       ok = consume_phase<MT, GS>(p, p.A, 0, it, b, slice, lane, tiles, auxs, full, empty, slot,
-                                 parity, consumed, rec0, false, tag, abort);
-    if (threadIdx.x == 0) dec_trace(p, 2);
+                                 parity, consumed, rec0, false, tag, abort, tw ? &wA : nullptr,
+                                 &fA, &lA);
+    if (threadIdx.x == 0) {
+      dec_trace(p, 2);
+      if (p.trace) {
+        p.trace[(size_t)blockIdx.x * kTraceEvents + 10] = wA;
+        p.trace[(size_t)blockIdx.x * kTraceEvents + 12] = (unsigned long long)nA;
+      }
+    }
     if (p.ffn) {
       // the records of this CTA's phase-B items: warp w builds items w, w + 8, ...
       if (ok && b < p.B.ctas) {
@@ -659,10 +681,19 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       named_barrier(1, kNC * 32);
       if (*abort) ok = false;
       if (threadIdx.x == 0) dec_trace(p, 3);
+      const int nB = it.ph == 1 ? it.n : 0;
       if (ok)
         ok = consume_phase<MT, GS>(p, p.B, 1, it, b, slice, lane, tiles, auxs, full, empty, slot,
-                                   parity, consumed, recb, true, tag, abort);
+                                   parity, consumed, recb, true, tag, abort, tw ? &wB : nullptr,
+                                   &fB, &lB);
       if (threadIdx.x == 0) dec_trace(p, 4);
+      if (threadIdx.x == 0 && p.trace) {
+        unsigned long long* tr = p.trace + (size_t)blockIdx.x * kTraceEvents;
+        tr[9] = fB;
+        tr[11] = wB;
+        tr[13] = (unsigned long long)nB;
+        tr[14] = lB;
+      }
     }
     if (!ok) *abort = 1;
     // the y reduction tasks of this CTA (8 columns each)

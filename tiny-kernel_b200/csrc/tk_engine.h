@@ -43,7 +43,7 @@ constexpr int kZeroBytes = kTileCols / 2;   // packed zero points of one slice, 
 // Device-side event trace (per CTA, global-timer ns), written when EngineParams.trace
 // is set: start, prologue done, (unused), phase-0 items done, (unused), phase-1 items
 // done, end, producer first issue, producer last issue, first stage landed.
-constexpr int kTraceEvents = 10;
+constexpr int kTraceEvents = 16;
 
 // error bits written to the device error word
 constexpr unsigned kErrTmaWait = 1u;
