@@ -540,7 +540,8 @@ bool dec_plan(const DecPhase& A, const DecPhase* B, int m, int mt, int gs, bool 
   pl.pro_stages = (int)((pro + pl.tile_stage_bytes - 1) / pl.tile_stage_bytes);
   const int rec0 = A.groups * pl.frag_bytes, recb = pl.recb_items * pl.frag_bytes;
   for (int s = kMaxStages; s >= 2; --s) {
-    const size_t need = decode_smem_bytes(s, pl.tile_stage_bytes, pl.aux_stage_bytes, rec0, recb);
+    const size_t need = decode_smem_bytes(s, pl.tile_stage_bytes, pl.aux_stage_bytes, rec0, recb,
+                                          dec_comb_bytes(mt, gs));
     if (need <= (size_t)smem_limit) {
       pl.stages = s;
       pl.smem = need;
@@ -594,7 +595,8 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   if (d->stages_override > 0 && d->stages_override < pl.stages && d->stages_override > pl.pro_stages) {
     pl.stages = d->stages_override;
     pl.smem = decode_smem_bytes(pl.stages, pl.tile_stage_bytes, pl.aux_stage_bytes,
-                                p.A.groups * pl.frag_bytes, pl.recb_items * pl.frag_bytes);
+                                p.A.groups * pl.frag_bytes, pl.recb_items * pl.frag_bytes,
+                                dec_comb_bytes(mt, gs));
   }
   // scratch: epochs, then the tagged partials of A and of B
   const size_t epoch_bytes = kDecEpochSlots * sizeof(unsigned);
