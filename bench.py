@@ -14,9 +14,11 @@ once: by rank 0's kernel, before the all-reduce).
 value     whole-job algorithmic GB/s: FFN bytes (weights + x + norm weight + out) per step
           x steps / max-over-ranks device time; inputs resident in HBM; L2 defeated by
           rotating several weight copies whose total exceeds 3x the L2 size.
-e2e       the same metric through the C ABI with host buffers: every step queues the
-          activation's upload from pinned host memory, the FFN and the output's download on
-          the device's stream and waits once for the result (tk_device_synchronize).
+e2e       the same metric through the C ABI with host buffers, every step: one FFN block on one
+          GPU is one synchronous tk_int4_ffn call with TK_FFN_HOST_IO (the kernel reads x from
+          and writes y to pinned host memory over the host link); the matvec, stacks and
+          tensor parallelism queue the activation's upload from pinned host memory, the step and
+          the output's download on the device's stream and wait once (tk_device_synchronize).
 --impl reference  times the CPU transcription of the reference shaders (oracle/), all host
           threads, on the same workload (the reference itself is Zig + Metal and cannot run
           on this Linux host).
@@ -553,7 +555,17 @@ def main():
     e2e_steps = max(1, min(steps_timed, 2000 // L))
     devstream = torch.cuda.ExternalStream(dev.stream())
 
+    # One FFN block on one GPU: a single synchronous call with x and y in pinned host memory
+    # (TK_FFN_HOST_IO: the kernel reads x and writes y over the host link).  Otherwise (matvec,
+    # stacks, tensor parallel): queue the upload, the step and the download, then wait once.
+    host_io = (not matvec) and L == 1 and pg is None and group is None
+
     def e2e_step(i):
+        if host_io:
+            nw, g, u, d = mats[i % copies][0]
+            ops.int4_ffn(dev, xb_host.ptr, nw, g, u, d, ob_host.ptr, m, hidden, inter, GS, eps=EPS,
+                         host_io=True, sync=True)
+            return
         check(Lb.tk_buffer_upload_async(dev.handle, xd.data_ptr(), xb_host.ptr, xb_host.nbytes,
                                         None))
         res = run_step(i, xd, (xa, xb), False, on=devstream)
@@ -679,7 +691,11 @@ def main():
             "cpu_baseline": cpu_base,
             "e2e": {"value": round(e2e, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": m * hidden * 4, "d2h_bytes_per_step": m * out_cols * 4,
-                    "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 5)},
+                    "steps": e2e_steps, "ms_per_step": round(e2e_ms / e2e_steps, 5),
+                    "how": ("tk_int4_ffn with TK_FFN_HOST_IO, synchronous: the kernel reads x from "
+                            "and writes y to pinned host memory" if host_io else
+                            "tk_buffer_upload_async + the step + tk_buffer_download_async, one "
+                            "tk_device_synchronize")},
             "parity": parity,
             "gpu_launches": steps_timed * launches_per_step,
             "clocks": clk.summary(),

@@ -77,6 +77,12 @@ extern "C" {
 
 /* flags for tk_int4_ffn */
 #define TK_FFN_RESIDUAL 1u /* out = x + FFN(x)  (Llama residual, llama.zig:216-231)  */
+/* x and out are pinned host memory (TK_MEM_HOST, cudaMallocHost or cudaHostRegister'd, mapped
+ * into the device's address space): the batch 1-2 kernel reads x and writes out over the host
+ * link itself, with no staging copies; other paths stage them through device scratch.  h_out,
+ * when given, stays device memory.  The reference's buffers are host-visible shared memory
+ * (StorageModeShared, src/metal/device.zig:109), which is what this flag serves. */
+#define TK_FFN_HOST_IO 2u
 
 typedef struct tk_device tk_device;
 

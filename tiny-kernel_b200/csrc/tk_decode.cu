@@ -1,16 +1,14 @@
 // tk_decode.cu -- the batch 1-2 decode kernel: qmatmul_int4 and the INT4 Llama FFN in one
 // persistent launch per call, with a counter-free split-K exchange (tk_decode.h).
 //
-// Warp roles (one CTA per SM; 16 consumer warps, or 8 at group size 16, and one producer):
-//   last warp (producer) lane 0 issues every copy of the CTA: first the prologue data (x rows and
+// Warp roles (one CTA per SM, 288 threads):
+//   warp 8 (producer)   lane 0 issues every copy of the CTA: first the prologue data (x rows and
 //                       the norm weight, 1-D bulk copies into the first ring stages), then per
 //                       work item the packed rows (2-D TMA box of 1040-byte rows), the f16 scales
 //                       and the packed zero points of a 1024-column tile and one group.  Items of
 //                       phase B are copied as soon as a stage is free: their weights do not
 //                       depend on h, so they land while phase A finishes and h is assembled.
-//   consumer warp w     slice w % 8 = 128 columns of every item, rows of half w / 8 of every
-//                       group (group size >= 32; the two warps of a slice add their sums at
-//                       segment ends), dp2a arithmetic (tk_dp2a.cuh).
+//   warps 0-7 (consumers) slice w = 128 columns of every item, dp2a arithmetic (tk_dp2a.cuh).
 //                       prologue: rmsnorm + the int16 records of every group of x, in smem;
 //                       phase A, then (FFN) the phase-B records: h = silu(gate) * up summed from
 //                       the tagged gate/up partials of the other CTAs, one item per warp, in
@@ -36,6 +34,8 @@ namespace tk {
 
 namespace {
 
+constexpr int kNC = kDecConsumers;
+constexpr int kProducerWarp = kNC;
 
 // CTA whose stream-K range holds unit u (ranges [U*b/W, U*(b+1)/W))
 __device__ __forceinline__ int dec_cta_of_unit(unsigned u, unsigned units, unsigned W) {
@@ -205,85 +205,21 @@ __device__ __forceinline__ bool dec_wait_full(uint64_t* bar, uint32_t par, volat
 // arithmetic; each finished segment's partial sums are stored as tagged words.  Records: the
 // group's (rec_by_item == 0: rec + grp * frag_bytes) or the item's (rec + i * frag_bytes).
 // Returns false on an abort.
-// The ring has no producer warp.  S stages, one full mbarrier each; thread 0 issues the prologue
-// copies and the first items, and afterwards a consumer warp that has read its part of a stage
-// counts it in freed[slot]: the warp that completes the count (the last of the consumer warps)
-// refills the stage with the item one ring length ahead.  Every warp walks the refill sequence
-// (`ahead`) in step, so whichever warp is last knows the item.
-struct Ring {
-  const TmapPack* maps;
-  uint8_t* tiles;
-  uint8_t* auxs;
-  uint64_t* full;
-  int* freed;                  // [S] consumer warps done with the stage's current item
-  unsigned long long* armed;   // ring positions armed so far (for the drain after an abort)
-  uint64_t pol;
-  int nw;                      // consumer warps
-};
-
-__device__ __forceinline__ void ring_issue(const Ring& R, const DecodeParams& p, const It& it,
-                                           int slot) {
-  const DecPhase& P = it.ph == 0 ? p.A : p.B;
-  issue_item(*R.maps, P, it, R.tiles + (size_t)slot * p.tile_stage_bytes,
-             R.auxs + (size_t)slot * p.aux_stage_bytes, &R.full[slot], R.pol);
-  atomicAdd(R.armed, 1ull);
-}
-
-// Shared-memory counter increment with acquire-release semantics at CTA scope: this warp's reads
-// of the stage (ordered before it by __syncwarp) happen before the last warp's refill copy.
-__device__ __forceinline__ int atom_add_acq_rel_smem(int* p, int v) {
-  int old;
-  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;"
-               : "=r"(old)
-               : "r"(smem_addr(p)), "r"(v)
-               : "memory");
-  return old;
-}
-
-// This warp is done reading stage `slot`; the last warp to be done refills it with `ahead`'s
-// item.  Advances `ahead` (every warp, every stage).
-__device__ __forceinline__ void ring_free(const Ring& R, const DecodeParams& p, It& ahead, int slot,
-                                          int lane, unsigned b) {
-  __syncwarp();
-  if (lane == 0 && atom_add_acq_rel_smem(&R.freed[slot], 1) == R.nw - 1) {
-    R.freed[slot] = 0;  // seen by the next round's warps through the full barrier
-    if (ahead.ph < 2) ring_issue(R, p, ahead, slot);
-  }
-  if (ahead.ph < 2) it_next(ahead, p, b);
-}
-
-// Pair exchange of partial sums at segment ends (two consumer warps per slice): the warp of the
-// second half stores its sums, the first half's warp adds them to its own; one mbarrier pair per
-// slice (comb_full: the second half stored, comb_empty: the first half read), bounded waits.
-struct PairXchg {
-  float* buf;           // [kSlices][32 lanes][4 MT] floats
-  uint64_t* full;       // [kSlices]
-  uint64_t* empty;      // [kSlices]
-  int count;            // segment ends this warp has exchanged
-};
-
 template <int MT, int GS>
-__device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, It& it,
-                              unsigned b, int slice, int half, int lane, const Ring& ring,
-                              It& ahead, int& slot, uint32_t& parity, long long& consumed,
-                              const uint8_t* rec,
-                              bool rec_by_item, unsigned tag, volatile int* abort,
-                              PairXchg& px, unsigned long long* wait_ns,
+__device__ __noinline__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, It& it,
+                              unsigned b, int slice, int lane, uint8_t* tiles, uint8_t* auxs,
+                              uint64_t* full, uint64_t* empty, int& slot, uint32_t& parity,
+                              long long& consumed, const uint8_t* rec, bool rec_by_item,
+                              unsigned tag, volatile int* abort, unsigned long long* wait_ns,
                               unsigned long long* first_ns, unsigned long long* last_ns) {
-  constexpr int SPLIT = dec_split(GS);
-  constexpr int R = GS / 2 / SPLIT;         // packed rows of a group this warp takes
+  constexpr int R = GS / 2;                 // packed rows per group
   constexpr int HB = R <= 32 ? R / 2 : 16;  // rows per chunk
   constexpr int NCH = R / HB;               // chunks per item (2 or 4)
-  constexpr int SPH = R / kStepRows;        // k-steps of the group this warp takes
-  const int rbase = half * R;               // first row of this warp's half
   constexpr int tok_stride = dp_tok_stride(GS);
   const int S = p.stages;
   const int fb = p.frag_bytes;
-  uint64_t* full = ring.full;
-  auto stage_tile = [&](int sl) {
-    return ring.tiles + (size_t)sl * p.tile_stage_bytes + slice * kTileCols;
-  };
-  auto stage_aux = [&](int sl) { return ring.auxs + (size_t)sl * p.aux_stage_bytes; };
+  auto stage_tile = [&](int sl) { return tiles + (size_t)sl * p.tile_stage_bytes + slice * kTileCols; };
+  auto stage_aux = [&](int sl) { return auxs + (size_t)sl * p.aux_stage_bytes; };
   auto item_rec = [&](const It& x) { return rec + (size_t)(rec_by_item ? x.i : x.grp) * fb; };
   if (it.ph != ph) return true;
   uint32_t wA[HB], wB[HB];
@@ -302,16 +238,13 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
     *last_ns = t1;
     return r;
   };
-  // this warp's k-steps of an item: [s0, s1) clipped to its half of the group
-  auto hs0 = [&](const It& x) { return max(x.s0, half * SPH); };
-  auto hs1 = [&](const It& x) { return min(x.s1, (half + 1) * SPH); };
   if (!wait_stage(slot, parity)) return false;
   if (wait_ns) *first_ns = global_timer_ns();
   {
     const uint8_t* r = item_rec(it);
-    dp_load_meta<MT, GS>(stage_aux(slot), r, slice, lane, hs0(it), hs1(it), Mc);
-    dp_load_rows<HB>(stage_tile(slot), rbase, it.s0 * kStepRows, it.s1 * kStepRows, lane, wA);
-    dp_load_x<MT, HB>(r, tok_stride, rbase, XA);
+    dp_load_meta<MT, GS>(stage_aux(slot), r, slice, lane, it.s0, it.s1, Mc);
+    dp_load_rows<HB>(stage_tile(slot), 0, it.s0 * kStepRows, it.s1 * kStepRows, lane, wA);
+    dp_load_x<MT, HB>(r, tok_stride, 0, XA);
   }
   for (;;) {
     const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
@@ -332,27 +265,28 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
       for (int i = 0; i < 4; ++i) aL[m][i] = aH[m][i] = 0;
 #pragma unroll
     for (int c = 0; c < NCH; c += 2) {
-      dp_load_rows<HB>(tl, rbase + (c + 1) * HB, r0, r1, lane, wB);
-      dp_load_x<MT, HB>(r, tok_stride, rbase + (c + 1) * HB, XB);
+      dp_load_rows<HB>(tl, (c + 1) * HB, r0, r1, lane, wB);
+      dp_load_x<MT, HB>(r, tok_stride, (c + 1) * HB, XB);
       bool nready = false;
       if (c + 2 == NCH) {
-        // every byte of this warp's part of the stage is loaded: free it
-        ring_free(ring, p, ahead, slot, lane, b);
+        // every byte of this stage is loaded (in issue order before the arrival)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
         if (prefetch) nready = mbar_test_wait(&full[nslot], npar);
       }
       dp_compute<MT, HB>(wA, XA, aL, aH);
       if (c + 2 < NCH) {
-        dp_load_rows<HB>(tl, rbase + (c + 2) * HB, r0, r1, lane, wA);
-        dp_load_x<MT, HB>(r, tok_stride, rbase + (c + 2) * HB, XA);
+        dp_load_rows<HB>(tl, (c + 2) * HB, r0, r1, lane, wA);
+        dp_load_x<MT, HB>(r, tok_stride, (c + 2) * HB, XA);
       } else if (prefetch) {
         // the next item's first chunk while this item's last chunk computes
         if (!__all_sync(0xffffffffu, nready) && !wait_stage(nslot, npar)) {
           ok = false;
         } else {
           const uint8_t* nr = item_rec(nx);
-          dp_load_meta<MT, GS>(stage_aux(nslot), nr, slice, lane, hs0(nx), hs1(nx), Mn);
-          dp_load_rows<HB>(stage_tile(nslot), rbase, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
-          dp_load_x<MT, HB>(nr, tok_stride, rbase, XA);
+          dp_load_meta<MT, GS>(stage_aux(nslot), nr, slice, lane, nx.s0, nx.s1, Mn);
+          dp_load_rows<HB>(stage_tile(nslot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
+          dp_load_x<MT, HB>(nr, tok_stride, 0, XA);
           next_loaded = true;
         }
       }
@@ -363,40 +297,7 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
     slot = nslot;
     parity = npar;
     if (seg_end) {
-      if constexpr (SPLIT == 2) {
-        // the second half's sums join the first half's (in that order: deterministic)
-        float* cb = px.buf + ((size_t)slice * 32 + lane) * 4 * MT;
-        const uint32_t xpar = (uint32_t)(px.count & 1);
-        bool xok = true;
-        if (half == 1) {
-          if (px.count > 0)
-            xok = dec_wait_full(&px.empty[slice], xpar ^ 1u, abort, p.err, p.timeout_ns, lane);
-          if (xok) {
-#pragma unroll
-            for (int i = 0; i < 4 * MT; i += 4)
-              *reinterpret_cast<float4*>(cb + i) = make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&px.full[slice]);
-          }
-        } else {
-          xok = dec_wait_full(&px.full[slice], xpar, abort, p.err, p.timeout_ns, lane);
-          if (xok) {
-#pragma unroll
-            for (int i = 0; i < 4 * MT; i += 4) {
-              const float4 o = *reinterpret_cast<const float4*>(cb + i);
-              y[i] += o.x;
-              y[i + 1] += o.y;
-              y[i + 2] += o.z;
-              y[i + 3] += o.w;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&px.empty[slice]);
-          }
-        }
-        ++px.count;
-        if (!xok) return false;
-      }
-      if (half == 0 && slice < it_slices(P, it)) {
+      if (slice < it_slices(P, it)) {
         int c0 = 0;
         dec_nseg(P, it.cu, &c0);
         const int seg = (int)b - c0;
@@ -418,9 +319,9 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
     if (!next_loaded) {
       if (!wait_stage(slot, parity)) return false;
       const uint8_t* nr = item_rec(nx);
-      dp_load_meta<MT, GS>(stage_aux(slot), nr, slice, lane, hs0(nx), hs1(nx), Mn);
-      dp_load_rows<HB>(stage_tile(slot), rbase, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
-      dp_load_x<MT, HB>(nr, tok_stride, rbase, XA);
+      dp_load_meta<MT, GS>(stage_aux(slot), nr, slice, lane, nx.s0, nx.s1, Mn);
+      dp_load_rows<HB>(stage_tile(slot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
+      dp_load_x<MT, HB>(nr, tok_stride, 0, XA);
     }
     it = nx;
     Mc = Mn;
@@ -452,7 +353,7 @@ __device__ __forceinline__ bool dec_poll_again(uint64_t& t0, volatile int* abort
 // in a fixed tree, so the result's bits do not depend on timing.  Returns false on an abort.
 template <int MT>
 __device__ bool reduce_task(const DecodeParams& p, const DecPhase& L, int task, unsigned tag,
-                            int lane, volatile int* abort) {
+                            int lane, volatile int* abort, const float* res_stash) {
   constexpr int B = kDecReduceBatch;  // segments per lane per batch
   const int col = task * 8 + (lane >> 2), j = lane & 3;
   const int cu = col / kWideCols, cl = col % kWideCols;
@@ -483,7 +384,8 @@ __device__ bool reduce_task(const DecodeParams& p, const DecPhase& L, int task, 
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     if (j == 0 && m < p.m) {
-      if (p.residual) acc = p.residual[(size_t)m * p.ldr + col] + acc;
+      if (p.residual)
+        acc = (res_stash ? res_stash[m * 8 + (lane >> 2)] : p.residual[(size_t)m * p.ldr + col]) + acc;
       p.out[(size_t)m * p.ldo + col] = acc;
     }
   }
@@ -579,37 +481,30 @@ __device__ bool build_h_record(const DecodeParams& p, int grp, bool write_h, uin
 }
 
 template <int MT, int GS>
-__global__ void __launch_bounds__(dec_threads(GS), 1)
+__global__ void __launch_bounds__(kDecThreads, 1)
     int4_decode_kernel(const __grid_constant__ TmapPack maps, const __grid_constant__ DecodeParams p) {
-  constexpr int kNC = dec_consumers(GS);  // consumer warps (all the warps of the CTA)
   extern __shared__ uint8_t smem_raw[];
   __shared__ float s_red[MT * kNC];
   __shared__ float s_rms[MT];
-  __shared__ uint64_t s_xfull[kSlices], s_xempty[kSlices];
-  __shared__ int s_freed[kMaxStages];
-  __shared__ unsigned long long s_armed;  // ring positions armed (prologue stages included)
+  __shared__ volatile long long s_armed;  // items (prologue stages included) armed by the producer
   __shared__ volatile int s_abort;
   __shared__ volatile int s_never;
   __shared__ unsigned s_tag;
+  __shared__ float s_res[kDecMaxTasksPerCta * 8 * MT];  // residual of this CTA's tasks (host x)
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = p.stages, P0 = p.pro_stages;
+  const int S = p.stages;
   uint8_t* tiles = smem;
   uint8_t* auxs = smem + (size_t)S * p.tile_stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(auxs + (size_t)S * p.aux_stage_bytes);
-  uint8_t* rec0 = reinterpret_cast<uint8_t*>(full + 2 * S);  // 16-byte aligned
+  uint64_t* empty = full + S;
+  uint8_t* rec0 = reinterpret_cast<uint8_t*>(empty + S);  // 16-byte aligned (S barriers each)
   uint8_t* recb = rec0 + (size_t)p.A.groups * p.frag_bytes;
-  float* comb = reinterpret_cast<float*>(recb + (size_t)p.recb_items * p.frag_bytes);
   const unsigned b = blockIdx.x;
-  const Ring ring{&maps, tiles, auxs, full, s_freed, &s_armed, l2_evict_first(), kNC};
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
-      s_freed[i] = 0;
-    }
-    for (int i = 0; i < kSlices; ++i) {
-      mbar_init(&s_xfull[i], 1);
-      mbar_init(&s_xempty[i], 1);
+      mbar_init(&empty[i], kNC);
     }
     fence_mbar_init();
     s_armed = 0;
@@ -620,165 +515,233 @@ __global__ void __launch_bounds__(dec_threads(GS), 1)
   }
   __syncthreads();
   const unsigned tag = s_tag;
-  // every warp walks the items twice: `it` (the ring position it consumes) and `ahead` (the item
-  // S positions later, which the stage it frees receives); ring position P0 + i holds item i
-  It it, ahead;
-  it_start(it, p, b);
-  ahead = it;
-  for (int i = 0; i < S - P0 && ahead.ph < 2; ++i) it_next(ahead, p, b);
-  if (threadIdx.x == 0) {
-    // the prologue copies (x rows, then the norm weight) over the first P0 stages' tiles, then
-    // the first items into the other stages
-    const uint32_t xrow = (uint32_t)p.A.K * 4u;
-    const uint32_t total = xrow * (uint32_t)p.m + (p.norm_w ? xrow : 0u);
-    mbar_arrive_expect_tx(&full[0], total);
-    for (int m = 0; m < p.m; ++m)
-      bulk_load(tiles + (size_t)m * xrow, p.x + (size_t)m * p.ldx, xrow, &full[0], ring.pol);
-    if (p.norm_w) bulk_load(tiles + (size_t)p.m * xrow, p.norm_w, xrow, &full[0], ring.pol);
-    for (int i = 1; i < P0; ++i) mbar_arrive(&full[i]);
-    atomicAdd(&s_armed, (unsigned long long)P0);
-    It first = it;
-    for (int sl = P0; sl < S && first.ph < 2; ++sl) {
-      ring_issue(ring, p, first, sl);
-      it_next(first, p, b);
-    }
-    dec_trace(p, 7);
-  }
-  const int slice = warp % kSlices, half = warp / kSlices;
-  volatile int* abort = &s_abort;
-  PairXchg px{comb, s_xfull, s_xempty, 0};
   int slot = 0;
   uint32_t parity = 0;
   long long consumed = 0;
-  // prologue: wait for x (and the norm weight), then the records of every group of x; every warp
-  // takes the same branch (an abort is published before the barrier)
-  if (!dec_wait_full(&full[0], 0, abort, p.err, p.timeout_ns, lane) && lane == 0) *abort = 1;
-  __syncthreads();
-  bool ok = *abort == 0;
-  if (ok) {
-    const float* xs = reinterpret_cast<const float*>(tiles);
-    const float* ws = xs + (size_t)p.m * p.A.K;
-    const int nchunks = p.A.K / kTileCols;
-    float rms[MT];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) rms[m] = 1.f;
-    if (p.norm_w) {
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        float v = 0.f;
-        if (m < p.m)
-          for (int ch = warp; ch < nchunks; ch += kNC) {
-            const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.A.K + ch * kTileCols + 4 * lane);
-            v = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, v))));
-          }
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) s_red[m * kNC + warp] = v;
-      }
-      __syncthreads();
-      if (threadIdx.x < MT) {
-        float tot = 0.f;
-        for (int i = 0; i < kNC; ++i) tot += s_red[threadIdx.x * kNC + i];
-        s_rms[threadIdx.x] = rsqrtf(tot / (float)p.A.K + p.eps);
-      }
-      __syncthreads();
-#pragma unroll
-      for (int m = 0; m < MT; ++m) rms[m] = s_rms[m];
-    }
-    for (int ch = warp; ch < nchunks; ch += kNC) {
-      float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
-      if (p.norm_w) w4 = *reinterpret_cast<const float4*>(ws + ch * kTileCols + 4 * lane);
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (m < p.m) {
-          const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.A.K + ch * kTileCols + 4 * lane);
-          if (p.norm_w) {
-            v[0] = a.x * rms[m] * w4.x;
-            v[1] = a.y * rms[m] * w4.y;
-            v[2] = a.z * rms[m] * w4.z;
-            v[3] = a.w * rms[m] * w4.w;
-          } else {
-            v[0] = a.x;
-            v[1] = a.y;
-            v[2] = a.z;
-            v[3] = a.w;
-          }
-        }
-        build_records_dp<MT>(v, m, GS, rec0 + (size_t)(ch * kTileCols / GS) * p.frag_bytes,
-                             p.frag_bytes, lane, -1);
-      }
-    }
-  }
-  // every warp has read the prologue data and written its records: free the prologue stages
-  __syncthreads();
-  if (ok) {
-    for (int i = 0; i < P0; ++i) ring_free(ring, p, ahead, i, lane, b);
-    slot = P0 % S;
-    parity = (uint32_t)((P0 / S) & 1);
-    consumed = P0;
-  }
-  if (threadIdx.x == 0) dec_trace(p, 1);
 
-  // trace of warp 0: stage waits per phase, item counts, first / last phase-B stage
-  const bool tw = p.trace && warp == 0;
-  unsigned long long wA = 0, wB = 0, fB = 0, lB = 0, lA = 0, fA = 0;
-  const int nA = it.ph == 0 ? it.n : 0;
-  if (ok)
-    ok = consume_phase<MT, GS>(p, p.A, 0, it, b, slice, half, lane, ring, ahead, slot, parity,
-                               consumed, rec0, false, tag, abort, px, tw ? &wA : nullptr, &fA, &lA);
-  if (threadIdx.x == 0) {
-    dec_trace(p, 2);
-    if (p.trace) {
-      p.trace[(size_t)blockIdx.x * kTraceEvents + 10] = wA;
-      p.trace[(size_t)blockIdx.x * kTraceEvents + 12] = (unsigned long long)nA;
+  if (warp == kProducerWarp) {
+    // ------------------------------- producer ---------------------------------------------
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first();
+      const int P0 = p.pro_stages;
+      // prologue: x rows then the norm weight, contiguous over the first P0 stages' tiles
+      {
+        const uint32_t xrow = (uint32_t)p.A.K * 4u;
+        const uint32_t total = (p.x_host ? 0u : xrow * (uint32_t)p.m) + (p.norm_w ? xrow : 0u);
+        if (total) mbar_arrive_expect_tx(&full[0], total);
+        else mbar_arrive(&full[0]);
+        if (!p.x_host)
+          for (int m = 0; m < p.m; ++m)
+            bulk_load(tiles + (size_t)m * xrow, p.x + (size_t)m * p.ldx, xrow, &full[0], pol);
+        if (p.norm_w) bulk_load(tiles + (size_t)p.m * xrow, p.norm_w, xrow, &full[0], pol);
+        for (int i = 1; i < P0; ++i) mbar_arrive(&full[i]);
+        s_armed = P0;
+      }
+      long long G = P0;
+      int ws = P0 % S;
+      uint32_t wround = (uint32_t)(P0 / S);
+      It it;
+      it_start(it, p, b);
+      dec_trace(p, 7);
+      while (it.ph < 2) {
+        if (wround > 0) {
+          // bounded wait for the consumers to free the slot
+          bool ok = mbar_try_wait(&empty[ws], (wround - 1) & 1);
+          if (!ok) {
+            const uint64_t t0 = global_timer_ns();
+            // suspended in the wait (time hint) rather than spinning: the producer shares an SM
+            // sub-partition with two consumer warps
+            while (!(ok = mbar_try_wait_hint(&empty[ws], (wround - 1) & 1, 2000))) {
+              if (s_abort) break;
+              if (global_timer_ns() - t0 > p.timeout_ns) {
+                atomicOr(p.err, kErrTmaWait);
+                s_abort = 1;
+                break;
+              }
+            }
+          }
+          if (!ok) break;
+        }
+        if (s_abort) break;
+        const DecPhase& P = it.ph == 0 ? p.A : p.B;
+        issue_item(maps, P, it, tiles + (size_t)ws * p.tile_stage_bytes,
+                   auxs + (size_t)ws * p.aux_stage_bytes, &full[ws], pol);
+        s_armed = ++G;
+        it_next(it, p, b);
+        if (++ws == S) {
+          ws = 0;
+          ++wround;
+        }
+      }
+      s_armed = G;
+      dec_trace(p, 8);
     }
-  }
-  if (p.ffn) {
-    // the records of this CTA's phase-B items: warp w builds items w, w + kNC, ...
-    if (ok && b < p.B.ctas) {
-      It bi;
-      bi.ph = 1;
-      it_seek(bi, p, b);
-      for (int i = 0; bi.ph == 1 && ok; ++i) {
-        if (i % kNC == warp)
-          ok = build_h_record<MT, GS>(p, bi.grp, p.h_out && bi.cu == 0 && bi.s0 == 0,
-                                      recb + (size_t)i * p.frag_bytes, tag, lane, abort);
-        it_next(bi, p, b);
+    __syncwarp();
+  } else {
+    // ------------------------------- consumers --------------------------------------------
+    const int slice = warp;
+    volatile int* abort = &s_abort;
+    if (p.x_host) {
+      // x over the host link: 16-byte plain loads by the consumer threads into the prologue area
+      const int row4 = p.A.K / 4;
+      for (int i = threadIdx.x; i < p.m * row4; i += kNC * 32) {
+        const int m = i / row4, c = i - m * row4;
+        reinterpret_cast<float4*>(tiles)[i] =
+            reinterpret_cast<const float4*>(p.x + (size_t)m * p.ldx)[c];
+      }
+    }
+    // prologue: wait for x (and the norm weight), then the records of every group of x; the
+    // consumer warps take the same branch (an abort is published before the barrier)
+    if (!dec_wait_full(&full[0], 0, abort, p.err, p.timeout_ns, lane) && lane == 0) *abort = 1;
+    named_barrier(1, kNC * 32);
+    bool ok = *abort == 0;
+    if (p.x_host && p.residual) {
+      // keep the residual of this CTA's reduction tasks (the prologue area is reused)
+      for (int i = threadIdx.x; i < kDecMaxTasksPerCta * 8 * MT; i += kNC * 32) {
+        const int k = i / (8 * MT), m = (i / 8) % MT, c = i % 8;
+        const int t = (int)b + (int)gridDim.x * k;
+        if (t < p.red_tasks && m < p.m)
+          s_res[i] = reinterpret_cast<const float*>(tiles)[(size_t)m * p.A.K + t * 8 + c];
+      }
+    }
+    const bool pro_landed = ok;
+    if (ok) {
+      const float* xs = reinterpret_cast<const float*>(tiles);
+      const float* ws = xs + (size_t)p.m * p.A.K;
+      const int nchunks = p.A.K / kTileCols;
+      float rms[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) rms[m] = 1.f;
+      if (p.norm_w) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float v = 0.f;
+          if (m < p.m)
+            for (int ch = warp; ch < nchunks; ch += kNC) {
+              const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.A.K + ch * kTileCols + 4 * lane);
+              v = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, v))));
+            }
+          for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+          if (lane == 0) s_red[m * kNC + warp] = v;
+        }
+        named_barrier(1, kNC * 32);
+        if (threadIdx.x < MT) {
+          float tot = 0.f;
+          for (int i = 0; i < kNC; ++i) tot += s_red[threadIdx.x * kNC + i];
+          s_rms[threadIdx.x] = rsqrtf(tot / (float)p.A.K + p.eps);
+        }
+        named_barrier(1, kNC * 32);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) rms[m] = s_rms[m];
+      }
+      for (int ch = warp; ch < nchunks; ch += kNC) {
+        float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (p.norm_w) w4 = *reinterpret_cast<const float4*>(ws + ch * kTileCols + 4 * lane);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+          if (m < p.m) {
+            const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.A.K + ch * kTileCols + 4 * lane);
+            if (p.norm_w) {
+              v[0] = a.x * rms[m] * w4.x;
+              v[1] = a.y * rms[m] * w4.y;
+              v[2] = a.z * rms[m] * w4.z;
+              v[3] = a.w * rms[m] * w4.w;
+            } else {
+              v[0] = a.x;
+              v[1] = a.y;
+              v[2] = a.z;
+              v[3] = a.w;
+            }
+          }
+          build_records_dp<MT>(v, m, GS, rec0 + (size_t)(ch * kTileCols / GS) * p.frag_bytes,
+                               p.frag_bytes, lane, -1);
+        }
+      }
+    }
+    // every consumer has read the prologue data and written its records: free the stages
+    named_barrier(1, kNC * 32);
+    __syncwarp();
+    if (lane == 0)
+      for (int i = 0; i < p.pro_stages; ++i) mbar_arrive(&empty[i]);
+    if (pro_landed) {
+      slot = p.pro_stages % S;
+      parity = (uint32_t)((p.pro_stages / S) & 1);
+      consumed = p.pro_stages;
+    }
+    if (threadIdx.x == 0) dec_trace(p, 1);
+    if (s_abort) ok = false;
+
+    It it;
+    it_start(it, p, b);
+    // trace of consumer warp 0: stage waits per phase, item counts, first / last phase-B stage
+    const bool tw = p.trace && warp == 0;
+    unsigned long long wA = 0, wB = 0, fB = 0, lB = 0, lA = 0, fA = 0;
+    const int nA = it.ph == 0 ? it.n : 0;
+    if (ok)
+      ok = consume_phase<MT, GS>(p, p.A, 0, it, b, slice, lane, tiles, auxs, full, empty, slot,
+                                 parity, consumed, rec0, false, tag, abort, tw ? &wA : nullptr,
+                                 &fA, &lA);
+    if (threadIdx.x == 0) {
+      dec_trace(p, 2);
+      if (p.trace) {
+        p.trace[(size_t)blockIdx.x * kTraceEvents + 10] = wA;
+        p.trace[(size_t)blockIdx.x * kTraceEvents + 12] = (unsigned long long)nA;
+      }
+    }
+    if (p.ffn) {
+      // the records of this CTA's phase-B items: warp w builds items w, w + 8, ...
+      if (ok && b < p.B.ctas) {
+        It bi;
+        bi.ph = 1;
+        it_seek(bi, p, b);
+        for (int i = 0; bi.ph == 1 && ok; ++i) {
+          if (i % kNC == warp)
+            ok = build_h_record<MT, GS>(p, bi.grp, p.h_out && bi.cu == 0 && bi.s0 == 0,
+                                        recb + (size_t)i * p.frag_bytes, tag, lane, abort);
+          it_next(bi, p, b);
+        }
+      }
+      if (!ok) *abort = 1;
+      named_barrier(1, kNC * 32);
+      if (*abort) ok = false;
+      if (threadIdx.x == 0) dec_trace(p, 3);
+      const int nB = it.ph == 1 ? it.n : 0;
+      if (ok)
+        ok = consume_phase<MT, GS>(p, p.B, 1, it, b, slice, lane, tiles, auxs, full, empty, slot,
+                                   parity, consumed, recb, true, tag, abort, tw ? &wB : nullptr,
+                                   &fB, &lB);
+      if (threadIdx.x == 0) dec_trace(p, 4);
+      if (threadIdx.x == 0 && p.trace) {
+        unsigned long long* tr = p.trace + (size_t)blockIdx.x * kTraceEvents;
+        tr[9] = fB;
+        tr[11] = wB;
+        tr[13] = (unsigned long long)nB;
+        tr[14] = lB;
       }
     }
     if (!ok) *abort = 1;
-    __syncthreads();
-    if (*abort) ok = false;
-    if (threadIdx.x == 0) dec_trace(p, 3);
-    const int nB = it.ph == 1 ? it.n : 0;
-    if (ok)
-      ok = consume_phase<MT, GS>(p, p.B, 1, it, b, slice, half, lane, ring, ahead, slot, parity,
-                                 consumed, recb, true, tag, abort, px, tw ? &wB : nullptr, &fB,
-                                 &lB);
-    if (threadIdx.x == 0) dec_trace(p, 4);
-    if (threadIdx.x == 0 && p.trace) {
-      unsigned long long* tr = p.trace + (size_t)blockIdx.x * kTraceEvents;
-      tr[9] = fB;
-      tr[11] = wB;
-      tr[13] = (unsigned long long)nB;
-      tr[14] = lB;
+    // the y reduction tasks of this CTA (8 columns each)
+    const DecPhase& L = p.ffn ? p.B : p.A;
+    for (int k = warp; ok; k += kNC) {
+      const int t = (int)b + (int)gridDim.x * k;
+      if (t >= p.red_tasks) break;
+      ok = reduce_task<MT>(p, L, t, tag, lane, abort,
+                           (p.x_host && p.residual) ? s_res + k * 8 * MT : nullptr);
     }
+    if (threadIdx.x == 0) dec_trace(p, 5);
   }
-  if (!ok) *abort = 1;
-  // the y reduction tasks of this CTA (8 columns each)
-  const DecPhase& L = p.ffn ? p.B : p.A;
-  for (int t = (int)b + (int)gridDim.x * warp; ok && t < p.red_tasks; t += (int)gridDim.x * kNC)
-    ok = reduce_task<MT>(p, L, t, tag, lane, abort);
-  if (threadIdx.x == 0) dec_trace(p, 5);
   __syncthreads();
-  // after an abort: wait for the stages armed but not consumed, so no copy is in flight when the
-  // CTA exits
-  const long long armed = (long long)s_armed;
-  for (long long G = consumed; G < armed; ++G) {
-    dec_wait_full(&full[slot], parity, &s_never, p.err, p.timeout_ns, lane);
-    if (++slot == S) {
-      slot = 0;
-      parity ^= 1u;
+  if (warp < kNC) {
+    // after an abort: wait for the stages armed but not consumed, so no copy is in flight when
+    // the CTA exits
+    const long long armed = s_armed;
+    for (long long G = consumed; G < armed; ++G) {
+      dec_wait_full(&full[slot], parity, &s_never, p.err, p.timeout_ns, lane);
+      if (++slot == S) {
+        slot = 0;
+        parity ^= 1u;
+      }
     }
   }
   if (threadIdx.x == 0) {
@@ -792,7 +755,7 @@ cudaError_t dec_launch_mt(const TmapPack& maps, const DecodeParams& p, int grid,
                           cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(dec_threads(GS));
+  cfg.blockDim = dim3(kDecThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -808,7 +771,7 @@ cudaError_t dec_prepare_mt(size_t smem, int* blocks) {
   auto kern = int4_decode_kernel<MT, GS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kern, dec_threads(GS), smem);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, kern, kDecThreads, smem);
 }
 
 template <int MT>
@@ -837,9 +800,9 @@ cudaError_t dec_launch_gs(int gs, const TmapPack& maps, const DecodeParams& p, i
 }  // namespace
 
 size_t decode_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes,
-                         int recb_bytes, int comb_bytes) {
+                         int recb_bytes) {
   return 1024 + (size_t)stages * ((size_t)tile_stage_bytes + aux_stage_bytes + 16) +
-         (size_t)rec0_bytes + (size_t)recb_bytes + (size_t)comb_bytes;
+         (size_t)rec0_bytes + (size_t)recb_bytes;
 }
 
 // The attribute and occupancy query are redone only when an instantiation is launched with

@@ -22,14 +22,12 @@
 
 namespace tk {
 
-// Warps (all consumers, no producer warp): two per 128-column slice (each takes half of every
-// group's rows) from group size 32 on, one per slice at group size 16.
-__host__ __device__ constexpr int dec_split(int gs) { return gs >= 32 ? 2 : 1; }
-__host__ __device__ constexpr int dec_consumers(int gs) { return kSlices * dec_split(gs); }
-__host__ __device__ constexpr int dec_threads(int gs) { return dec_consumers(gs) * 32; }
+constexpr int kDecConsumers = 8;                      // consumer warps (one per 128-col slice)
+constexpr int kDecThreads = (kDecConsumers + 1) * 32;  // + the producer warp
 constexpr int kDecEpochSlots = 1024;  // launch counters: CTA b reads slot b, writes b + k*grid
 constexpr int kDecMaxItemsB = 64;     // phase-B items of one CTA whose records live in smem
 constexpr int kDecReduceBatch = 8;    // partials in flight per lane of a reduction task
+constexpr int kDecMaxTasksPerCta = 16;  // reduction tasks per CTA whose residual smem holds
 
 // error bits of the device error word (shared with the engine's)
 constexpr unsigned kErrDecPoll = 16u;  // a tagged partial never arrived
@@ -60,6 +58,7 @@ struct DecodeParams {
   int ldo;
   const float* residual;  // optional, added to y
   int ldr;
+  int x_host;  // x (and the residual, which is x) is pinned host memory: read with plain loads
   float* h_out;  // optional f32 h [m][ldh]
   int ldh;
   // shared memory: S stages of (tile | aux), then the records
@@ -74,13 +73,9 @@ struct DecodeParams {
   unsigned long long* trace;  // optional [grid][kTraceEvents] global-timer stamps
 };
 
-// Dynamic shared memory of a launch with these sizes (1024-byte alignment slack included), and
-// the bytes the consumer-warp pairs exchange their partial sums through at segment ends.
+// Dynamic shared memory of a launch with these sizes (1024-byte alignment slack included).
 size_t decode_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes,
-                         int recb_bytes, int comb_bytes);
-__host__ __device__ constexpr int dec_comb_bytes(int mt, int gs) {
-  return dec_split(gs) == 2 ? kSlices * 32 * 4 * mt * 4 : 0;
-}
+                         int recb_bytes);
 cudaError_t decode_occupancy(int mt, int gs, size_t smem, int* blocks);
 cudaError_t decode_launch(int mt, int gs, const TmapPack& maps, const DecodeParams& p, int grid,
                           size_t smem, cudaStream_t stream);

@@ -105,6 +105,7 @@ struct tk_device {
   int down_prefetch = 1;  // TK_DOWN_PREFETCH=0 turns off the L2 prefetch of the down projection
   int decode_enabled = 1;  // TK_DECODE=0 routes batch 1-2 through the streaming engine instead
   ScratchBuf dec;          // decode kernel: launch epochs + tagged partial sums of both phases
+  ScratchBuf io;           // TK_FFN_HOST_IO staging of x and out for paths that need it
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   unsigned long long launches = 0;      // kernels enqueued through this device
   // timed-out peer-memory exchanges seen by tk_device_check_error: a tk_tp group created before
@@ -540,8 +541,7 @@ bool dec_plan(const DecPhase& A, const DecPhase* B, int m, int mt, int gs, bool 
   pl.pro_stages = (int)((pro + pl.tile_stage_bytes - 1) / pl.tile_stage_bytes);
   const int rec0 = A.groups * pl.frag_bytes, recb = pl.recb_items * pl.frag_bytes;
   for (int s = kMaxStages; s >= 2; --s) {
-    const size_t need = decode_smem_bytes(s, pl.tile_stage_bytes, pl.aux_stage_bytes, rec0, recb,
-                                          dec_comb_bytes(mt, gs));
+    const size_t need = decode_smem_bytes(s, pl.tile_stage_bytes, pl.aux_stage_bytes, rec0, recb);
     if (need <= (size_t)smem_limit) {
       pl.stages = s;
       pl.smem = need;
@@ -575,7 +575,7 @@ bool decode_shape(int m, int k, int n, int inter, int gs, int grid, bool ffn) {
 int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
                const tk_int4_matrix* a0, const tk_int4_matrix* a1, const tk_int4_matrix* down,
                float* out, float* h_out, int m, int k, int n, int inter, int gs, bool residual,
-               cudaStream_t st) {
+               cudaStream_t st, bool x_host = false) {
   const bool ffn = down != nullptr;
   const int mt = m;  // instantiations for 1 and 2 rows
   const int grid = engine_grid(d);
@@ -595,8 +595,7 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   if (d->stages_override > 0 && d->stages_override < pl.stages && d->stages_override > pl.pro_stages) {
     pl.stages = d->stages_override;
     pl.smem = decode_smem_bytes(pl.stages, pl.tile_stage_bytes, pl.aux_stage_bytes,
-                                p.A.groups * pl.frag_bytes, pl.recb_items * pl.frag_bytes,
-                                dec_comb_bytes(mt, gs));
+                                p.A.groups * pl.frag_bytes, pl.recb_items * pl.frag_bytes);
   }
   // scratch: epochs, then the tagged partials of A and of B
   const size_t epoch_bytes = kDecEpochSlots * sizeof(unsigned);
@@ -632,6 +631,7 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   p.ldo = n_out;
   p.residual = residual ? x : nullptr;
   p.ldr = k;
+  p.x_host = x_host ? 1 : 0;
   p.h_out = ffn ? h_out : nullptr;
   p.ldh = inter;
   p.stages = pl.stages;
@@ -641,6 +641,8 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   p.frag_bytes = pl.frag_bytes;
   p.recb_items = pl.recb_items;
   p.red_tasks = n_out / 8;
+  if (x_host && residual && p.red_tasks > kDecMaxTasksPerCta * grid)
+    return fail(TK_ERR_UNSUPPORTED, "host x: residual tasks exceed the kernel's stash");
   p.err = d->err;
   p.timeout_ns = d->timeout_ns;
   p.trace = d->trace;
@@ -969,7 +971,7 @@ void tk_device_destroy(tk_device* d) {
   cudaSetDevice(d->ordinal);
   if (d->stream) cudaStreamSynchronize(d->stream);
   for (auto* b : {&d->frag[0], &d->partials[0], &d->partials[1], &d->counters[0],
-                  &d->counters[1], &d->g_x16, &d->g_h16, &d->g_part, &d->dec})
+                  &d->counters[1], &d->g_x16, &d->g_h16, &d->g_part, &d->dec, &d->io})
     if (b->ptr) cudaFree(b->ptr);
   if (d->sync) cudaFree(d->sync);
   if (d->err) cudaFree(d->err);
@@ -1331,11 +1333,35 @@ int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const t
   if (st != TK_OK) return st;
   st = check_qshape(m, inter, hidden, gs);
   if (st != TK_OK) return st;
-  if (flags & ~TK_FFN_RESIDUAL) return fail(TK_ERR_ARG, "unknown flags 0x%x", flags);
+  if (flags & ~(TK_FFN_RESIDUAL | TK_FFN_HOST_IO))
+    return fail(TK_ERR_ARG, "unknown flags 0x%x", flags);
   st = set_device(d);
   if (st != TK_OK) return st;
   cudaStream_t cs = pick_stream(d, stream);
   const bool residual = (flags & TK_FFN_RESIDUAL) != 0;
+  if (flags & TK_FFN_HOST_IO) {
+    // x and out in pinned host memory: the batch 1-2 decode kernel reads and writes them over the
+    // host link itself; every other path stages them through device scratch
+    const bool aligned = aligned16(x) && aligned16(norm_w) && aligned16(out) &&
+                         (!h_out || aligned16(h_out)) && matrix_aligned(gate) &&
+                         matrix_aligned(up) && matrix_aligned(down);
+    if (m <= 2 && d->decode_enabled && aligned && engine_shape(hidden, inter, gs) &&
+        engine_shape(inter, hidden, gs)) {
+      st = decode_run(d, x, norm_w, eps, gate, up, down, out, h_out, (int)m, (int)hidden, 0,
+                      (int)inter, (int)gs, residual, cs, true);
+      if (st != TK_ERR_UNSUPPORTED) return st;
+    }
+    const size_t bytes = (size_t)m * hidden * sizeof(float);
+    if ((st = scratch_ensure(d, d->io, 2 * bytes)) != TK_OK) return st;
+    float* xd = static_cast<float*>(d->io.ptr);
+    float* od = xd + (size_t)m * hidden;
+    TK_CUDA_TRY(cudaMemcpyAsync(xd, x, bytes, cudaMemcpyHostToDevice, cs));
+    st = tk_int4_ffn_async(d, xd, norm_w, gate, up, down, od, h_out, m, hidden, inter, gs, eps,
+                           flags & ~TK_FFN_HOST_IO, stream);
+    if (st != TK_OK) return st;
+    TK_CUDA_TRY(cudaMemcpyAsync(out, od, bytes, cudaMemcpyDeviceToHost, cs));
+    return TK_OK;
+  }
   const bool fast = engine_shape(hidden, inter, gs) && engine_shape(inter, hidden, gs) &&
                     aligned16(x) && aligned16(norm_w) && aligned16(out) &&
                     (!h_out || aligned16(h_out)) && matrix_aligned(gate) && matrix_aligned(up) &&
@@ -1828,6 +1854,8 @@ int tk_int4_ffn_tp_async(tk_tp* tp, const float* x, const float* norm_w, const t
                          uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs, float eps,
                          uint32_t flags, void* stream) {
   if (!tp) return fail(TK_ERR_ARG, "tp is NULL");
+  if (flags & TK_FFN_HOST_IO)
+    return fail(TK_ERR_ARG, "TK_FFN_HOST_IO is not supported by the tensor-parallel FFN");
   // the residual is added once, by rank 0, before the sum
   const uint32_t f = tp->rank == 0 ? flags : (flags & ~TK_FFN_RESIDUAL);
   int st = tk_int4_ffn_async(tp->dev, x, norm_w, gate, up, down, out, nullptr, m, hidden, inter, gs,

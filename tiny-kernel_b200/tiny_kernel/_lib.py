@@ -26,6 +26,7 @@ TK_MEM_SHARED = 1
 TK_MEM_HOST = 2
 
 TK_FFN_RESIDUAL = 1
+TK_FFN_HOST_IO = 2
 TK_TP_UNIQUE_ID_BYTES = 128
 TK_Q4_0_REFERENCE_ORDER = 0
 TK_Q4_0_GGML_ORDER = 1

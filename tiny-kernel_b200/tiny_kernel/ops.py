@@ -44,11 +44,12 @@ def matrix(w_packed, scales, zeros) -> Int4MatrixC:
 
 
 def int4_ffn(device, x, norm_weight, gate, up, down, out, m, hidden, inter, group_size,
-             eps=1e-5, h_out=None, residual=False, stream=None, sync=True):
-    """gate/up/down: (w_packed, scales, zeros) triples or Int4MatrixC."""
+             eps=1e-5, h_out=None, residual=False, stream=None, sync=True, host_io=False):
+    """gate/up/down: (w_packed, scales, zeros) triples or Int4MatrixC.  host_io: x and out are
+    pinned host buffers (TK_FFN_HOST_IO)."""
     L = _lib.lib()
     mats = [g if isinstance(g, Int4MatrixC) else matrix(*g) for g in (gate, up, down)]
-    flags = _lib.TK_FFN_RESIDUAL if residual else 0
+    flags = (_lib.TK_FFN_RESIDUAL if residual else 0) | (_lib.TK_FFN_HOST_IO if host_io else 0)
     args = (_dev(device), _ptr(x), _ptr(norm_weight), C.byref(mats[0]), C.byref(mats[1]),
             C.byref(mats[2]), _ptr(out), _ptr(h_out), int(m), int(hidden), int(inter),
             int(group_size), float(eps), flags)
