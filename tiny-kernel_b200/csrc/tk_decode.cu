@@ -51,19 +51,15 @@ __device__ __forceinline__ int dec_nseg(const DecPhase& P, int cu, int* first) {
   return dec_cta_of_unit(a + per - 1, P.units, P.ctas) - c0 + 1;
 }
 
-// One CTA's walk over its items (one group of one column unit each) of phase A, then B.  The
-// phase's sizes are read from the kernel parameters (constant bank), not kept in registers.
+// One CTA's walk over its items (one group of one column unit each) of phase A, then B.
 struct It {
   int ph;       // 0: phase A, 1: phase B, 2: done
   int i, n;     // item index within the phase, the CTA's items in the phase
   int cu, grp;  // column unit (tile * nmat + matrix) and group
   int s0, s1;   // k-steps [s0, s1) of the group
   int last_s1;
+  int groups, spg, nmat, N;
 };
-
-__device__ __forceinline__ const DecPhase& it_phase(const DecodeParams& p, const It& it) {
-  return it.ph == 0 ? p.A : p.B;
-}
 
 __device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned b) {
   while (it.ph < 2) {
@@ -77,6 +73,10 @@ __device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned 
       const unsigned beg = U * b / W, end = U * (b + 1) / W;
       const unsigned fg0 = beg / (unsigned)P.spg, fgl = (end - 1) / (unsigned)P.spg;
       const unsigned cl = fg0 / (unsigned)P.groups;
+      it.groups = P.groups;
+      it.spg = P.spg;
+      it.nmat = P.nmat;
+      it.N = P.N;
       it.i = 0;
       it.n = (int)(fgl - fg0 + 1);
       it.cu = (int)cl;
@@ -93,36 +93,35 @@ __device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned 
 __device__ __forceinline__ void it_start(It& it, const DecodeParams& p, unsigned b) {
   it.ph = 0;
   it.i = it.n = it.cu = it.grp = it.s0 = it.s1 = it.last_s1 = 0;
+  it.groups = it.spg = it.nmat = 1;
+  it.N = 0;
   it_seek(it, p, b);
 }
 
 __device__ __forceinline__ void it_next(It& it, const DecodeParams& p, unsigned b) {
   if (++it.i < it.n) {
-    const DecPhase& P = it_phase(p, it);
-    if (++it.grp == P.groups) {
+    if (++it.grp == it.groups) {
       it.grp = 0;
       ++it.cu;
     }
     it.s0 = 0;
-    it.s1 = it.i == it.n - 1 ? it.last_s1 : P.spg;
+    it.s1 = it.i == it.n - 1 ? it.last_s1 : it.spg;
     return;
   }
   ++it.ph;
   it_seek(it, p, b);
 }
 
-__device__ __forceinline__ int it_tile(const DecPhase& P, const It& it) {
-  return it.cu >> (P.nmat - 1);
-}
+__device__ __forceinline__ int it_tile(const It& it) { return it.cu >> (it.nmat - 1); }
 
 // 128-column slices of the item's tile that hold columns (8 except in a ragged last tile).
-__device__ __forceinline__ int it_slices(const DecPhase& P, const It& it) {
-  const int rem = (P.N - it_tile(P, it) * kWideCols) / kTileCols;
+__device__ __forceinline__ int it_slices(const It& it) {
+  const int rem = (it.N - it_tile(it) * kWideCols) / kTileCols;
   return rem < kSlices ? rem : kSlices;
 }
 
-__device__ __forceinline__ bool it_seg_end(const DecPhase& P, const It& it) {
-  return it.grp == P.groups - 1 || it.i == it.n - 1;
+__device__ __forceinline__ bool it_seg_end(const It& it) {
+  return it.grp == it.groups - 1 || it.i == it.n - 1;
 }
 
 __device__ __forceinline__ void dec_trace(const DecodeParams& p, int ev) {
@@ -133,15 +132,15 @@ __device__ __forceinline__ void dec_trace(const DecodeParams& p, int ev) {
 __device__ __forceinline__ void issue_item(const TmapPack& maps, const DecPhase& P, const It& it,
                                            uint8_t* tile, uint8_t* aux, uint64_t* bar,
                                            uint64_t pol) {
-  const int mat = it.cu & (P.nmat - 1);
-  const int wt = it_tile(P, it);
-  const int ns = it_slices(P, it);
+  const int mat = it.cu & (it.nmat - 1);
+  const int wt = it_tile(it);
+  const int ns = it_slices(it);
   const uint32_t bytes = (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes +
                                     ns * (kScaleBytes + kZeroBytes));
   mbar_arrive_expect_tx(bar, bytes);
-  const int row0 = it.grp * P.spg * kStepRows;
+  const int row0 = it.grp * it.spg * kStepRows;
   const int x = wt * (kWideCols / 8);  // u64 element of the tile's first byte
-  if (it.s0 == 0 && it.s1 == P.spg) {
+  if (it.s0 == 0 && it.s1 == it.spg) {
     tma_load_2d(tile, &maps.map[P.map_base + 2 * mat], bar, x, row0, pol);
   } else {
     for (int s = it.s0; s < it.s1; ++s)
@@ -206,7 +205,7 @@ __device__ __forceinline__ bool dec_wait_full(uint64_t* bar, uint32_t par, volat
 // group's (rec_by_item == 0: rec + grp * frag_bytes) or the item's (rec + i * frag_bytes).
 // Returns false on an abort.
 template <int MT, int GS>
-__device__ __noinline__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, It& it,
+__device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, It& it,
                               unsigned b, int slice, int lane, uint8_t* tiles, uint8_t* auxs,
                               uint64_t* full, uint64_t* empty, int& slot, uint32_t& parity,
                               long long& consumed, const uint8_t* rec, bool rec_by_item,
@@ -250,7 +249,7 @@ __device__ __noinline__ bool consume_phase(const DecodeParams& p, const DecPhase
     const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
     const uint8_t* tl = stage_tile(slot);
     const uint8_t* r = item_rec(it);
-    const bool seg_end = it_seg_end(P, it);
+    const bool seg_end = it_seg_end(it);
     It nx = it;
     it_next(nx, p, b);
     const int nslot = slot + 1 == S ? 0 : slot + 1;
@@ -297,7 +296,7 @@ __device__ __noinline__ bool consume_phase(const DecodeParams& p, const DecPhase
     slot = nslot;
     parity = npar;
     if (seg_end) {
-      if (slice < it_slices(P, it)) {
+      if (slice < it_slices(it)) {
         int c0 = 0;
         dec_nseg(P, it.cu, &c0);
         const int seg = (int)b - c0;
@@ -480,6 +479,40 @@ __device__ bool build_h_record(const DecodeParams& p, int grp, bool write_h, uin
   return true;
 }
 
+// x in pinned host memory (TK_FFN_HOST_IO): every CTA reads only its share of x over the host
+// link and publishes it as tagged words (x_dev, device memory); then the CTA's consumer threads
+// gather the whole of x from there (L2), retrying until every word carries this launch's tag, into
+// the prologue area.  One read of x over the link per launch, not one per CTA.
+template <int MT>
+__device__ bool gather_host_x(const DecodeParams& p, uint8_t* tiles, unsigned b, unsigned tag,
+                              int lane, volatile int* abort) {
+  const int n = p.m * p.A.K;  // floats
+  const int i0 = (int)((long long)n * b / gridDim.x), i1 = (int)((long long)n * (b + 1) / gridDim.x);
+  for (int i = i0 + (int)threadIdx.x; i < i1; i += kNC * 32) {
+    const int m = i / p.A.K, c = i - m * p.A.K;
+    p.x_dev[i] = tagged(p.x[(size_t)m * p.ldx + c], tag);
+  }
+  float* xs = reinterpret_cast<float*>(tiles);
+  for (int i = (int)threadIdx.x; i < n; i += kNC * 32) {
+    uint64_t t0 = 0;
+    unsigned long long v;
+    for (;;) {
+      v = ld_cg_u64(p.x_dev + i);
+      if ((unsigned)(v >> 32) == tag) break;
+      const uint64_t now = global_timer_ns();
+      if (t0 == 0) t0 = now;
+      if (*abort) return false;
+      if (now - t0 > p.timeout_ns) {
+        atomicOr(p.err, kErrDecPoll);
+        return false;
+      }
+      __nanosleep(64);
+    }
+    xs[i] = __uint_as_float((unsigned)v);
+  }
+  return true;
+}
+
 template <int MT, int GS>
 __global__ void __launch_bounds__(kDecThreads, 1)
     int4_decode_kernel(const __grid_constant__ TmapPack maps, const __grid_constant__ DecodeParams p) {
@@ -581,21 +614,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // ------------------------------- consumers --------------------------------------------
     const int slice = warp;
     volatile int* abort = &s_abort;
-    if (p.x_host) {
-      // x over the host link: 16-byte plain loads by the consumer threads into the prologue area
-      const int row4 = p.A.K / 4;
-      for (int i = threadIdx.x; i < p.m * row4; i += kNC * 32) {
-        const int m = i / row4, c = i - m * row4;
-        reinterpret_cast<float4*>(tiles)[i] =
-            reinterpret_cast<const float4*>(p.x + (size_t)m * p.ldx)[c];
-      }
-    }
+    if (p.x_host && !gather_host_x<MT>(p, tiles, b, tag, lane, abort) && lane == 0) *abort = 1;
     // prologue: wait for x (and the norm weight), then the records of every group of x; the
     // consumer warps take the same branch (an abort is published before the barrier)
     if (!dec_wait_full(&full[0], 0, abort, p.err, p.timeout_ns, lane) && lane == 0) *abort = 1;
     named_barrier(1, kNC * 32);
     bool ok = *abort == 0;
-    if (p.x_host && p.residual) {
+    if (ok && p.x_host && p.residual) {
       // keep the residual of this CTA's reduction tasks (the prologue area is reused)
       for (int i = threadIdx.x; i < kDecMaxTasksPerCta * 8 * MT; i += kNC * 32) {
         const int k = i / (8 * MT), m = (i / 8) % MT, c = i % 8;

@@ -59,6 +59,7 @@ struct DecodeParams {
   const float* residual;  // optional, added to y
   int ldr;
   int x_host;  // x (and the residual, which is x) is pinned host memory: read with plain loads
+  unsigned long long* x_dev;  // x_host: [m * K] tagged words through which the CTAs share x
   float* h_out;  // optional f32 h [m][ldh]
   int ldh;
   // shared memory: S stages of (tile | aux), then the records

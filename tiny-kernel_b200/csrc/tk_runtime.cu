@@ -601,12 +601,14 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   const size_t epoch_bytes = kDecEpochSlots * sizeof(unsigned);
   const size_t partA = (size_t)p.A.tiles * p.A.nmat * p.A.maxseg * mt * kWideCols * 8;
   const size_t partB = ffn ? (size_t)p.B.tiles * p.B.maxseg * mt * kWideCols * 8 : 0;
-  int stt = scratch_ensure(d, d->dec, epoch_bytes + partA + partB);
+  const size_t xdev = (size_t)m * k * 8;  // tagged x for TK_FFN_HOST_IO
+  int stt = scratch_ensure(d, d->dec, epoch_bytes + partA + partB + xdev);
   if (stt != TK_OK) return stt;
   uint8_t* base = static_cast<uint8_t*>(d->dec.ptr);
   p.epoch = reinterpret_cast<unsigned*>(base);
   p.A.part = reinterpret_cast<unsigned long long*>(base + epoch_bytes);
   p.B.part = ffn ? reinterpret_cast<unsigned long long*>(base + epoch_bytes + partA) : nullptr;
+  p.x_dev = reinterpret_cast<unsigned long long*>(base + epoch_bytes + partA + partB);
   TmapPack maps;
   std::memset(&maps, 0, sizeof(maps));
   p.A.map_base = 0;
