@@ -540,7 +540,19 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       mbar_init(&empty[i], kNC);
     }
     fence_mbar_init();
-    s_armed = 0;
+    // the prologue copies go out first (x rows, then the norm weight, contiguous over the first
+    // pro_stages stages' tiles): everything the consumers do first waits for them
+    const uint32_t xrow = (uint32_t)p.A.K * 4u;
+    const uint32_t total = (p.x_host ? 0u : xrow * (uint32_t)p.m) + (p.norm_w ? xrow : 0u);
+    const uint64_t pol = l2_evict_first();
+    if (total) mbar_arrive_expect_tx(&full[0], total);
+    else mbar_arrive(&full[0]);
+    if (!p.x_host)
+      for (int m = 0; m < p.m; ++m)
+        bulk_load(tiles + (size_t)m * xrow, p.x + (size_t)m * p.ldx, xrow, &full[0], pol);
+    if (p.norm_w) bulk_load(tiles + (size_t)p.m * xrow, p.norm_w, xrow, &full[0], pol);
+    for (int i = 1; i < p.pro_stages; ++i) mbar_arrive(&full[i]);
+    s_armed = p.pro_stages;
     s_abort = 0;
     s_never = 0;
     s_tag = p.epoch[b] + 1u;
@@ -556,20 +568,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // ------------------------------- producer ---------------------------------------------
     if (lane == 0) {
       const uint64_t pol = l2_evict_first();
-      const int P0 = p.pro_stages;
-      // prologue: x rows then the norm weight, contiguous over the first P0 stages' tiles
-      {
-        const uint32_t xrow = (uint32_t)p.A.K * 4u;
-        const uint32_t total = (p.x_host ? 0u : xrow * (uint32_t)p.m) + (p.norm_w ? xrow : 0u);
-        if (total) mbar_arrive_expect_tx(&full[0], total);
-        else mbar_arrive(&full[0]);
-        if (!p.x_host)
-          for (int m = 0; m < p.m; ++m)
-            bulk_load(tiles + (size_t)m * xrow, p.x + (size_t)m * p.ldx, xrow, &full[0], pol);
-        if (p.norm_w) bulk_load(tiles + (size_t)p.m * xrow, p.norm_w, xrow, &full[0], pol);
-        for (int i = 1; i < P0; ++i) mbar_arrive(&full[i]);
-        s_armed = P0;
-      }
+      const int P0 = p.pro_stages;  // stages the prologue copies (issued by thread 0) occupy
       long long G = P0;
       int ws = P0 % S;
       uint32_t wround = (uint32_t)(P0 / S);
@@ -701,48 +700,45 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     it_start(it, p, b);
     // trace of consumer warp 0: stage waits per phase, item counts, first / last phase-B stage
     const bool tw = p.trace && warp == 0;
-    unsigned long long wA = 0, wB = 0, fB = 0, lB = 0, lA = 0, fA = 0;
-    const int nA = it.ph == 0 ? it.n : 0;
-    if (ok)
-      ok = consume_phase<MT, GS>(p, p.A, 0, it, b, slice, lane, tiles, auxs, full, empty, slot,
-                                 parity, consumed, rec0, false, tag, abort, tw ? &wA : nullptr,
-                                 &fA, &lA);
-    if (threadIdx.x == 0) {
-      dec_trace(p, 2);
-      if (p.trace) {
-        p.trace[(size_t)blockIdx.x * kTraceEvents + 10] = wA;
-        p.trace[(size_t)blockIdx.x * kTraceEvents + 12] = (unsigned long long)nA;
-      }
-    }
-    if (p.ffn) {
-      // the records of this CTA's phase-B items: warp w builds items w, w + 8, ...
-      if (ok && b < p.B.ctas) {
-        It bi;
-        bi.ph = 1;
-        it_seek(bi, p, b);
-        for (int i = 0; bi.ph == 1 && ok; ++i) {
-          if (i % kNC == warp)
-            ok = build_h_record<MT, GS>(p, bi.grp, p.h_out && bi.cu == 0 && bi.s0 == 0,
-                                        recb + (size_t)i * p.frag_bytes, tag, lane, abort);
-          it_next(bi, p, b);
+    // one copy of the item loop for both phases (instruction-cache footprint)
+    const int nph = p.ffn ? 2 : 1;
+#pragma unroll 1
+    for (int ph = 0; ph < nph; ++ph) {
+      if (ph == 1) {
+        // the records of this CTA's phase-B items: warp w builds items w, w + 8, ...
+        if (ok && b < p.B.ctas) {
+          It bi;
+          bi.ph = 1;
+          it_seek(bi, p, b);
+          for (int i = 0; bi.ph == 1 && ok; ++i) {
+            if (i % kNC == warp)
+              ok = build_h_record<MT, GS>(p, bi.grp, p.h_out && bi.cu == 0 && bi.s0 == 0,
+                                          recb + (size_t)i * p.frag_bytes, tag, lane, abort);
+            it_next(bi, p, b);
+          }
         }
+        if (!ok) *abort = 1;
+        named_barrier(1, kNC * 32);
+        if (*abort) ok = false;
+        if (threadIdx.x == 0) dec_trace(p, 3);
       }
-      if (!ok) *abort = 1;
-      named_barrier(1, kNC * 32);
-      if (*abort) ok = false;
-      if (threadIdx.x == 0) dec_trace(p, 3);
-      const int nB = it.ph == 1 ? it.n : 0;
+      const int nitems = it.ph == ph ? it.n : 0;
+      unsigned long long wt = 0, ft = 0, lt = 0;
       if (ok)
-        ok = consume_phase<MT, GS>(p, p.B, 1, it, b, slice, lane, tiles, auxs, full, empty, slot,
-                                   parity, consumed, recb, true, tag, abort, tw ? &wB : nullptr,
-                                   &fB, &lB);
-      if (threadIdx.x == 0) dec_trace(p, 4);
-      if (threadIdx.x == 0 && p.trace) {
-        unsigned long long* tr = p.trace + (size_t)blockIdx.x * kTraceEvents;
-        tr[9] = fB;
-        tr[11] = wB;
-        tr[13] = (unsigned long long)nB;
-        tr[14] = lB;
+        ok = consume_phase<MT, GS>(p, ph == 0 ? p.A : p.B, ph, it, b, slice, lane, tiles, auxs,
+                                   full, empty, slot, parity, consumed, ph == 0 ? rec0 : recb,
+                                   ph == 1, tag, abort, tw ? &wt : nullptr, &ft, &lt);
+      if (threadIdx.x == 0) {
+        dec_trace(p, ph == 0 ? 2 : 4);
+        if (p.trace) {
+          unsigned long long* tr = p.trace + (size_t)blockIdx.x * kTraceEvents;
+          tr[10 + ph] = wt;
+          tr[12 + ph] = (unsigned long long)nitems;
+          if (ph == 1) {
+            tr[9] = ft;
+            tr[14] = lt;
+          }
+        }
       }
     }
     if (!ok) *abort = 1;
