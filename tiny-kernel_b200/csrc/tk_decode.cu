@@ -700,10 +700,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     it_start(it, p, b);
     // trace of consumer warp 0: stage waits per phase, item counts, first / last phase-B stage
     const bool tw = p.trace && warp == 0;
-    // one copy of the item loop for both phases (instruction-cache footprint)
+    // phase A, then (FFN) the phase-B records and phase B; the two phases' loops are separate
+    // inlined copies (one shared copy with the phase chosen at run time measured slower)
     const int nph = p.ffn ? 2 : 1;
-#pragma unroll 1
-    for (int ph = 0; ph < nph; ++ph) {
+#pragma unroll
+    for (int ph = 0; ph < 2; ++ph) {
+      if (ph >= nph) break;
       if (ph == 1) {
         // the records of this CTA's phase-B items: warp w builds items w, w + 8, ...
         if (ok && b < p.B.ctas) {
