@@ -51,23 +51,19 @@ __device__ __forceinline__ int dec_nseg(const DecPhase& P, int cu, int* first) {
   return dec_cta_of_unit(a + per - 1, P.units, P.ctas) - c0 + 1;
 }
 
-// One CTA's walk over its items (one group of one column unit each) of phase A, then B.
+// One CTA's walk over its items (one group of one column unit each) through the phases.
 struct It {
-  int ph;       // 0: phase A, 1: phase B, 2: done
+  int ph;       // phase of the item; p.nph: done
   int i, n;     // item index within the phase, the CTA's items in the phase
-  int cu, grp;  // column unit (tile * nmat + matrix) and group
+  int cu, grp;  // column unit (phase tile * nmat + matrix) and group, both within the phase
   int s0, s1;   // k-steps [s0, s1) of the group
   int last_s1;
-  int groups, spg, nmat, N;
+  int groups, spg, nmat, N, wt0, g0;  // the phase's sizes and offsets
 };
 
 __device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned b) {
-  while (it.ph < 2) {
-    if (it.ph == 1 && !p.ffn) {
-      it.ph = 2;
-      return;
-    }
-    const DecPhase& P = it.ph == 0 ? p.A : p.B;
+  while (it.ph < p.nph) {
+    const DecPhase& P = p.ph[it.ph];
     if (b < P.ctas) {
       const unsigned U = P.units, W = P.ctas;
       const unsigned beg = U * b / W, end = U * (b + 1) / W;
@@ -77,6 +73,8 @@ __device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned 
       it.spg = P.spg;
       it.nmat = P.nmat;
       it.N = P.N;
+      it.wt0 = P.wt0;
+      it.g0 = P.g0;
       it.i = 0;
       it.n = (int)(fgl - fg0 + 1);
       it.cu = (int)cl;
@@ -94,7 +92,7 @@ __device__ __forceinline__ void it_start(It& it, const DecodeParams& p, unsigned
   it.ph = 0;
   it.i = it.n = it.cu = it.grp = it.s0 = it.s1 = it.last_s1 = 0;
   it.groups = it.spg = it.nmat = 1;
-  it.N = 0;
+  it.N = it.wt0 = it.g0 = 0;
   it_seek(it, p, b);
 }
 
@@ -112,7 +110,9 @@ __device__ __forceinline__ void it_next(It& it, const DecodeParams& p, unsigned 
   it_seek(it, p, b);
 }
 
-__device__ __forceinline__ int it_tile(const It& it) { return it.cu >> (it.nmat - 1); }
+// Absolute 1024-column tile of the item (of N) and its absolute group (of K).
+__device__ __forceinline__ int it_tile(const It& it) { return it.wt0 + (it.cu >> (it.nmat - 1)); }
+__device__ __forceinline__ int it_group(const It& it) { return it.g0 + it.grp; }
 
 // 128-column slices of the item's tile that hold columns (8 except in a ragged last tile).
 __device__ __forceinline__ int it_slices(const It& it) {
@@ -138,7 +138,7 @@ __device__ __forceinline__ void issue_item(const TmapPack& maps, const DecPhase&
   const uint32_t bytes = (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes +
                                     ns * (kScaleBytes + kZeroBytes));
   mbar_arrive_expect_tx(bar, bytes);
-  const int row0 = it.grp * it.spg * kStepRows;
+  const int row0 = it_group(it) * it.spg * kStepRows;
   const int x = wt * (kWideCols / 8);  // u64 element of the tile's first byte
   if (it.s0 == 0 && it.s1 == it.spg) {
     tma_load_2d(tile, &maps.map[P.map_base + 2 * mat], bar, x, row0, pol);
@@ -148,8 +148,9 @@ __device__ __forceinline__ void issue_item(const TmapPack& maps, const DecPhase&
                   row0 + s * kStepRows, pol);
   }
   const int col0 = wt * kWideCols;
-  bulk_load(aux, P.scales[mat] + (size_t)it.grp * P.N + col0, (uint32_t)(ns * kScaleBytes), bar, pol);
-  bulk_load(aux + kSlices * kScaleBytes, P.zeros[mat] + (size_t)it.grp * (P.N / 2) + col0 / 2,
+  const size_t g = (size_t)it_group(it);
+  bulk_load(aux, P.scales[mat] + g * P.N + col0, (uint32_t)(ns * kScaleBytes), bar, pol);
+  bulk_load(aux + kSlices * kScaleBytes, P.zeros[mat] + g * (P.N / 2) + col0 / 2,
             (uint32_t)(ns * kZeroBytes), bar, pol);
 }
 
@@ -202,7 +203,8 @@ __device__ __forceinline__ bool dec_wait_full(uint64_t* bar, uint32_t par, volat
 
 // Consumer warp `slice`: all of this CTA's items of phase `ph` (it.ph == ph on entry), dp2a
 // arithmetic; each finished segment's partial sums are stored as tagged words.  Records: the
-// group's (rec_by_item == 0: rec + grp * frag_bytes) or the item's (rec + i * frag_bytes).
+// group's (rec_by_item == 0: rec + absolute group * frag_bytes, the x records) or the item's
+// (rec + i * frag_bytes, the phase's h records).
 // Returns false on an abort.
 template <int MT, int GS>
 __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, It& it,
@@ -219,7 +221,9 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
   const int fb = p.frag_bytes;
   auto stage_tile = [&](int sl) { return tiles + (size_t)sl * p.tile_stage_bytes + slice * kTileCols; };
   auto stage_aux = [&](int sl) { return auxs + (size_t)sl * p.aux_stage_bytes; };
-  auto item_rec = [&](const It& x) { return rec + (size_t)(rec_by_item ? x.i : x.grp) * fb; };
+  auto item_rec = [&](const It& x) {
+    return rec + (size_t)(rec_by_item ? x.i : it_group(x)) * fb;
+  };
   if (it.ph != ph) return true;
   uint32_t wA[HB], wB[HB];
   uint4 XA[MT][HB / 4], XB[MT][HB / 4];
@@ -347,19 +351,23 @@ __device__ __forceinline__ bool dec_poll_again(uint64_t& t0, volatile int* abort
   return true;
 }
 
-// One reduction task of the last phase: 8 output columns, 4 lanes per column; lane (c, j) sums
-// the segments j, j + 4, j + 8, ... of column c in order, then the four lanes combine their sums
-// in a fixed tree, so the result's bits do not depend on timing.  Returns false on an abort.
+// One reduction task of the output phases (phases [q0, q1): the B phases, or qmatmul's one
+// phase): 8 output columns, 4 lanes per column; lane (c, j) sums the segments j, j + 4, j + 8,
+// ... of column c phase by phase in order, then the four lanes combine their sums in a fixed
+// tree, so the result's bits do not depend on timing.  Returns false on an abort.
 template <int MT>
-__device__ bool reduce_task(const DecodeParams& p, const DecPhase& L, int task, unsigned tag,
+__device__ bool reduce_task(const DecodeParams& p, int q0, int q1, int task, unsigned tag,
                             int lane, volatile int* abort, const float* res_stash) {
   constexpr int B = kDecReduceBatch;  // segments per lane per batch
   const int col = task * 8 + (lane >> 2), j = lane & 3;
-  const int cu = col / kWideCols, cl = col % kWideCols;
-  const int ns = dec_nseg(L, cu, nullptr);
+  const int cu = col / kWideCols, cl = col % kWideCols;  // output phases cover every tile
 #pragma unroll 1
   for (int m = 0; m < MT; ++m) {
     float acc = 0.f;
+#pragma unroll 1
+    for (int q = q0; q < q1; ++q) {
+    const DecPhase& L = p.ph[q];
+    const int ns = dec_nseg(L, cu, nullptr);
     for (int base = 0; base < ns; base += 4 * B) {
       uint64_t t0 = 0;
       for (;;) {
@@ -380,6 +388,7 @@ __device__ bool reduce_task(const DecodeParams& p, const DecPhase& L, int task, 
         if (!dec_poll_again(t0, abort, p.err, p.timeout_ns, lane)) return false;
       }
     }
+    }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     if (j == 0 && m < p.m) {
@@ -391,21 +400,23 @@ __device__ bool reduce_task(const DecodeParams& p, const DecPhase& L, int task, 
   return true;
 }
 
-// The record of one phase-B item (h group `grp`), built by one warp from the gate/up partials:
+// The record of one item of B phase na + j (absolute h group `grp`), built by one warp from the
+// gate/up partials of A phase j:
 // h = silu(sum of the gate segments) * (sum of the up segments) over the group's GS columns,
 // quantised into the dp2a record at `rec`; write_h: also store h to h_out.  Lanes: li = lane & 15
 // owns columns 4 li .. 4 li + 3 of the group; for GS <= 64 lanes 0-15 sum the gate segments and
 // lanes 16-31 the up segments at the same time, for GS = 128 every lane sums both.  Segments are
 // loaded 8 / MT at a time, all of a batch in flight, and summed in segment order.
 template <int MT, int GS>
-__device__ bool build_h_record(const DecodeParams& p, int grp, bool write_h, uint8_t* rec,
+__device__ bool build_h_record(const DecodeParams& p, int j, int grp, bool write_h, uint8_t* rec,
                                unsigned tag, int lane, volatile int* abort) {
   constexpr int kSB = 8 / MT;              // segments in flight per batch
   constexpr bool kSplit = GS / 4 <= 16;  // a half warp per matrix
   constexpr int kMats = kSplit ? 1 : 2;  // matrices summed per lane
-  const DecPhase& A = p.A;
-  const int c0 = grp * GS;  // first h column of the group
-  const int ta = c0 / kWideCols, cl = c0 % kWideCols;
+  const DecPhase& A = p.ph[j];
+  const int c0 = grp * GS;  // first h column of the group (absolute)
+  // the A phase's tile (phase-local) and column within it
+  const int ta = c0 / kWideCols - A.wt0, cl = c0 % kWideCols;
   const int li = kSplit ? (lane & 15) : lane;
   const bool owner = li < GS / 4;
   float acc[kMats][MT][4];
@@ -486,10 +497,10 @@ __device__ bool build_h_record(const DecodeParams& p, int grp, bool write_h, uin
 template <int MT>
 __device__ bool gather_host_x(const DecodeParams& p, uint8_t* tiles, unsigned b, unsigned tag,
                               int lane, volatile int* abort) {
-  const int n = p.m * p.A.K;  // floats
+  const int n = p.m * p.ph[0].K;  // floats
   const int i0 = (int)((long long)n * b / gridDim.x), i1 = (int)((long long)n * (b + 1) / gridDim.x);
   for (int i = i0 + (int)threadIdx.x; i < i1; i += kNC * 32) {
-    const int m = i / p.A.K, c = i - m * p.A.K;
+    const int m = i / p.ph[0].K, c = i - m * p.ph[0].K;
     p.x_dev[i] = tagged(p.x[(size_t)m * p.ldx + c], tag);
   }
   float* xs = reinterpret_cast<float*>(tiles);
@@ -532,7 +543,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(auxs + (size_t)S * p.aux_stage_bytes);
   uint64_t* empty = full + S;
   uint8_t* rec0 = reinterpret_cast<uint8_t*>(empty + S);  // 16-byte aligned (S barriers each)
-  uint8_t* recb = rec0 + (size_t)p.A.groups * p.frag_bytes;
+  uint8_t* recb = rec0 + (size_t)p.ph[0].groups * p.frag_bytes;
   const unsigned b = blockIdx.x;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -542,7 +553,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     fence_mbar_init();
     // the prologue copies go out first (x rows, then the norm weight, contiguous over the first
     // pro_stages stages' tiles): everything the consumers do first waits for them
-    const uint32_t xrow = (uint32_t)p.A.K * 4u;
+    const uint32_t xrow = (uint32_t)p.ph[0].K * 4u;
     const uint32_t total = (p.x_host ? 0u : xrow * (uint32_t)p.m) + (p.norm_w ? xrow : 0u);
     const uint64_t pol = l2_evict_first();
     if (total) mbar_arrive_expect_tx(&full[0], total);
@@ -575,7 +586,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       It it;
       it_start(it, p, b);
       dec_trace(p, 7);
-      while (it.ph < 2) {
+      while (it.ph < p.nph) {
         if (wround > 0) {
           // bounded wait for the consumers to free the slot
           bool ok = mbar_try_wait(&empty[ws], (wround - 1) & 1);
@@ -595,7 +606,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           if (!ok) break;
         }
         if (s_abort) break;
-        const DecPhase& P = it.ph == 0 ? p.A : p.B;
+        const DecPhase& P = p.ph[it.ph];
         issue_item(maps, P, it, tiles + (size_t)ws * p.tile_stage_bytes,
                    auxs + (size_t)ws * p.aux_stage_bytes, &full[ws], pol);
         s_armed = ++G;
@@ -625,14 +636,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         const int k = i / (8 * MT), m = (i / 8) % MT, c = i % 8;
         const int t = (int)b + (int)gridDim.x * k;
         if (t < p.red_tasks && m < p.m)
-          s_res[i] = reinterpret_cast<const float*>(tiles)[(size_t)m * p.A.K + t * 8 + c];
+          s_res[i] = reinterpret_cast<const float*>(tiles)[(size_t)m * p.ph[0].K + t * 8 + c];
       }
     }
     const bool pro_landed = ok;
     if (ok) {
       const float* xs = reinterpret_cast<const float*>(tiles);
-      const float* ws = xs + (size_t)p.m * p.A.K;
-      const int nchunks = p.A.K / kTileCols;
+      const float* ws = xs + (size_t)p.m * p.ph[0].K;
+      const int nchunks = p.ph[0].K / kTileCols;
       float rms[MT];
 #pragma unroll
       for (int m = 0; m < MT; ++m) rms[m] = 1.f;
@@ -642,7 +653,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           float v = 0.f;
           if (m < p.m)
             for (int ch = warp; ch < nchunks; ch += kNC) {
-              const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.A.K + ch * kTileCols + 4 * lane);
+              const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.ph[0].K + ch * kTileCols + 4 * lane);
               v = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, v))));
             }
           for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -652,7 +663,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (threadIdx.x < MT) {
           float tot = 0.f;
           for (int i = 0; i < kNC; ++i) tot += s_red[threadIdx.x * kNC + i];
-          s_rms[threadIdx.x] = rsqrtf(tot / (float)p.A.K + p.eps);
+          s_rms[threadIdx.x] = rsqrtf(tot / (float)p.ph[0].K + p.eps);
         }
         named_barrier(1, kNC * 32);
 #pragma unroll
@@ -665,7 +676,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         for (int m = 0; m < MT; ++m) {
           float v[4] = {0.f, 0.f, 0.f, 0.f};
           if (m < p.m) {
-            const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.A.K + ch * kTileCols + 4 * lane);
+            const float4 a = *reinterpret_cast<const float4*>(xs + (size_t)m * p.ph[0].K + ch * kTileCols + 4 * lane);
             if (p.norm_w) {
               v[0] = a.x * rms[m] * w4.x;
               v[1] = a.y * rms[m] * w4.y;
@@ -700,56 +711,72 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     it_start(it, p, b);
     // trace of consumer warp 0: stage waits per phase, item counts, first / last phase-B stage
     const bool tw = p.trace && warp == 0;
-    // phase A, then (FFN) the phase-B records and phase B; the two phases' loops are separate
-    // inlined copies (one shared copy with the phase chosen at run time measured slower)
-    const int nph = p.ffn ? 2 : 1;
-#pragma unroll
-    for (int ph = 0; ph < 2; ++ph) {
-      if (ph >= nph) break;
-      if (ph == 1) {
-        // the records of this CTA's phase-B items: warp w builds items w, w + 8, ...
-        if (ok && b < p.B.ctas) {
-          It bi;
-          bi.ph = 1;
-          it_seek(bi, p, b);
-          for (int i = 0; bi.ph == 1 && ok; ++i) {
-            if (i % kNC == warp)
-              ok = build_h_record<MT, GS>(p, bi.grp, p.h_out && bi.cu == 0 && bi.s0 == 0,
-                                          recb + (size_t)i * p.frag_bytes, tag, lane, abort);
-            it_next(bi, p, b);
-          }
-        }
-        if (!ok) *abort = 1;
-        named_barrier(1, kNC * 32);
-        if (*abort) ok = false;
-        if (threadIdx.x == 0) dec_trace(p, 3);
-      }
-      const int nitems = it.ph == ph ? it.n : 0;
-      unsigned long long wt = 0, ft = 0, lt = 0;
+    // the A phases (x records), then per B phase its records and its items: one inlined copy of
+    // the item loop for each kind (a single copy with the kind chosen at run time measured slower)
+    unsigned long long wt = 0, ft = 0, lt = 0;
+    int nitems = 0;
+#pragma unroll 1
+    for (int q = 0; q < p.na; ++q) {
+      nitems += it.ph == q ? it.n : 0;
       if (ok)
-        ok = consume_phase<MT, GS>(p, ph == 0 ? p.A : p.B, ph, it, b, slice, lane, tiles, auxs,
-                                   full, empty, slot, parity, consumed, ph == 0 ? rec0 : recb,
-                                   ph == 1, tag, abort, tw ? &wt : nullptr, &ft, &lt);
-      if (threadIdx.x == 0) {
-        dec_trace(p, ph == 0 ? 2 : 4);
-        if (p.trace) {
-          unsigned long long* tr = p.trace + (size_t)blockIdx.x * kTraceEvents;
-          tr[10 + ph] = wt;
-          tr[12 + ph] = (unsigned long long)nitems;
-          if (ph == 1) {
-            tr[9] = ft;
-            tr[14] = lt;
-          }
+        ok = consume_phase<MT, GS>(p, p.ph[q], q, it, b, slice, lane, tiles, auxs, full, empty,
+                                   slot, parity, consumed, rec0, false, tag, abort,
+                                   tw ? &wt : nullptr, &ft, &lt);
+    }
+    if (threadIdx.x == 0) {
+      dec_trace(p, 2);
+      if (p.trace) {
+        p.trace[(size_t)blockIdx.x * kTraceEvents + 10] = wt;
+        p.trace[(size_t)blockIdx.x * kTraceEvents + 12] = (unsigned long long)nitems;
+      }
+    }
+    wt = 0;
+    nitems = 0;
+    const int nb = p.nph - p.na;
+#pragma unroll 1
+    for (int j = 0; j < nb; ++j) {
+      const int q = p.na + j;
+      uint8_t* recq = recb + (size_t)j * p.recb_items * p.frag_bytes;
+      // the records of this CTA's items of B phase q: warp w builds items w, w + 8, ...
+      if (ok && b < p.ph[q].ctas) {
+        It bi;
+        bi.ph = q;
+        it_seek(bi, p, b);
+        for (int i = 0; bi.ph == q && ok; ++i) {
+          if (i % kNC == warp)
+            ok = build_h_record<MT, GS>(p, j, it_group(bi),
+                                        p.h_out && it_tile(bi) == 0 && bi.s0 == 0,
+                                        recq + (size_t)i * p.frag_bytes, tag, lane, abort);
+          it_next(bi, p, b);
         }
+      }
+      if (!ok) *abort = 1;
+      named_barrier(1, kNC * 32);
+      if (*abort) ok = false;
+      if (threadIdx.x == 0 && j == 0) dec_trace(p, 3);
+      nitems += it.ph == q ? it.n : 0;
+      if (ok)
+        ok = consume_phase<MT, GS>(p, p.ph[q], q, it, b, slice, lane, tiles, auxs, full, empty,
+                                   slot, parity, consumed, recq, true, tag, abort,
+                                   tw ? &wt : nullptr, &ft, &lt);
+    }
+    if (threadIdx.x == 0 && nb > 0) {
+      dec_trace(p, 4);
+      if (p.trace) {
+        unsigned long long* tr = p.trace + (size_t)blockIdx.x * kTraceEvents;
+        tr[9] = ft;
+        tr[11] = wt;
+        tr[13] = (unsigned long long)nitems;
+        tr[14] = lt;
       }
     }
     if (!ok) *abort = 1;
-    // the y reduction tasks of this CTA (8 columns each)
-    const DecPhase& L = p.ffn ? p.B : p.A;
+    // the y reduction tasks of this CTA (8 columns each) over the output phases
+    const int q0 = nb > 0 ? p.na : 0, q1 = p.nph;
     for (int k = warp; ok; k += kNC) {
       const int t = (int)b + (int)gridDim.x * k;
       if (t >= p.red_tasks) break;
-      ok = reduce_task<MT>(p, L, t, tag, lane, abort,
+      ok = reduce_task<MT>(p, q0, q1, t, tag, lane, abort,
                            (p.x_host && p.residual) ? s_res + k * 8 * MT : nullptr);
     }
     if (threadIdx.x == 0) dec_trace(p, 5);

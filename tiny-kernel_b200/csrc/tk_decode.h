@@ -33,10 +33,11 @@ constexpr int kDecMaxTasksPerCta = 16;  // reduction tasks per CTA whose residua
 constexpr unsigned kErrDecPoll = 16u;  // a tagged partial never arrived
 
 struct DecPhase {
-  int K, N;           // contraction size and output columns
+  int K, N;           // contraction size and output columns of the whole matrix
   int nmat;           // 1, or 2 (gate and up at the same columns)
-  int tiles;          // ceil(N / 1024)
-  int groups, spg;    // K / group size, k-steps per group
+  int wt0, tiles;     // the phase's 1024-column tiles [wt0, wt0 + tiles) of N
+  int g0, groups;     // the phase's groups [g0, g0 + groups) of K
+  int spg;            // k-steps (16 k) per group
   unsigned units;     // tiles * nmat * groups * spg
   unsigned ctas;      // min(grid, units): CTAs that hold a range of this phase
   int map_base;       // tensor maps of matrix i: map[map_base + 2i] (group box), +1 (k-step box)
@@ -46,11 +47,19 @@ struct DecPhase {
   int maxseg;
 };
 
+// Phases of a launch: A phases (x records: qmatmul_int4's one phase, or the FFN's gate/up over
+// consecutive column ranges), then B phases (the FFN's down projection over the h groups of the
+// A phase with the same index, records built from that A phase's partial sums).  Splitting the
+// FFN in two lets B0's records be built long after A0 has finished everywhere and B0's work hide
+// the wait for A1's last partial sums.
+constexpr int kDecMaxPhases = 4;
+
 struct DecodeParams {
   int m;     // live rows (<= MT)
-  int ffn;   // 1: A is gate/up and B the down projection; 0: A only (qmatmul_int4)
-  DecPhase A, B;
-  const float* x;  // [m][ldx], K = A.K
+  int nph;   // phases
+  int na;    // A phases (ph[0 .. na)); B phases ph[na .. nph), nph - na == na or 0
+  DecPhase ph[kDecMaxPhases];
+  const float* x;  // [m][ldx], K = ph[0].K
   int ldx;
   const float* norm_w;  // non-null: rmsnorm(x) with eps first (the FFN)
   float eps;
@@ -66,8 +75,8 @@ struct DecodeParams {
   int stages, tile_stage_bytes, aux_stage_bytes;
   int pro_stages;  // the first stages hold the prologue copies: x rows, then the norm weight
   int frag_bytes;  // record bytes per group
-  int recb_items;  // phase-B records per CTA (the largest item count of a CTA's range)
-  int red_tasks;   // 8-column reduction tasks of the last phase
+  int recb_items;  // records per CTA per B phase (the largest item count of a CTA's range)
+  int red_tasks;   // 8-column reduction tasks over the last phases' outputs
   unsigned* epoch;  // [kDecEpochSlots]
   unsigned* err;
   unsigned long long timeout_ns;

@@ -89,6 +89,7 @@ struct tk_device {
   unsigned long long timeout_ns = kDefaultTimeoutNs;
   int stages_override = 0;
   int ffn_split = 1;  // gate/up tile ranges of the FFN (TK_FFN_SPLIT, 1..4)
+  bool ffn_split_set = false;  // TK_FFN_SPLIT given (the decode kernel's default is 2)
   SyncState* sync = nullptr;
   unsigned* err = nullptr;
   // Pinned host copies of the error word, one slot per synchronising call (a ring), so that the
@@ -489,14 +490,18 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
 constexpr int kDecSmemLimit = 227 * 1024;  // B200 opt-in shared memory per block
 constexpr int kDefaultGrid = 148;          // B200 SMs (the path queries assume the full device)
 
-// One phase of the decode kernel over K x N with nmat matrices on `grid` CTAs.
-void dec_fill(DecPhase& P, int K, int N, int gs, int nmat, int grid) {
+// One phase of the decode kernel: tiles [wt0, wt1) of N (all when wt1 < 0) and groups [g0, g1) of
+// K (all when g1 < 0), nmat matrices, on `grid` CTAs.
+void dec_fill(DecPhase& P, int K, int N, int gs, int nmat, int grid, int wt0 = 0, int wt1 = -1,
+              int g0 = 0, int g1 = -1) {
   std::memset(&P, 0, sizeof(P));
   P.K = K;
   P.N = N;
   P.nmat = nmat;
-  P.tiles = (N + kWideCols - 1) / kWideCols;
-  P.groups = K / gs;
+  P.wt0 = wt0;
+  P.tiles = (wt1 < 0 ? (N + kWideCols - 1) / kWideCols : wt1) - wt0;
+  P.g0 = g0;
+  P.groups = (g1 < 0 ? K / gs : g1) - g0;
   P.spg = gs / 16;
   P.units = (unsigned)((long long)P.tiles * nmat * P.groups * P.spg);
   P.ctas = std::min<unsigned>((unsigned)grid, P.units);
@@ -521,6 +526,29 @@ int dec_max_items(const DecPhase& P) {
   return mx;
 }
 
+// The phases of a launch: qmatmul_int4 is one A phase over K x N; the FFN is `split` gate/up phases
+// over consecutive tile ranges of the intermediate, then as many down phases over the matching
+// h groups (records of B phase j from the partial sums of A phase j).
+void dec_phases(DecodeParams& p, bool ffn, int k, int n, int inter, int gs, int grid, int split) {
+  if (!ffn) {
+    dec_fill(p.ph[0], k, n, gs, 1, grid);
+    p.na = p.nph = 1;
+    return;
+  }
+  const int tiles_i = (inter + kWideCols - 1) / kWideCols;
+  const int S = std::max(1, std::min({split, tiles_i, kDecMaxPhases / 2}));
+  const int groups_h = inter / gs;
+  for (int j = 0; j < S; ++j) {
+    const int t0 = tiles_i * j / S, t1 = tiles_i * (j + 1) / S;
+    dec_fill(p.ph[j], k, inter, gs, 2, grid, t0, t1);
+    const int g0 = std::min(groups_h, t0 * kWideCols / gs);
+    const int g1 = j == S - 1 ? groups_h : std::min(groups_h, t1 * kWideCols / gs);
+    dec_fill(p.ph[S + j], inter, k, gs, 1, grid, 0, -1, g0, g1);
+  }
+  p.na = S;
+  p.nph = 2 * S;
+}
+
 struct DecPlan {
   int stages = 0, pro_stages = 0, tile_stage_bytes = 0, aux_stage_bytes = 0;
   int recb_items = 0, frag_bytes = 0;
@@ -529,17 +557,19 @@ struct DecPlan {
 
 // Shared-memory plan of a decode launch; false when the shape does not fit (the caller then takes
 // the streaming engine).
-bool dec_plan(const DecPhase& A, const DecPhase* B, int m, int mt, int gs, bool norm, int smem_limit,
+bool dec_plan(const DecodeParams& p, int m, int mt, int gs, bool norm, int smem_limit,
               DecPlan* out) {
   DecPlan pl;
   pl.tile_stage_bytes = ((gs / 16) * kStepRows * kRowBytes + 127) & ~127;
   pl.aux_stage_bytes = kSlices * (kScaleBytes + kZeroBytes);
   pl.frag_bytes = record_bytes(gs, mt);
-  pl.recb_items = B ? dec_max_items(*B) : 0;
+  for (int q = p.na; q < p.nph; ++q) pl.recb_items = std::max(pl.recb_items, dec_max_items(p.ph[q]));
   if (pl.recb_items > kDecMaxItemsB) return false;
+  const DecPhase& A = p.ph[0];
   const long long pro = (long long)A.K * 4 * (m + (norm ? 1 : 0));
   pl.pro_stages = (int)((pro + pl.tile_stage_bytes - 1) / pl.tile_stage_bytes);
-  const int rec0 = A.groups * pl.frag_bytes, recb = pl.recb_items * pl.frag_bytes;
+  const int rec0 = A.groups * pl.frag_bytes;
+  const int recb = (p.nph - p.na) * pl.recb_items * pl.frag_bytes;
   for (int s = kMaxStages; s >= 2; --s) {
     const size_t need = decode_smem_bytes(s, pl.tile_stage_bytes, pl.aux_stage_bytes, rec0, recb);
     if (need <= (size_t)smem_limit) {
@@ -550,24 +580,23 @@ bool dec_plan(const DecPhase& A, const DecPhase* B, int m, int mt, int gs, bool 
   }
   if (pl.stages < 2 || pl.pro_stages >= pl.stages) return false;
   // 32-bit stream-K arithmetic in the kernel
-  if ((long long)A.units * A.ctas >= (1LL << 31)) return false;
-  if (B && (long long)B->units * B->ctas >= (1LL << 31)) return false;
+  for (int q = 0; q < p.nph; ++q)
+    if ((long long)p.ph[q].units * p.ph[q].ctas >= (1LL << 31)) return false;
   *out = pl;
   return true;
 }
 
+// Gate/up tile ranges of the decode kernel's FFN (TK_FFN_SPLIT; 2 unless set).
+int dec_split(const tk_device* d) { return d->ffn_split_set ? d->ffn_split : 2; }
+
 // Can the decode kernel take this call (default device settings)?
 bool decode_shape(int m, int k, int n, int inter, int gs, int grid, bool ffn) {
   if (m < 1 || m > 2 || !(gs == 16 || gs == 32 || gs == 64 || gs == 128)) return false;
-  DecPhase A, B;
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  dec_phases(p, ffn, k, n, inter, gs, grid, 2);
   DecPlan pl;
-  if (ffn) {
-    dec_fill(A, k, inter, gs, 2, grid);
-    dec_fill(B, inter, k, gs, 1, grid);
-    return dec_plan(A, &B, m, m, gs, true, kDecSmemLimit - kStaticSmemReserve, &pl);
-  }
-  dec_fill(A, k, n, gs, 1, grid);
-  return dec_plan(A, nullptr, m, m, gs, false, kDecSmemLimit - kStaticSmemReserve, &pl);
+  return dec_plan(p, m, m, gs, ffn, kDecSmemLimit - kStaticSmemReserve, &pl);
 }
 
 // One decode launch for m <= 2 rows: qmatmul_int4 (gate == nullptr) or the FFN.  Returns
@@ -582,47 +611,57 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   DecodeParams p;
   std::memset(&p, 0, sizeof(p));
   p.m = m;
-  p.ffn = ffn ? 1 : 0;
-  if (ffn) {
-    dec_fill(p.A, k, inter, gs, 2, grid);
-    dec_fill(p.B, inter, k, gs, 1, grid);
-  } else {
-    dec_fill(p.A, k, n, gs, 1, grid);
-  }
+  dec_phases(p, ffn, k, n, inter, gs, grid, dec_split(d));
   DecPlan pl;
-  if (!dec_plan(p.A, ffn ? &p.B : nullptr, m, mt, gs, ffn, d->smem_optin - kStaticSmemReserve, &pl))
+  if (!dec_plan(p, m, mt, gs, ffn, d->smem_optin - kStaticSmemReserve, &pl))
     return fail(TK_ERR_UNSUPPORTED, "shape does not fit the decode kernel");
   if (d->stages_override > 0 && d->stages_override < pl.stages && d->stages_override > pl.pro_stages) {
     pl.stages = d->stages_override;
     pl.smem = decode_smem_bytes(pl.stages, pl.tile_stage_bytes, pl.aux_stage_bytes,
-                                p.A.groups * pl.frag_bytes, pl.recb_items * pl.frag_bytes);
+                                p.ph[0].groups * pl.frag_bytes,
+                                (p.nph - p.na) * pl.recb_items * pl.frag_bytes);
   }
-  // scratch: epochs, then the tagged partials of A and of B
+  // scratch: epochs, then the tagged partials of every phase, then the tagged host x
   const size_t epoch_bytes = kDecEpochSlots * sizeof(unsigned);
-  const size_t partA = (size_t)p.A.tiles * p.A.nmat * p.A.maxseg * mt * kWideCols * 8;
-  const size_t partB = ffn ? (size_t)p.B.tiles * p.B.maxseg * mt * kWideCols * 8 : 0;
+  size_t part_bytes[kDecMaxPhases], total = epoch_bytes;
+  for (int q = 0; q < p.nph; ++q) {
+    const DecPhase& P = p.ph[q];
+    part_bytes[q] = (size_t)P.tiles * P.nmat * P.maxseg * mt * kWideCols * 8;
+    total += part_bytes[q];
+  }
   const size_t xdev = (size_t)m * k * 8;  // tagged x for TK_FFN_HOST_IO
-  int stt = scratch_ensure(d, d->dec, epoch_bytes + partA + partB + xdev);
+  int stt = scratch_ensure(d, d->dec, total + xdev);
   if (stt != TK_OK) return stt;
   uint8_t* base = static_cast<uint8_t*>(d->dec.ptr);
   p.epoch = reinterpret_cast<unsigned*>(base);
-  p.A.part = reinterpret_cast<unsigned long long*>(base + epoch_bytes);
-  p.B.part = ffn ? reinterpret_cast<unsigned long long*>(base + epoch_bytes + partA) : nullptr;
-  p.x_dev = reinterpret_cast<unsigned long long*>(base + epoch_bytes + partA + partB);
+  size_t off = epoch_bytes;
+  for (int q = 0; q < p.nph; ++q) {
+    p.ph[q].part = reinterpret_cast<unsigned long long*>(base + off);
+    off += part_bytes[q];
+  }
+  p.x_dev = reinterpret_cast<unsigned long long*>(base + off);
   TmapPack maps;
   std::memset(&maps, 0, sizeof(maps));
-  p.A.map_base = 0;
-  p.A.scales[0] = a0->scales;
-  p.A.zeros[0] = a0->zeros;
   if ((stt = matrix_tmaps(d, a0->w_packed, ffn ? inter : n, k, gs, maps, 0)) != TK_OK) return stt;
   if (ffn) {
-    p.A.scales[1] = a1->scales;
-    p.A.zeros[1] = a1->zeros;
     if ((stt = matrix_tmaps(d, a1->w_packed, inter, k, gs, maps, 2)) != TK_OK) return stt;
-    p.B.map_base = 4;
-    p.B.scales[0] = down->scales;
-    p.B.zeros[0] = down->zeros;
     if ((stt = matrix_tmaps(d, down->w_packed, k, inter, gs, maps, 4)) != TK_OK) return stt;
+  }
+  for (int q = 0; q < p.na; ++q) {
+    DecPhase& A = p.ph[q];
+    A.map_base = 0;  // gate (or the qmatmul matrix): maps 0, 1; up: maps 2, 3
+    A.scales[0] = a0->scales;
+    A.zeros[0] = a0->zeros;
+    if (ffn) {
+      A.scales[1] = a1->scales;
+      A.zeros[1] = a1->zeros;
+    }
+  }
+  for (int q = p.na; q < p.nph; ++q) {
+    DecPhase& B = p.ph[q];
+    B.map_base = 4;  // down: maps 4, 5
+    B.scales[0] = down->scales;
+    B.zeros[0] = down->zeros;
   }
   p.x = x;
   p.ldx = k;
@@ -948,7 +987,10 @@ int tk_device_create(int ordinal, tk_device** out) {
   d->sm_count = d->prop.multiProcessorCount;
   d->smem_optin = (int)d->prop.sharedMemPerBlockOptin;
   if (const char* env = std::getenv("TK_ENGINE_STAGES")) d->stages_override = std::atoi(env);
-  if (const char* env = std::getenv("TK_FFN_SPLIT")) d->ffn_split = std::atoi(env);
+  if (const char* env = std::getenv("TK_FFN_SPLIT")) {
+    d->ffn_split = std::atoi(env);
+    d->ffn_split_set = true;
+  }
   if (const char* env = std::getenv("TK_GEMM")) d->gemm_enabled = std::atoi(env);
   if (const char* env = std::getenv("TK_DOWN_PREFETCH")) d->down_prefetch = std::atoi(env);
   if (const char* env = std::getenv("TK_ENGINE_CTAS")) d->engine_ctas = std::atoi(env);
