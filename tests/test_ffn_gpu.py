@@ -94,22 +94,26 @@ def test_ffn_deterministic(torch_cuda, tkdev):
     (16, 512, 1024, 64, True),     # the tcgen05 GEMM: staged
 ])
 def test_ffn_host_io_matches_device_buffers(torch_cuda, tkdev, m, hidden, inter, gs, residual):
-    """TK_FFN_HOST_IO: x and out in pinned host memory give the same bits as device buffers."""
+    """TK_FFN_HOST_IO: x and out in pinned host memory give the same bits as device buffers, on
+    the first call (run directly, then recorded as a graph) and on three repeats with new
+    contents in the same buffers (replays of the recorded graph)."""
     import tiny_kernel as tk
     torch = torch_cuda
     W = data.make_ffn(91, hidden, inter, gs)
-    x = data.make_x(92, f"hio{m}", m, hidden)
-    y_dev, _ = run_ffn(torch, tkdev, x, W, residual=residual, want_h=False)
     xb = tk.Buffer(tkdev, "f32", m * hidden, kind=2)
     ob = tk.Buffer(tkdev, "f32", m * hidden, kind=2)
-    xb.slice()[:] = x.reshape(-1)
-    ob.slice()[:] = np.nan
     gate, up, down = (mat_dev(torch, M) for M in (W.gate, W.up, W.down))
-    ops.int4_ffn(tkdev, xb, dev(torch, W.norm_w), gate, up, down, ob, m, hidden, inter, gs,
-                 eps=EPS, residual=residual, host_io=True)
-    y_host = ob.slice().reshape(m, hidden).copy()
-    assert np.array_equal(y_host.view(np.uint32), y_dev.view(np.uint32))
-    ref = oracle.ffn_f64(x, W.norm_w, W.gate, W.up, W.down, EPS, residual=residual)
-    assert oracle.normwise_err(y_host, ref) <= TOL
+    nw = dev(torch, W.norm_w)
+    for call in range(4):
+        x = data.make_x(92 + call, f"hio{m}", m, hidden)
+        y_dev, _ = run_ffn(torch, tkdev, x, W, residual=residual, want_h=False)
+        xb.slice()[:] = x.reshape(-1)
+        ob.slice()[:] = np.nan
+        ops.int4_ffn(tkdev, xb, nw, gate, up, down, ob, m, hidden, inter, gs, eps=EPS,
+                     residual=residual, host_io=True)
+        y_host = ob.slice().reshape(m, hidden).copy()
+        assert np.array_equal(y_host.view(np.uint32), y_dev.view(np.uint32)), call
+        ref = oracle.ffn_f64(x, W.norm_w, W.gate, W.up, W.down, EPS, residual=residual)
+        assert oracle.normwise_err(y_host, ref) <= TOL
     xb.deinit()
     ob.deinit()

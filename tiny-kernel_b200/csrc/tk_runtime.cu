@@ -79,6 +79,19 @@ constexpr int kStaticSmemReserve = 4096;
 
 }  // namespace
 
+// A synchronous host-buffer FFN call recorded as a CUDA graph (upload, kernels, download, the
+// error word's read-back): a repeated call with the same arguments is one graph launch and one
+// wait.  Keyed by every argument; valid while the device's scratch buffers are not reallocated.
+struct FfnGraph {
+  const void* ptr[13];  // x, norm weight, gate / up / down (w, s, z), out, h_out
+  uint32_t shape[5];    // m, hidden, inter, group size, flags
+  uint32_t eps_bits;
+  unsigned gen;
+  unsigned long long last_use;
+  cudaGraphExec_t exec;
+  unsigned* err_host;  // pinned, written by the graph's last copy
+};
+
 struct tk_device {
   int ordinal = 0;
   cudaStream_t stream = nullptr;
@@ -105,7 +118,9 @@ struct tk_device {
   int down_prefetch = 1;  // TK_DOWN_PREFETCH=0 turns off the L2 prefetch of the down projection
   int decode_enabled = 1;  // TK_DECODE=0 routes batch 1-2 through the streaming engine instead
   ScratchBuf dec;          // decode kernel: launch epochs + tagged partial sums of both phases
-  ScratchBuf io;           // TK_FFN_HOST_IO staging of x and out for paths that need it
+  ScratchBuf io;           // TK_FFN_HOST_IO staging of x and out
+  unsigned scratch_gen = 0;  // bumped whenever a scratch buffer is reallocated
+  std::vector<struct FfnGraph> ffn_graphs;  // synchronous TK_FFN_HOST_IO calls, recorded
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
   unsigned long long launches = 0;      // kernels enqueued through this device
   // timed-out peer-memory exchanges seen by tk_device_check_error: a tk_tp group created before
@@ -158,6 +173,7 @@ int scratch_ensure(tk_device* d, ScratchBuf& b, size_t need) {
   TK_CUDA_TRY(cudaMalloc(&b.ptr, cap));
   TK_CUDA_TRY(cudaMemset(b.ptr, 0, cap));
   b.cap = cap;
+  ++d->scratch_gen;  // graphs recorded over the old buffers are stale
   return TK_OK;
 }
 
@@ -605,7 +621,7 @@ bool decode_shape(int m, int k, int n, int inter, int gs, int grid, bool ffn) {
 int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
                const tk_int4_matrix* a0, const tk_int4_matrix* a1, const tk_int4_matrix* down,
                float* out, float* h_out, int m, int k, int n, int inter, int gs, bool residual,
-               cudaStream_t st, bool x_host = false) {
+               cudaStream_t st) {
   const bool ffn = down != nullptr;
   const int mt = m;  // instantiations for 1 and 2 rows
   const int grid = engine_grid(d);
@@ -630,8 +646,7 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
     part_bytes[q] = (size_t)P.tiles * P.nmat * P.maxseg * mt * kWideCols * 8;
     total += part_bytes[q];
   }
-  const size_t xdev = (size_t)m * k * 8;  // tagged x for TK_FFN_HOST_IO
-  int stt = scratch_ensure(d, d->dec, total + xdev);
+  int stt = scratch_ensure(d, d->dec, total);
   if (stt != TK_OK) return stt;
   uint8_t* base = static_cast<uint8_t*>(d->dec.ptr);
   p.epoch = reinterpret_cast<unsigned*>(base);
@@ -640,7 +655,6 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
     p.ph[q].part = reinterpret_cast<unsigned long long*>(base + off);
     off += part_bytes[q];
   }
-  p.x_dev = reinterpret_cast<unsigned long long*>(base + off);
   TmapPack maps;
   std::memset(&maps, 0, sizeof(maps));
   if ((stt = matrix_tmaps(d, a0->w_packed, ffn ? inter : n, k, gs, maps, 0)) != TK_OK) return stt;
@@ -673,7 +687,6 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   p.ldo = n_out;
   p.residual = residual ? x : nullptr;
   p.ldr = k;
-  p.x_host = x_host ? 1 : 0;
   p.h_out = ffn ? h_out : nullptr;
   p.ldh = inter;
   p.stages = pl.stages;
@@ -683,8 +696,6 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   p.frag_bytes = pl.frag_bytes;
   p.recb_items = pl.recb_items;
   p.red_tasks = n_out / 8;
-  if (x_host && residual && p.red_tasks > kDecMaxTasksPerCta * grid)
-    return fail(TK_ERR_UNSUPPORTED, "host x: residual tasks exceed the kernel's stash");
   p.err = d->err;
   p.timeout_ns = d->timeout_ns;
   p.trace = d->trace;
@@ -1012,6 +1023,10 @@ void tk_device_destroy(tk_device* d) {
   if (!d) return;
   cudaSetDevice(d->ordinal);
   if (d->stream) cudaStreamSynchronize(d->stream);
+  for (auto& g : d->ffn_graphs) {
+    cudaGraphExecDestroy(g.exec);
+    cudaFreeHost(g.err_host);
+  }
   for (auto* b : {&d->frag[0], &d->partials[0], &d->partials[1], &d->counters[0],
                   &d->counters[1], &d->g_x16, &d->g_h16, &d->g_part, &d->dec, &d->io})
     if (b->ptr) cudaFree(b->ptr);
@@ -1382,17 +1397,8 @@ int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const t
   cudaStream_t cs = pick_stream(d, stream);
   const bool residual = (flags & TK_FFN_RESIDUAL) != 0;
   if (flags & TK_FFN_HOST_IO) {
-    // x and out in pinned host memory: the batch 1-2 decode kernel reads and writes them over the
-    // host link itself; every other path stages them through device scratch
-    const bool aligned = aligned16(x) && aligned16(norm_w) && aligned16(out) &&
-                         (!h_out || aligned16(h_out)) && matrix_aligned(gate) &&
-                         matrix_aligned(up) && matrix_aligned(down);
-    if (m <= 2 && d->decode_enabled && aligned && engine_shape(hidden, inter, gs) &&
-        engine_shape(inter, hidden, gs)) {
-      st = decode_run(d, x, norm_w, eps, gate, up, down, out, h_out, (int)m, (int)hidden, 0,
-                      (int)inter, (int)gs, residual, cs, true);
-      if (st != TK_ERR_UNSUPPORTED) return st;
-    }
+    // x and out in pinned host memory: staged through device scratch by the copy engines (a
+    // kernel reading x over the host link itself measured slower: every CTA needs all of x)
     const size_t bytes = (size_t)m * hidden * sizeof(float);
     if ((st = scratch_ensure(d, d->io, 2 * bytes)) != TK_OK) return st;
     float* xd = static_cast<float*>(d->io.ptr);
@@ -1456,10 +1462,77 @@ int tk_int4_ffn(tk_device* d, const float* x, const float* norm_w, const tk_int4
                 const tk_int4_matrix* up, const tk_int4_matrix* down, float* out, float* h_out,
                 uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs, float eps,
                 uint32_t flags) {
+  const bool graphable = (flags & TK_FFN_HOST_IO) && d && gate && up && down && !d->trace;
+  FfnGraph key{};
+  if (graphable) {
+    const void* ptrs[13] = {x, norm_w, gate->w_packed, gate->scales, gate->zeros, up->w_packed,
+                            up->scales, up->zeros, down->w_packed, down->scales, down->zeros, out,
+                            h_out};
+    std::memcpy(key.ptr, ptrs, sizeof(ptrs));
+    const uint32_t shape[5] = {m, hidden, inter, gs, flags};
+    std::memcpy(key.shape, shape, sizeof(shape));
+    std::memcpy(&key.eps_bits, &eps, sizeof(eps));
+    int st = set_device(d);
+    if (st != TK_OK) return st;
+    static unsigned long long use_clock = 0;
+    for (auto& g : d->ffn_graphs)
+      if (g.gen == d->scratch_gen && !std::memcmp(g.ptr, key.ptr, sizeof(key.ptr)) &&
+          !std::memcmp(g.shape, key.shape, sizeof(key.shape)) && g.eps_bits == key.eps_bits) {
+        g.last_use = ++use_clock;
+        TK_CUDA_TRY(cudaGraphLaunch(g.exec, d->stream));
+        TK_CUDA_TRY(cudaStreamSynchronize(d->stream));
+        if (*static_cast<volatile unsigned*>(g.err_host) == 0) return TK_OK;
+        return tk_device_check_error(d);  // reports the timeout and resets the scratch
+      }
+  }
   int st = tk_int4_ffn_async(d, x, norm_w, gate, up, down, out, h_out, m, hidden, inter, gs, eps,
                              flags, nullptr);
   if (st != TK_OK) return st;
-  return sync_and_check(d, d->stream);
+  st = sync_and_check(d, d->stream);
+  if (st != TK_OK || !graphable) return st;
+  // The call ran (and sized every scratch buffer): record it for the next identical call.  A
+  // failed recording only costs the speed-up.
+  unsigned* err_host = nullptr;
+  if (cudaHostAlloc(reinterpret_cast<void**>(&err_host), sizeof(unsigned), cudaHostAllocDefault) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return TK_OK;
+  }
+  *err_host = 0;
+  const unsigned gen = d->scratch_gen;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  bool ok = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+  if (ok) {
+    const int rs = tk_int4_ffn_async(d, x, norm_w, gate, up, down, out, h_out, m, hidden, inter,
+                                     gs, eps, flags, nullptr);
+    const bool copied = rs == TK_OK && cudaMemcpyAsync(err_host, d->err, sizeof(unsigned),
+                                                       cudaMemcpyDeviceToHost, d->stream) ==
+                                           cudaSuccess;
+    ok = cudaStreamEndCapture(d->stream, &graph) == cudaSuccess && copied;
+  }
+  if (ok) ok = cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+  if (graph) cudaGraphDestroy(graph);
+  cudaGetLastError();
+  if (!ok || gen != d->scratch_gen) {
+    if (exec) cudaGraphExecDestroy(exec);
+    cudaFreeHost(err_host);
+    return TK_OK;
+  }
+  key.gen = gen;
+  key.exec = exec;
+  key.err_host = err_host;
+  key.last_use = 0;
+  constexpr size_t kMaxGraphs = 64;  // e.g. every layer of a 32-layer decode stack
+  if (d->ffn_graphs.size() >= kMaxGraphs) {
+    auto lru = std::min_element(d->ffn_graphs.begin(), d->ffn_graphs.end(),
+                                [](const FfnGraph& a, const FfnGraph& b) { return a.last_use < b.last_use; });
+    cudaGraphExecDestroy(lru->exec);
+    cudaFreeHost(lru->err_host);
+    d->ffn_graphs.erase(lru);
+  }
+  d->ffn_graphs.push_back(key);
+  return TK_OK;
 }
 
 }  // extern "C"
