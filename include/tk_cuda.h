@@ -77,11 +77,14 @@ extern "C" {
 
 /* flags for tk_int4_ffn */
 #define TK_FFN_RESIDUAL 1u /* out = x + FFN(x)  (Llama residual, llama.zig:216-231)  */
-/* x and out are pinned host memory (TK_MEM_HOST, cudaMallocHost or cudaHostRegister'd): the call
- * copies x in and out back through device scratch on its stream (h_out, when given, stays device
- * memory).  The synchronous tk_int4_ffn records such a call as a CUDA graph (copy in, kernels,
- * copy out, the error word's read-back) and replays it when it is called again with the same
- * arguments: one launch and one wait per call.  The recorded graphs (up to 64 per device, least
+/* x and out are pinned host memory (TK_MEM_HOST, cudaMallocHost or cudaHostRegister'd; h_out,
+ * when given, stays device memory).  At 1-2 rows the decode kernel reads x and writes out over
+ * the host link itself (x is read once per call: each CTA reads a share and passes it on to the
+ * others through device scratch); other batches copy x in and out through device scratch on the
+ * call's stream.  The synchronous tk_int4_ffn records such a call as a CUDA graph (the kernel
+ * node, which reports a failure straight to a pinned host word, or copy in, kernels, copy out and
+ * the error word's read-back) and replays it when it is called again with the same arguments: one
+ * launch and one wait per call.  The recorded graphs (up to 64 per device, least
  * recently used replaced) are dropped when the device's scratch grows; synchronous calls on one
  * device from several threads at once are not supported (the reference is single-threaded,
  * src/metal/device.zig:7).  The reference's buffers are host-visible shared memory

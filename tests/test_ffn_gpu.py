@@ -88,6 +88,7 @@ def test_ffn_deterministic(torch_cuda, tkdev):
 
 @pytest.mark.parametrize("m,hidden,inter,gs,residual", [
     (1, 4096, 14336, 64, False),   # config 1: the decode kernel reads / writes host memory itself
+    (2, 4096, 14336, 64, True),    # residual from the kernel's own copy of x
     (1, 512, 1024, 64, True),
     (2, 256, 512, 32, True),
     (3, 384, 256, 128, False),     # the engine: staged through device scratch

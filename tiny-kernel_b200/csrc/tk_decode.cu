@@ -357,7 +357,7 @@ __device__ __forceinline__ bool dec_poll_again(uint64_t& t0, volatile int* abort
 // tree, so the result's bits do not depend on timing.  Returns false on an abort.
 template <int MT>
 __device__ bool reduce_task(const DecodeParams& p, int q0, int q1, int task, unsigned tag,
-                            int lane, volatile int* abort) {
+                            int lane, volatile int* abort, const float* res_stash) {
   constexpr int B = kDecReduceBatch;  // segments per lane per batch
   const int col = task * 8 + (lane >> 2), j = lane & 3;
   const int cu = col / kWideCols, cl = col % kWideCols;  // output phases cover every tile
@@ -393,7 +393,7 @@ __device__ bool reduce_task(const DecodeParams& p, int q0, int q1, int task, uns
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     if (j == 0 && m < p.m) {
       if (p.residual)
-        acc = p.residual[(size_t)m * p.ldr + col] + acc;
+        acc = (res_stash ? res_stash[m * 8 + (lane >> 2)] : p.residual[(size_t)m * p.ldr + col]) + acc;
       p.out[(size_t)m * p.ldo + col] = acc;
     }
   }
@@ -490,6 +490,50 @@ __device__ bool build_h_record(const DecodeParams& p, int j, int grp, bool write
   return true;
 }
 
+// x in pinned host memory: every CTA reads only its share of x over the host link and publishes
+// it as tagged words (x_dev, device memory); then the CTA's consumer threads gather the whole of x
+// from there (L2), eight words in flight per thread, retrying until every word carries this
+// launch's tag, into the prologue area.  One read of x over the link per launch, not one per CTA.
+template <int MT>
+__device__ bool gather_host_x(const DecodeParams& p, uint8_t* tiles, unsigned b, unsigned tag,
+                              volatile int* abort) {
+  constexpr int kT = kNC * 32, kB = 8;
+  const int n = p.m * p.ph[0].K;  // floats
+  const int i0 = (int)((long long)n * b / gridDim.x), i1 = (int)((long long)n * (b + 1) / gridDim.x);
+  for (int i = i0 + (int)threadIdx.x; i < i1; i += kT) {
+    const int m = i / p.ph[0].K, c = i - m * p.ph[0].K;
+    p.x_dev[i] = tagged(p.x[(size_t)m * p.ldx + c], tag);
+  }
+  float* xs = reinterpret_cast<float*>(tiles);
+  for (int base = (int)threadIdx.x; base < n; base += kT * kB) {
+    uint64_t t0 = 0;
+    for (;;) {
+      unsigned long long v[kB];
+#pragma unroll
+      for (int j = 0; j < kB; ++j)
+        v[j] = base + j * kT < n ? ld_cg_u64(p.x_dev + base + j * kT) : ((unsigned long long)tag << 32);
+      bool ok = true;
+#pragma unroll
+      for (int j = 0; j < kB; ++j) ok = ok && (unsigned)(v[j] >> 32) == tag;
+      if (ok) {
+#pragma unroll
+        for (int j = 0; j < kB; ++j)
+          if (base + j * kT < n) xs[base + j * kT] = __uint_as_float((unsigned)v[j]);
+        break;
+      }
+      const uint64_t now = global_timer_ns();
+      if (t0 == 0) t0 = now;
+      if (*abort) return false;
+      if (now - t0 > p.timeout_ns) {
+        atomicOr(p.err, kErrDecPoll);
+        return false;
+      }
+      __nanosleep(32);
+    }
+  }
+  return true;
+}
+
 template <int MT, int GS>
 __global__ void __launch_bounds__(kDecThreads, 1)
     int4_decode_kernel(const __grid_constant__ TmapPack maps, const __grid_constant__ DecodeParams p) {
@@ -500,6 +544,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   __shared__ volatile int s_abort;
   __shared__ volatile int s_never;
   __shared__ unsigned s_tag;
+  __shared__ float s_res[kDecMaxTasksPerCta * 8 * MT];  // residual of this CTA's tasks (host x)
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.stages;
@@ -519,10 +564,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // the prologue copies go out first (x rows, then the norm weight, contiguous over the first
     // pro_stages stages' tiles): everything the consumers do first waits for them
     const uint32_t xrow = (uint32_t)p.ph[0].K * 4u;
-    const uint32_t total = xrow * (uint32_t)p.m + (p.norm_w ? xrow : 0u);
+    const uint32_t total = (p.x_host ? 0u : xrow * (uint32_t)p.m) + (p.norm_w ? xrow : 0u);
     const uint64_t pol = l2_evict_first();
-    mbar_arrive_expect_tx(&full[0], total);
-    for (int m = 0; m < p.m; ++m)
+    if (total) mbar_arrive_expect_tx(&full[0], total);
+    else mbar_arrive(&full[0]);
+    for (int m = 0; m < (p.x_host ? 0 : p.m); ++m)
         bulk_load(tiles + (size_t)m * xrow, p.x + (size_t)m * p.ldx, xrow, &full[0], pol);
     if (p.norm_w) bulk_load(tiles + (size_t)p.m * xrow, p.norm_w, xrow, &full[0], pol);
     for (int i = 1; i < p.pro_stages; ++i) mbar_arrive(&full[i]);
@@ -587,12 +633,22 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // ------------------------------- consumers --------------------------------------------
     const int slice = warp;
     volatile int* abort = &s_abort;
+    if (p.x_host && !gather_host_x<MT>(p, tiles, b, tag, abort)) *abort = 1;
     // prologue: wait for x (and the norm weight), then the records of every group of x; the
     // consumer warps take the same branch (an abort is published before the barrier)
     if (!dec_wait_full(&full[0], 0, abort, p.err, p.timeout_ns, lane) && lane == 0) *abort = 1;
     named_barrier(1, kNC * 32);
     bool ok = *abort == 0;
     const bool pro_landed = ok;
+    if (ok && p.x_host && p.residual) {
+      // keep the residual of this CTA's reduction tasks (the prologue area is reused)
+      for (int i = threadIdx.x; i < kDecMaxTasksPerCta * 8 * MT; i += kNC * 32) {
+        const int k = i / (8 * MT), m = (i / 8) % MT, c = i % 8;
+        const int t = (int)b + (int)gridDim.x * k;
+        if (t < p.red_tasks && m < p.m)
+          s_res[i] = reinterpret_cast<const float*>(tiles)[(size_t)m * p.ph[0].K + t * 8 + c];
+      }
+    }
     if (ok) {
       const float* xs = reinterpret_cast<const float*>(tiles);
       const float* ws = xs + (size_t)p.m * p.ph[0].K;
@@ -729,7 +785,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     for (int k = warp; ok; k += kNC) {
       const int t = (int)b + (int)gridDim.x * k;
       if (t >= p.red_tasks) break;
-      ok = reduce_task<MT>(p, q0, q1, t, tag, lane, abort);
+      ok = reduce_task<MT>(p, q0, q1, t, tag, lane, abort,
+                           (p.x_host && p.residual) ? s_res + k * 8 * MT : nullptr);
     }
     if (threadIdx.x == 0) dec_trace(p, 5);
   }
@@ -748,6 +805,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
   if (threadIdx.x == 0) {
     for (unsigned j = b; j < (unsigned)kDecEpochSlots; j += gridDim.x) p.epoch[j] = tag;
+    // a CTA that gave up tells the host directly (its bits are in p.err as well)
+    if (p.err_host && s_abort) *reinterpret_cast<volatile unsigned*>(p.err_host) = 1u;
     dec_trace(p, 6);
   }
 }

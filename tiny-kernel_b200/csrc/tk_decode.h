@@ -27,6 +27,7 @@ constexpr int kDecThreads = (kDecConsumers + 1) * 32;  // + the producer warp
 constexpr int kDecEpochSlots = 1024;  // launch counters: CTA b reads slot b, writes b + k*grid
 constexpr int kDecMaxItemsB = 64;     // phase-B items of one CTA whose records live in smem
 constexpr int kDecReduceBatch = 8;    // partials in flight per lane of a reduction task
+constexpr int kDecMaxTasksPerCta = 16;  // reduction tasks per CTA whose residual smem holds
 
 // error bits of the device error word (shared with the engine's)
 constexpr unsigned kErrDecPoll = 16u;  // a tagged partial never arrived
@@ -66,6 +67,9 @@ struct DecodeParams {
   int ldo;
   const float* residual;  // optional, added to y
   int ldr;
+  int x_host;                 // x (and the residual, which is x) and out are pinned host memory
+  unsigned long long* x_dev;  // x_host: [m * K] tagged words through which the CTAs share x
+  unsigned* err_host;         // optional pinned host word set nonzero by a CTA that failed
   float* h_out;  // optional f32 h [m][ldh]
   int ldh;
   // shared memory: S stages of (tile | aux), then the records

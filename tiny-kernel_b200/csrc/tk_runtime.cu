@@ -119,6 +119,12 @@ struct tk_device {
   int decode_enabled = 1;  // TK_DECODE=0 routes batch 1-2 through the streaming engine instead
   ScratchBuf dec;          // decode kernel: launch epochs + tagged partial sums of both phases
   ScratchBuf io;           // TK_FFN_HOST_IO staging of x and out
+  size_t dec_xdev_bytes = 0;  // the decode scratch's tagged host-x area
+  // While a synchronous host-buffer call is being recorded into a graph: the pinned word its
+  // decode kernel reports a failure to, and whether a kernel took it (if none did, the graph
+  // ends with a copy of the device error word instead).
+  unsigned* capture_err_host = nullptr;
+  bool capture_err_used = false;
   unsigned scratch_gen = 0;  // bumped whenever a scratch buffer is reallocated
   std::vector<struct FfnGraph> ffn_graphs;  // synchronous TK_FFN_HOST_IO calls, recorded
   unsigned long long* trace = nullptr;  // [sm_count][kTraceEvents] when tracing is enabled
@@ -621,7 +627,7 @@ bool decode_shape(int m, int k, int n, int inter, int gs, int grid, bool ffn) {
 int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
                const tk_int4_matrix* a0, const tk_int4_matrix* a1, const tk_int4_matrix* down,
                float* out, float* h_out, int m, int k, int n, int inter, int gs, bool residual,
-               cudaStream_t st) {
+               cudaStream_t st, bool host_io = false) {
   const bool ffn = down != nullptr;
   const int mt = m;  // instantiations for 1 and 2 rows
   const int grid = engine_grid(d);
@@ -646,7 +652,10 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
     part_bytes[q] = (size_t)P.tiles * P.nmat * P.maxseg * mt * kWideCols * 8;
     total += part_bytes[q];
   }
-  int stt = scratch_ensure(d, d->dec, total);
+  // host x: the tagged words through which the CTAs share it (the area is kept once sized, so
+  // that a device-buffer call after a host-buffer one does not reallocate the scratch)
+  const size_t xdev = std::max<size_t>(host_io ? (size_t)m * k * 8 : 0, d->dec_xdev_bytes);
+  int stt = scratch_ensure(d, d->dec, total + xdev);
   if (stt != TK_OK) return stt;
   uint8_t* base = static_cast<uint8_t*>(d->dec.ptr);
   p.epoch = reinterpret_cast<unsigned*>(base);
@@ -655,6 +664,9 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
     p.ph[q].part = reinterpret_cast<unsigned long long*>(base + off);
     off += part_bytes[q];
   }
+  d->dec_xdev_bytes = xdev;
+  p.x_host = host_io ? 1 : 0;
+  p.x_dev = host_io ? reinterpret_cast<unsigned long long*>(base + off) : nullptr;
   TmapPack maps;
   std::memset(&maps, 0, sizeof(maps));
   if ((stt = matrix_tmaps(d, a0->w_packed, ffn ? inter : n, k, gs, maps, 0)) != TK_OK) return stt;
@@ -696,6 +708,10 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   p.frag_bytes = pl.frag_bytes;
   p.recb_items = pl.recb_items;
   p.red_tasks = n_out / 8;
+  if (host_io && residual && p.red_tasks > kDecMaxTasksPerCta * grid)
+    return fail(TK_ERR_UNSUPPORTED, "host x with the residual: too many reduction tasks");
+  p.err_host = d->capture_err_host;
+  if (p.err_host) d->capture_err_used = true;
   p.err = d->err;
   p.timeout_ns = d->timeout_ns;
   p.trace = d->trace;
@@ -1397,8 +1413,18 @@ int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const t
   cudaStream_t cs = pick_stream(d, stream);
   const bool residual = (flags & TK_FFN_RESIDUAL) != 0;
   if (flags & TK_FFN_HOST_IO) {
-    // x and out in pinned host memory: staged through device scratch by the copy engines (a
-    // kernel reading x over the host link itself measured slower: every CTA needs all of x)
+    // x and out in pinned host memory.  The batch 1-2 decode kernel reads x over the host link
+    // itself (each CTA a share, passed on to the others through device memory) and writes out
+    // there; the other paths stage both through device scratch with copies.
+    const bool aligned = aligned16(x) && aligned16(norm_w) && aligned16(out) &&
+                         (!h_out || aligned16(h_out)) && matrix_aligned(gate) &&
+                         matrix_aligned(up) && matrix_aligned(down);
+    if (m <= 2 && d->decode_enabled && aligned && engine_shape(hidden, inter, gs) &&
+        engine_shape(inter, hidden, gs)) {
+      st = decode_run(d, x, norm_w, eps, gate, up, down, out, h_out, (int)m, (int)hidden, 0,
+                      (int)inter, (int)gs, residual, cs, true);
+      if (st != TK_ERR_UNSUPPORTED) return st;
+    }
     const size_t bytes = (size_t)m * hidden * sizeof(float);
     if ((st = scratch_ensure(d, d->io, 2 * bytes)) != TK_OK) return st;
     float* xd = static_cast<float*>(d->io.ptr);
@@ -1479,6 +1505,7 @@ int tk_int4_ffn(tk_device* d, const float* x, const float* norm_w, const tk_int4
       if (g.gen == d->scratch_gen && !std::memcmp(g.ptr, key.ptr, sizeof(key.ptr)) &&
           !std::memcmp(g.shape, key.shape, sizeof(key.shape)) && g.eps_bits == key.eps_bits) {
         g.last_use = ++use_clock;
+        *static_cast<volatile unsigned*>(g.err_host) = 0u;
         TK_CUDA_TRY(cudaGraphLaunch(g.exec, d->stream));
         TK_CUDA_TRY(cudaStreamSynchronize(d->stream));
         if (*static_cast<volatile unsigned*>(g.err_host) == 0) return TK_OK;
@@ -1504,11 +1531,17 @@ int tk_int4_ffn(tk_device* d, const float* x, const float* norm_w, const tk_int4
   cudaGraphExec_t exec = nullptr;
   bool ok = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
   if (ok) {
+    // the decode kernel reports a failure to err_host itself; the other paths' graphs end with a
+    // copy of the device error word
+    d->capture_err_host = err_host;
+    d->capture_err_used = false;
     const int rs = tk_int4_ffn_async(d, x, norm_w, gate, up, down, out, h_out, m, hidden, inter,
                                      gs, eps, flags, nullptr);
-    const bool copied = rs == TK_OK && cudaMemcpyAsync(err_host, d->err, sizeof(unsigned),
-                                                       cudaMemcpyDeviceToHost, d->stream) ==
-                                           cudaSuccess;
+    d->capture_err_host = nullptr;
+    const bool copied =
+        rs == TK_OK && (d->capture_err_used ||
+                        cudaMemcpyAsync(err_host, d->err, sizeof(unsigned), cudaMemcpyDeviceToHost,
+                                        d->stream) == cudaSuccess);
     ok = cudaStreamEndCapture(d->stream, &graph) == cudaSuccess && copied;
   }
   if (ok) ok = cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
