@@ -321,8 +321,9 @@ int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *sca
  * A launch of the batch 1-2 decode kernel uses the slots as: start, prologue records done, phase A
  * done, phase-B records done, phase B done, reduction tasks done, end, producer first issue,
  * producer last issue, first phase-B stage in hand (all ns), then consumer warp 0's ns spent
- * waiting for stages in phase A and in phase B, the CTA's phase-A and phase-B item counts, and the
- * ns at which the last phase-B stage was in hand.
+ * waiting for stages in phase A and in phase B, the CTA's phase-A and phase-B item counts, the
+ * ns at which the last phase-B stage was in hand, and (x in host memory) the ns at which the
+ * CTA held the whole of x.
  * A launch of the batch >= 16 GEMM overwrites the buffer with SM-clock cycle counts instead,
  * for CTAs x + X * (y + Y * z) below sm_count: TMA producer waiting for free ring stages,
  * producer total, MMA issuer waiting for dequantised tiles, MMA waiting for TMA stages, MMA

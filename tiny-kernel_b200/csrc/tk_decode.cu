@@ -246,8 +246,8 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
   {
     const uint8_t* r = item_rec(it);
     dp_load_meta<MT, GS>(stage_aux(slot), r, slice, lane, it.s0, it.s1, Mc);
-    dp_load_rows<HB>(stage_tile(slot), 0, it.s0 * kStepRows, it.s1 * kStepRows, lane, wA);
-    dp_load_x<MT, HB>(r, tok_stride, 0, XA);
+    dp_load_rows_all<HB>(stage_tile(slot), 0, lane, wA);
+    dp_load_x_in<MT, HB>(r, tok_stride, 0, it.s0 * kStepRows, it.s1 * kStepRows, XA);
   }
   for (;;) {
     const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
@@ -268,8 +268,8 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
       for (int i = 0; i < 4; ++i) aL[m][i] = aH[m][i] = 0;
 #pragma unroll
     for (int c = 0; c < NCH; c += 2) {
-      dp_load_rows<HB>(tl, (c + 1) * HB, r0, r1, lane, wB);
-      dp_load_x<MT, HB>(r, tok_stride, (c + 1) * HB, XB);
+      dp_load_rows_all<HB>(tl, (c + 1) * HB, lane, wB);
+      dp_load_x_in<MT, HB>(r, tok_stride, (c + 1) * HB, r0, r1, XB);
       bool nready = false;
       if (c + 2 == NCH) {
         // every byte of this stage is loaded (in issue order before the arrival)
@@ -279,8 +279,8 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
       }
       dp_compute<MT, HB>(wA, XA, aL, aH);
       if (c + 2 < NCH) {
-        dp_load_rows<HB>(tl, (c + 2) * HB, r0, r1, lane, wA);
-        dp_load_x<MT, HB>(r, tok_stride, (c + 2) * HB, XA);
+        dp_load_rows_all<HB>(tl, (c + 2) * HB, lane, wA);
+        dp_load_x_in<MT, HB>(r, tok_stride, (c + 2) * HB, r0, r1, XA);
       } else if (prefetch) {
         // the next item's first chunk while this item's last chunk computes
         if (!__all_sync(0xffffffffu, nready) && !wait_stage(nslot, npar)) {
@@ -288,8 +288,8 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
         } else {
           const uint8_t* nr = item_rec(nx);
           dp_load_meta<MT, GS>(stage_aux(nslot), nr, slice, lane, nx.s0, nx.s1, Mn);
-          dp_load_rows<HB>(stage_tile(nslot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
-          dp_load_x<MT, HB>(nr, tok_stride, 0, XA);
+          dp_load_rows_all<HB>(stage_tile(nslot), 0, lane, wA);
+          dp_load_x_in<MT, HB>(nr, tok_stride, 0, nx.s0 * kStepRows, nx.s1 * kStepRows, XA);
           next_loaded = true;
         }
       }
@@ -323,8 +323,8 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
       if (!wait_stage(slot, parity)) return false;
       const uint8_t* nr = item_rec(nx);
       dp_load_meta<MT, GS>(stage_aux(slot), nr, slice, lane, nx.s0, nx.s1, Mn);
-      dp_load_rows<HB>(stage_tile(slot), 0, nx.s0 * kStepRows, nx.s1 * kStepRows, lane, wA);
-      dp_load_x<MT, HB>(nr, tok_stride, 0, XA);
+      dp_load_rows_all<HB>(stage_tile(slot), 0, lane, wA);
+      dp_load_x_in<MT, HB>(nr, tok_stride, 0, nx.s0 * kStepRows, nx.s1 * kStepRows, XA);
     }
     it = nx;
     Mc = Mn;
@@ -633,7 +633,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // ------------------------------- consumers --------------------------------------------
     const int slice = warp;
     volatile int* abort = &s_abort;
-    if (p.x_host && !gather_host_x<MT>(p, tiles, b, tag, abort)) *abort = 1;
+    if (p.x_host) {
+      if (!gather_host_x<MT>(p, tiles, b, tag, abort)) *abort = 1;
+      if (threadIdx.x == 0) dec_trace(p, 15);
+    }
     // prologue: wait for x (and the norm weight), then the records of every group of x; the
     // consumer warps take the same branch (an abort is published before the barrier)
     if (!dec_wait_full(&full[0], 0, abort, p.err, p.timeout_ns, lane) && lane == 0) *abort = 1;
