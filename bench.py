@@ -346,9 +346,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
-    ap.add_argument("--collective", default="nccl", choices=["p2p", "nccl"],
-                    help="tensor-parallel exchange: the library's group (one-shot all-reduce over "
-                         "NVLink peer memory, NCCL beyond its size limit) or torch.distributed NCCL")
+    ap.add_argument("--collective", default="lib", choices=["lib", "p2p", "nccl"],
+                    help="tensor-parallel exchange: the library's group (lib, or its old name "
+                         "p2p: at batch 1-2 fused into the decode kernel over NVLink peer "
+                         "memory, else a one-shot peer-memory all-reduce, NCCL beyond its size "
+                         "limit) or torch.distributed NCCL after the library's shard FFN")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -377,7 +379,7 @@ def main():
     dev = tk.init(local)
     matvec = args.config == 0
     group = None
-    if pg is not None and args.collective == "p2p" and not matvec:
+    if pg is not None and args.collective in ("lib", "p2p") and not matvec:
         from tiny_kernel.tp import Group, unique_id
         box = [unique_id() if rank == 0 else None]
         pg.broadcast_object_list(box, src=0)
@@ -676,8 +678,12 @@ def main():
                 "parallelism": (f"{world} replicas" if matvec else f"tp{world}"),
                 "weight_copies": copies,
                 "collective": (None if pg is None or matvec else
-                               ("peer-memory one-shot all-reduce" if group is not None and group.uses_p2p
-                                else "NCCL all-reduce")),
+                               "torch.distributed NCCL all-reduce" if group is None else
+                               {2: "fused into the decode kernel (peer stores over NVLink, "
+                                   "rank-order sum)",
+                                1: "peer-memory one-shot all-reduce kernel",
+                                0: "NCCL all-reduce (library group)"}[
+                                   group.ffn_exchange(m, hidden, inter, GS)]),
                 "l2_guard": f"{copies} weight copies x {L} block(s) = "
                             f"{copies * L * shard_w_bytes / 1e6:.0f} MB per GPU (> 3x L2)",
                 "launch": "cuda-graph" if graph is not None else "stream",

@@ -210,10 +210,16 @@ int tk_int4_ffn_async(tk_device *dev, const float *x, const float *norm_weight,
  * One process (or thread) per GPU.  Rank r holds the shard: gate/up columns and down K-rows
  * [r*I/tp, (r+1)*I/tp) of the full FFN (inter_shard = I/tp); x, the norm weight and out are full
  * size on every rank.  tk_int4_ffn_tp computes the shard's partial output and sums it across
- * the ranks in place (NCCL all-reduce, f32, on the device's stream or the given one); with
- * TK_FFN_RESIDUAL the residual is added once (by rank 0) before the sum.  NCCL (libnccl.so.2) is
- * loaded at the first tk_tp_* call; TK_ERR_NCCL when it is missing or a NCCL call fails.
- * Every rank must make the same tk_tp_* calls in the same order. */
+ * the ranks in place, on the device's stream or the given one (tk_int4_ffn_tp_exchange says
+ * how).  At 1-2 rows on a group whose ranks mapped one another's memory, the exchange is fused
+ * into the decode kernel: each reduction task stores its columns' partial sums into every
+ * rank's area over NVLink and sums the ranks' values in rank order, in the same launch (every
+ * rank gets the same bits; TK_ERR_ARG unless x, the norm weight, out and the matrices are 16-byte
+ * aligned); TK_TP_FUSED=0 in the environment at tk_tp_create turns this off.  Otherwise the
+ * shard's FFN is followed by tk_tp_allreduce_sum_f32.  With TK_FFN_RESIDUAL the residual is added
+ * once: after the sum (fused) or by rank 0 before it.  NCCL (libnccl.so.2) is loaded at the
+ * first tk_tp_* call; TK_ERR_NCCL when it is missing or a NCCL call fails.  Every rank must make
+ * the same tk_tp_* calls in the same order. */
 #define TK_TP_UNIQUE_ID_BYTES 128
 typedef struct tk_tp tk_tp;
 /* Rank 0 creates the group's id and hands it to the other ranks (any channel). */
@@ -242,6 +248,10 @@ int tk_int4_ffn_tp_async(tk_tp *tp, const float *x, const float *norm_weight,
 int tk_tp_allreduce_sum_f32(tk_tp *tp, float *buf, size_t count, void *stream);
 /* 1 when the group uses the peer-memory all-reduce, 0 when NCCL carries every exchange. */
 int tk_tp_uses_p2p(tk_tp *tp);
+/* The exchange tk_int4_ffn_tp uses for this shape: 2 fused into the decode kernel, 1 the
+ * peer-memory all-reduce kernel, 0 NCCL (or nothing to exchange, one rank). */
+int tk_int4_ffn_tp_exchange(tk_tp *tp, uint32_t m, uint32_t hidden, uint32_t inter_shard,
+                            uint32_t group_size);
 
 /* ---- fp32 matvec ---------------------------------------------------------------------
  * Replaces Matvec.forward(x, W, out, K, N) (src/kernels/fused.zig:62-89, shaders.zig:184-226):

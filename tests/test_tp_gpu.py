@@ -114,30 +114,41 @@ def _rank_native(rank, world, uid, cases, result_path):
     torch.cuda.set_device(rank)
     dev = tk.init(rank)
     group = Group(dev, world, rank, uid)
-    errs = []
+    errs, exch, outs = [], [], []
     try:
         for (m, hidden, inter, gs, residual) in cases:
             W = data.make_ffn(43, hidden, inter, gs)
-            x = data.make_x(44, f"tpn{m}", m, hidden)
             S = shard_ffn(W, rank, world)
 
             def d(a):
                 a = np.ascontiguousarray(a)
                 return torch.from_numpy(a.view(np.int16) if a.dtype == np.uint16 else a).cuda()
 
+            mats = [[d(a) for a in (M.w, M.s, M.z)] for M in (S.gate, S.up, S.down)]
+            nw = d(S.norm_w)
+            exch.append(group.ffn_exchange(m, hidden, S.inter, gs))
+            # three calls with new inputs in the same buffers: the exchange areas' two halves
+            # are used in turn
+            xd = torch.empty((m, hidden), dtype=torch.float32, device="cuda")
             out = torch.empty((m, hidden), dtype=torch.float32, device="cuda")
-            group.int4_ffn(d(x), d(S.norm_w), [d(a) for a in (S.gate.w, S.gate.s, S.gate.z)],
-                           [d(a) for a in (S.up.w, S.up.s, S.up.z)],
-                           [d(a) for a in (S.down.w, S.down.s, S.down.z)], out, m, hidden,
-                           S.inter, gs, eps=EPS, residual=residual)
-            if rank == 0:
-                ref = oracle.ffn_f64(x, W.norm_w, W.gate, W.up, W.down, EPS, residual=residual)
-                errs.append(float(oracle.normwise_err(out.cpu().numpy(), ref)))
+            for call in range(3):
+                x = data.make_x(44 + call, f"tpn{m}", m, hidden)
+                xd.copy_(torch.from_numpy(x))
+                group.int4_ffn(xd, nw, *mats, out, m, hidden, S.inter, gs, eps=EPS,
+                               residual=residual)
+                y = out.cpu().numpy()
+                outs.append(y)
+                if rank == 0:
+                    ref = oracle.ffn_f64(x, W.norm_w, W.gate, W.up, W.down, EPS,
+                                         residual=residual)
+                    errs.append(float(oracle.normwise_err(y, ref)))
     finally:
         group.close()
         dev.deinit()
+    np.save(f"{result_path}.out{rank}.npy", np.concatenate([o.reshape(-1) for o in outs]))
     if rank == 0:
         np.save(result_path, np.array(errs))
+        np.save(f"{result_path}.exch.npy", np.array(exch))
 
 
 @pytest.mark.parametrize("world", [2, 4])
@@ -147,12 +158,22 @@ def test_tp_ffn_native_group_vs_oracle(torch_cuda, tmp_path, world):
     import torch.multiprocessing as mp
 
     from tiny_kernel.tp import unique_id
-    cases = [(1, 4096, 14336, 64, False),   # config 1, TP2
-             (1, 1024, 2048, 64, True),     # residual added once (rank 0)
+    cases = [(1, 4096, 14336, 64, False),   # config 1: the exchange fused into the decode kernel
+             (1, 1024, 2048, 64, True),     # residual added once
+             (2, 1024, 2048, 64, True),     # two rows, fused
+             (4, 1024, 2048, 64, False),    # the engine + the peer-memory all-reduce
              (16, 1024, 2048, 64, False)]   # batch 16: the tcgen05 GEMM on each shard
     out = tmp_path / "errs_native.npy"
     mp.start_processes(_rank_native, args=(world, unique_id(), cases, str(out)), nprocs=world,
                        join=True, start_method="spawn")
     errs = np.load(out)
-    assert len(errs) == len(cases)
+    exch = np.load(f"{out}.exch.npy")
+    print(f"TP{world}: exchanges {exch.tolist()}, errors {errs.tolist()}")
+    assert len(errs) == 3 * len(cases)
     assert np.all(errs <= TOL), errs
+    if exch[3] == 1:  # the group maps its peers: 1-2 rows take the fused exchange
+        assert exch[0] == exch[1] == exch[2] == 2, exch
+    # every rank holds the same sum, bit for bit
+    ref = np.load(f"{out}.out0.npy")
+    for r in range(1, world):
+        assert np.array_equal(np.load(f"{out}.out{r}.npy").view(np.uint32), ref.view(np.uint32)), r

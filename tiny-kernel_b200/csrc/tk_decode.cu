@@ -169,6 +169,17 @@ __device__ __forceinline__ ulonglong2 ld_cg_u64x2(const unsigned long long* p) {
   return v;
 }
 
+// System-scope relaxed accesses of the peer exchange (single-copy atomic 64-bit words).
+__device__ __forceinline__ void st_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ unsigned long long ld_cg_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -214,8 +225,11 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
                               unsigned tag, volatile int* abort, unsigned long long* wait_ns,
                               unsigned long long* first_ns, unsigned long long* last_ns) {
   constexpr int R = GS / 2;                 // packed rows per group
-  constexpr int HB = R <= 32 ? R / 2 : 16;  // rows per chunk
-  constexpr int NCH = R / HB;               // chunks per item (2 or 4)
+  // rows per chunk: 16 at one row (the chunk pair fully unrolled), 8 at two (a rolled loop over
+  // chunk pairs, which keeps the two rows' accumulators and chunks in registers)
+  constexpr int HB = MT == 1 ? (R <= 32 ? R / 2 : 16) : (R <= 16 ? R / 2 : 8);
+  constexpr int NCH = R / HB;  // chunks per item (2 to 8)
+  constexpr int kPairUnroll = MT == 1 ? NCH / 2 : 1;
   constexpr int tok_stride = dp_tok_stride(GS);
   const int S = p.stages;
   const int fb = p.frag_bytes;
@@ -266,7 +280,7 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
     for (int m = 0; m < MT; ++m)
 #pragma unroll
       for (int i = 0; i < 4; ++i) aL[m][i] = aH[m][i] = 0;
-#pragma unroll
+#pragma unroll kPairUnroll
     for (int c = 0; c < NCH; c += 2) {
       dp_load_rows_all<HB>(tl, (c + 1) * HB, lane, wB);
       dp_load_x_in<MT, HB>(r, tok_stride, (c + 1) * HB, r0, r1, XB);
@@ -334,14 +348,15 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
 // Bounded poll step shared by the readers of tagged partials: returns 1 to retry, 0 to give up
 // (timeout -> error bit and abort, or another warp aborted).  t0 = 0 starts the clock.
 __device__ __forceinline__ bool dec_poll_again(uint64_t& t0, volatile int* abort, unsigned* err,
-                                               unsigned long long timeout_ns, int lane) {
+                                               unsigned long long timeout_ns, int lane,
+                                               unsigned bit = kErrDecPoll) {
   const uint64_t now = global_timer_ns();
   if (t0 == 0) t0 = now;
   int st = 0;
   if (lane == 0) {
     if (*abort) st = 1;
     else if (now - t0 > timeout_ns) {
-      atomicOr(err, kErrDecPoll);
+      atomicOr(err, bit);
       *abort = 1;
       st = 1;
     }
@@ -355,9 +370,42 @@ __device__ __forceinline__ bool dec_poll_again(uint64_t& t0, volatile int* abort
 // phase): 8 output columns, 4 lanes per column; lane (c, j) sums the segments j, j + 4, j + 8,
 // ... of column c phase by phase in order, then the four lanes combine their sums in a fixed
 // tree, so the result's bits do not depend on timing.  Returns false on an abort.
+// The fused tensor-parallel exchange of one output word (row m, column col) held by the four
+// lanes of a column: lane j stores it to ranks j, j + 4; then every lane reads the tp_n ranks'
+// words of the column from this rank's area, retrying until all carry the tag, and sums them
+// in rank order.  Returns false on an abort.
+__device__ bool tp_exchange(const DecodeParams& p, int m, int col, int j, int lane, unsigned ttag,
+                            volatile int* abort, float& acc) {
+  const size_t off = (size_t)m * p.ldo + col;
+  const size_t par = ttag & 1u;
+  const unsigned long long w = tagged(acc, ttag);
+  for (int q = j; q < p.tp_n; q += 4)
+    st_sys_u64(p.tp_recv[q] + (par * p.tp_n + p.tp_rank) * p.tp_words + off, w);
+  const unsigned long long* own = p.tp_recv[p.tp_rank] + par * p.tp_n * p.tp_words + off;
+  uint64_t t0 = 0;
+  for (;;) {
+    unsigned long long v[kDecMaxRanks];
+    bool ok = true;
+#pragma unroll
+    for (int q = 0; q < kDecMaxRanks; ++q) {
+      v[q] = q < p.tp_n ? ld_sys_u64(own + (size_t)q * p.tp_words) : ((unsigned long long)ttag << 32);
+      ok = ok && (unsigned)(v[q] >> 32) == ttag;
+    }
+    if (__all_sync(0xffffffffu, ok)) {
+      float s = 0.f;
+#pragma unroll
+      for (int q = 0; q < kDecMaxRanks; ++q)
+        if (q < p.tp_n) s += __uint_as_float((unsigned)v[q]);
+      acc = s;
+      return true;
+    }
+    if (!dec_poll_again(t0, abort, p.err, p.timeout_ns, lane, kErrDecPeer)) return false;
+  }
+}
+
 template <int MT>
 __device__ bool reduce_task(const DecodeParams& p, int q0, int q1, int task, unsigned tag,
-                            int lane, volatile int* abort, const float* res_stash) {
+                            unsigned ttag, int lane, volatile int* abort, const float* res_stash) {
   constexpr int B = kDecReduceBatch;  // segments per lane per batch
   const int col = task * 8 + (lane >> 2), j = lane & 3;
   const int cu = col / kWideCols, cl = col % kWideCols;  // output phases cover every tile
@@ -391,6 +439,8 @@ __device__ bool reduce_task(const DecodeParams& p, int q0, int q1, int task, uns
     }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    // this rank's partial y, summed over the group's ranks (m < p.m is warp-uniform)
+    if (p.tp_n > 1 && m < p.m && !tp_exchange(p, m, col, j, lane, ttag, abort, acc)) return false;
     if (j == 0 && m < p.m) {
       if (p.residual)
         acc = (res_stash ? res_stash[m * 8 + (lane >> 2)] : p.residual[(size_t)m * p.ldr + col]) + acc;
@@ -544,6 +594,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   __shared__ volatile int s_abort;
   __shared__ volatile int s_never;
   __shared__ unsigned s_tag;
+  __shared__ unsigned s_ttag;
   __shared__ float s_res[kDecMaxTasksPerCta * 8 * MT];  // residual of this CTA's tasks (host x)
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -576,6 +627,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     s_abort = 0;
     s_never = 0;
     s_tag = p.epoch[b] + 1u;
+    s_ttag = p.tp_n > 1 ? p.tp_epoch[b] + 1u : 0u;
     dec_trace(p, 0);
   }
   __syncthreads();
@@ -788,7 +840,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     for (int k = warp; ok; k += kNC) {
       const int t = (int)b + (int)gridDim.x * k;
       if (t >= p.red_tasks) break;
-      ok = reduce_task<MT>(p, q0, q1, t, tag, lane, abort,
+      ok = reduce_task<MT>(p, q0, q1, t, tag, s_ttag, lane, abort,
                            (p.x_host && p.residual) ? s_res + k * 8 * MT : nullptr);
     }
     if (threadIdx.x == 0) dec_trace(p, 5);
@@ -808,6 +860,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
   if (threadIdx.x == 0) {
     for (unsigned j = b; j < (unsigned)kDecEpochSlots; j += gridDim.x) p.epoch[j] = tag;
+    if (p.tp_n > 1)
+      for (unsigned j = b; j < (unsigned)kDecEpochSlots; j += gridDim.x) p.tp_epoch[j] = s_ttag;
     // a CTA that gave up tells the host directly (its bits are in p.err as well)
     if (p.err_host && s_abort) *reinterpret_cast<volatile unsigned*>(p.err_host) = 1u;
     dec_trace(p, 6);

@@ -31,6 +31,8 @@ constexpr int kDecMaxTasksPerCta = 16;  // reduction tasks per CTA whose residua
 
 // error bits of the device error word (shared with the engine's)
 constexpr unsigned kErrDecPoll = 16u;  // a tagged partial never arrived
+constexpr unsigned kErrDecPeer = 32u;  // a peer rank's tagged output never arrived
+constexpr int kDecMaxRanks = 8;        // ranks of a fused tensor-parallel exchange
 
 struct DecPhase {
   int K, N;           // contraction size and output columns of the whole matrix
@@ -82,6 +84,17 @@ struct DecodeParams {
   unsigned* err;
   unsigned long long timeout_ns;
   unsigned long long* trace;  // optional [grid][kTraceEvents] global-timer stamps
+  // Tensor-parallel exchange fused into the reduction (tp_n > 1, the FFN of one rank's shard):
+  // each reduction task stores its columns' partial y as tagged words into every rank's area
+  // (plain peer stores over NVLink), then sums the tp_n ranks' words of those columns in rank
+  // order -- every rank gets the same bits.  The tag is this rank's group launch count + 1
+  // (every rank of the group makes the same sequence of these launches); the area has two
+  // halves by the tag's parity, so a rank a launch ahead never overwrites words a peer has yet
+  // to read.
+  int tp_n, tp_rank;
+  unsigned long long* tp_recv[kDecMaxRanks];  // rank r's area, mapped here: [2][tp_n][tp_words]
+  int tp_words;                               // words per (parity, source rank) >= m * ldo
+  unsigned* tp_epoch;                         // this rank's group launch counters [kDecEpochSlots]
 };
 
 // Dynamic shared memory of a launch with these sizes (1024-byte alignment slack included).

@@ -510,6 +510,8 @@ int ffn_engine_chunk(tk_device* d, const float* x, const float* norm_w, const tk
 
 constexpr int kDecSmemLimit = 227 * 1024;  // B200 opt-in shared memory per block
 constexpr int kDefaultGrid = 148;          // B200 SMs (the path queries assume the full device)
+// words per (parity, source rank) of the fused tensor-parallel exchange: 2 rows x 16384 columns
+constexpr size_t kTpFuseWords = 2 * 16384;
 
 // One phase of the decode kernel: tiles [wt0, wt1) of N (all when wt1 < 0) and groups [g0, g1) of
 // K (all when g1 < 0), nmat matrices, on `grid` CTAs.
@@ -613,6 +615,13 @@ bool dec_plan(const DecodeParams& p, int m, int mt, int gs, bool norm, int smem_
 int dec_split(const tk_device* d) { return d->ffn_split; }
 
 // Can the decode kernel take this call (default device settings)?
+// The fused tensor-parallel exchange of a decode launch (DecodeParams::tp_*).
+struct TpFuse {
+  int n, rank, words;
+  unsigned long long* recv[kDecMaxRanks];
+  unsigned* epoch;
+};
+
 bool decode_shape(int m, int k, int n, int inter, int gs, int grid, bool ffn) {
   if (m < 1 || m > 2 || !(gs == 16 || gs == 32 || gs == 64 || gs == 128)) return false;
   DecodeParams p;
@@ -627,7 +636,7 @@ bool decode_shape(int m, int k, int n, int inter, int gs, int grid, bool ffn) {
 int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
                const tk_int4_matrix* a0, const tk_int4_matrix* a1, const tk_int4_matrix* down,
                float* out, float* h_out, int m, int k, int n, int inter, int gs, bool residual,
-               cudaStream_t st, bool host_io = false) {
+               cudaStream_t st, bool host_io = false, const TpFuse* tpf = nullptr) {
   const bool ffn = down != nullptr;
   const int mt = m;  // instantiations for 1 and 2 rows
   const int grid = engine_grid(d);
@@ -712,6 +721,16 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
     return fail(TK_ERR_UNSUPPORTED, "host x with the residual: too many reduction tasks");
   p.err_host = d->capture_err_host;
   if (p.err_host) d->capture_err_used = true;
+  p.tp_n = 1;
+  if (tpf && tpf->n > 1) {
+    if ((size_t)m * n_out > (size_t)tpf->words)
+      return fail(TK_ERR_UNSUPPORTED, "fused exchange: output larger than the exchange area");
+    p.tp_n = tpf->n;
+    p.tp_rank = tpf->rank;
+    p.tp_words = tpf->words;
+    p.tp_epoch = tpf->epoch;
+    for (int r = 0; r < tpf->n; ++r) p.tp_recv[r] = tpf->recv[r];
+  }
   p.err = d->err;
   p.timeout_ns = d->timeout_ns;
   p.trace = d->trace;
@@ -1071,7 +1090,7 @@ int tk_device_check_error(tk_device* d) {
   unsigned h = 0;
   TK_CUDA_TRY(cudaMemcpy(&h, d->err, sizeof(h), cudaMemcpyDeviceToHost));
   if (h == 0) return TK_OK;
-  if (h & tk::kErrP2PWait) ++d->p2p_timeouts;
+  if (h & (tk::kErrP2PWait | tk::kErrDecPeer)) ++d->p2p_timeouts;
   // Clear the error word and return the engine's scratch to its launch-ready state.
   TK_CUDA_TRY(cudaDeviceSynchronize());
   TK_CUDA_TRY(cudaMemset(d->err, 0, 256));
@@ -1810,6 +1829,10 @@ struct tk_tp {
   void* p2p_base = nullptr;              // this rank's receive area + flags + chunk epochs
   void* p2p_peer[tk::kP2PMaxRanks] = {};  // peers' areas mapped here (CUDA IPC)
   tk::P2PParams p2p_params{};
+  // the batch 1-2 FFN's exchange fused into the decode kernel (same mapped areas): launch
+  // counters of this rank and every rank's tagged-word area
+  TpFuse fuse{};
+  bool fused = false;
   // the device's p2p_timeouts when the group was made: a wait of this group that ran out leaves
   // the ranks' chunk epochs out of step, so the group takes no further exchange after one
   unsigned p2p_timeouts_at_create = 0;
@@ -1851,7 +1874,10 @@ int tp_p2p_setup(tk_tp* tp, const NcclApi* n) {
   const size_t slot = kP2PMaxFloats;
   const size_t recv_bytes = 2 * (size_t)R * slot * sizeof(float);
   const size_t flag_bytes = (size_t)R * kP2PMaxChunks * sizeof(unsigned);
-  const size_t bytes = recv_bytes + flag_bytes + kP2PMaxChunks * sizeof(unsigned);
+  const size_t counter_bytes = kP2PMaxChunks * sizeof(unsigned);
+  const size_t fuse_epoch_off = recv_bytes + flag_bytes + counter_bytes;
+  const size_t fuse_off = fuse_epoch_off + kDecEpochSlots * sizeof(unsigned);
+  const size_t bytes = fuse_off + 2 * (size_t)R * kTpFuseWords * 8;
   int ok = 1;
   cudaIpcMemHandle_t mine{};
   if (cudaMalloc(&tp->p2p_base, bytes) != cudaSuccess || cudaMemset(tp->p2p_base, 0, bytes) != cudaSuccess ||
@@ -1885,6 +1911,7 @@ int tp_p2p_setup(tk_tp* tp, const NcclApi* n) {
     }
     P.recv[q] = static_cast<float*>(base);
     P.flags[q] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(base) + recv_bytes);
+    tp->fuse.recv[q] = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(base) + fuse_off);
   }
   int all = 0;
   int st = tp_sum_int(tp, n, ok, &all);
@@ -1901,6 +1928,12 @@ int tp_p2p_setup(tk_tp* tp, const NcclApi* n) {
   P.err = tp->dev->err;
   P.timeout_ns = tp->dev->timeout_ns;
   tp->p2p = true;
+  tp->fuse.n = R;
+  tp->fuse.rank = tp->rank;
+  tp->fuse.words = (int)kTpFuseWords;
+  tp->fuse.epoch = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(tp->p2p_base) + fuse_epoch_off);
+  const char* fused = std::getenv("TK_TP_FUSED");
+  tp->fused = !(fused && !std::atoi(fused));
   return TK_OK;
 }
 
@@ -1997,6 +2030,16 @@ int tk_tp_allreduce_sum_f32(tk_tp* tp, float* buf, size_t count, void* stream) {
   return TK_OK;
 }
 
+int tk_int4_ffn_tp_exchange(tk_tp* tp, uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs) {
+  if (!tp) return fail(TK_ERR_ARG, "tp is NULL");
+  if (tp->nranks == 1) return 0;
+  if (!tp->p2p) return 0;
+  if (tp->fused && m <= 2 && tp->dev->decode_enabled && (size_t)m * hidden <= kTpFuseWords &&
+      tk_int4_ffn_path(m, hidden, inter, gs) == 3)
+    return 2;
+  return (size_t)m * hidden <= tk::kP2PMaxFloats ? 1 : 0;
+}
+
 int tk_int4_ffn_tp_async(tk_tp* tp, const float* x, const float* norm_w, const tk_int4_matrix* gate,
                          const tk_int4_matrix* up, const tk_int4_matrix* down, float* out,
                          uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs, float eps,
@@ -2004,6 +2047,30 @@ int tk_int4_ffn_tp_async(tk_tp* tp, const float* x, const float* norm_w, const t
   if (!tp) return fail(TK_ERR_ARG, "tp is NULL");
   if (flags & TK_FFN_HOST_IO)
     return fail(TK_ERR_ARG, "TK_FFN_HOST_IO is not supported by the tensor-parallel FFN");
+  if (tp->nranks > 1 && tk_int4_ffn_tp_exchange(tp, m, hidden, inter, gs) == 2) {
+    // one decode launch per rank: its reduction stores this rank's partial y into every rank's
+    // area and sums the ranks' words in rank order (the residual, if any, after the sum)
+    if (!x || !norm_w || !gate || !up || !down || !out) return fail(TK_ERR_ARG, "NULL argument");
+    for (const tk_int4_matrix* a : {gate, up, down})
+      if (!a->w_packed || !a->scales || !a->zeros) return fail(TK_ERR_ARG, "NULL matrix pointer");
+    if (flags & ~TK_FFN_RESIDUAL) return fail(TK_ERR_ARG, "unknown flags 0x%x", flags);
+    if (tp->dev->p2p_timeouts != tp->p2p_timeouts_at_create)
+      return fail(TK_ERR_TIMEOUT,
+                  "a peer-memory exchange on this device timed out; the group's ranks are out of "
+                  "step: destroy it (tk_tp_destroy) and create a new one");
+    // (a rank taking another exchange than its peers would leave them waiting: buffers that
+    // would send one rank elsewhere are an error)
+    if (!(aligned16(x) && aligned16(norm_w) && aligned16(out) && matrix_aligned(gate) &&
+          matrix_aligned(up) && matrix_aligned(down)))
+      return fail(TK_ERR_ARG, "the fused exchange needs 16-byte aligned buffers");
+    int st = set_device(tp->dev);
+    if (st != TK_OK) return st;
+    st = decode_run(tp->dev, x, norm_w, eps, gate, up, down, out, nullptr, (int)m, (int)hidden, 0,
+                    (int)inter, (int)gs, (flags & TK_FFN_RESIDUAL) != 0,
+                    pick_stream(tp->dev, stream), false, &tp->fuse);
+    // unsupported is decided by the shapes and the device type, alike on every rank
+    if (st != TK_ERR_UNSUPPORTED) return st;
+  }
   // the residual is added once, by rank 0, before the sum
   const uint32_t f = tp->rank == 0 ? flags : (flags & ~TK_FFN_RESIDUAL);
   int st = tk_int4_ffn_async(tp->dev, x, norm_w, gate, up, down, out, nullptr, m, hidden, inter, gs,

@@ -94,6 +94,7 @@ SIGNATURES = {
     "tk_tp_destroy": (None, [vp]),
     "tk_tp_allreduce_sum_f32": (i32, [vp, vp, C.c_size_t, vp]),
     "tk_tp_uses_p2p": (i32, [vp]),
+    "tk_int4_ffn_tp_exchange": (i32, [vp, u32, u32, u32, u32]),
     "tk_int4_ffn_tp": (i32, [vp, vp, vp, C.POINTER(Int4MatrixC), C.POINTER(Int4MatrixC),
                              C.POINTER(Int4MatrixC), vp, u32, u32, u32, u32, f32, u32]),
     "tk_int4_ffn_tp_async": (i32, [vp, vp, vp, C.POINTER(Int4MatrixC), C.POINTER(Int4MatrixC),

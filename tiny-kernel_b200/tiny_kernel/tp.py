@@ -72,6 +72,12 @@ class Group:
         """True when exchanges go over NVLink peer memory (the one-shot all-reduce)."""
         return bool(_lib.lib().tk_tp_uses_p2p(self.handle))
 
+    def ffn_exchange(self, m, hidden, inter_shard, group_size) -> int:
+        """How int4_ffn sums the ranks' outputs at this shape: 2 fused into the decode kernel,
+        1 the peer-memory all-reduce kernel, 0 NCCL."""
+        return int(_lib.lib().tk_int4_ffn_tp_exchange(self.handle, int(m), int(hidden),
+                                                      int(inter_shard), int(group_size)))
+
     def close(self):
         if self.handle:
             _lib.lib().tk_tp_destroy(self.handle)
