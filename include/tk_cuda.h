@@ -40,7 +40,10 @@
  *   TK_ENGINE_STAGES    cap on the engine's shared-memory ring depth (default: deepest fit)
  *   TK_FFN_SPLIT        gate/up tile ranges of the engine's FFN, 1..4 (default 1)
  *   TK_DOWN_PREFETCH=0  no L2 prefetch of the down projection at the gate/up -> down switch
+ *   TK_DECODE=0         1-2 rows run the streaming engine instead of the decode kernel
  *   TK_TP_NCCL=1        tk_tp groups use NCCL for every exchange (read at tk_tp_create)
+ *   TK_TP_FUSED=0       tk_tp groups do not fuse the batch 1-2 FFN's exchange into the decode
+ *                       kernel (read at tk_tp_create)
  *   TK_NCCL_LIB         path of the libnccl.so.2 the tk_tp_* calls load
  *
  * INT4 weight layout (identical to qmatmul_int4, src/kernels/shaders.zig:442-501):
@@ -149,11 +152,11 @@ int tk_buffer_download_async(tk_device *dev, void *dst_host, const void *src_dev
  * x f32 [m][k], out f32 [m][n].  The reference computes row 0 only and requires
  * k <= 4096; this entry point computes all m rows and any k with k % group_size == 0,
  * group_size % 8 == 0, n even.  Shapes with n % 128 == 0, k % 128 == 0 and
- * group_size in {16, 32, 64, 128} (16-byte aligned pointers) run the TMA-fed streaming
- * engine up to 15 rows -- dp2a on the CUDA cores against activations quantised to int16 per
- * group at 1-2 rows, int8 tensor-core MMAs (mma.sync) against int8 hi/lo activation parts at
- * 3-4 rows, chunks of 4 rows beyond -- and the tcgen05 dequant-to-f16 GEMM from 16 rows
- * (tk_qmatmul_int4_path); other legal shapes run a plain CUDA-core kernel. */
+ * group_size in {16, 32, 64, 128} (16-byte aligned pointers) run TMA-fed kernels: at 1-2 rows
+ * the decode kernel (one persistent launch, dp2a on the CUDA cores against activations
+ * quantised to int16 per group), at 3-15 rows the streaming engine in chunks of 4 rows (int8
+ * tensor-core MMAs, mma.sync, against int8 hi/lo activation parts), from 16 rows the tcgen05
+ * dequant-to-f16 GEMM (tk_qmatmul_int4_path); other legal shapes run a plain CUDA-core kernel. */
 int tk_qmatmul_int4(tk_device *dev, const float *x, const uint8_t *w_packed,
                     const uint16_t *scales, const uint8_t *zeros, float *out, uint32_t m,
                     uint32_t k, uint32_t n, uint32_t group_size);
