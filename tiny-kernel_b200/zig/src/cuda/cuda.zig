@@ -73,6 +73,11 @@ pub const Device = struct {
         return Buffer(T).init(self, count);
     }
 
+    /// Pinned host memory (TK_MEM_HOST): the x / out of FusedInt4FFN.forwardHostIo.
+    pub fn createHostBuffer(self: *Device, comptime T: type, count: usize) !Buffer(T) {
+        return Buffer(T).initKind(self, count, c.TK_MEM_HOST);
+    }
+
     pub fn createBufferWithData(self: *Device, comptime T: type, data: []const T) !Buffer(T) {
         var b = try Buffer(T).init(self, data.len);
         @memcpy(b.slice(), data);
@@ -96,8 +101,13 @@ pub fn Buffer(comptime T: type) type {
         const Self = @This();
 
         pub fn init(device: *Device, count: usize) !Self {
+            return initKind(device, count, c.TK_MEM_SHARED);
+        }
+
+        /// kind: TK_MEM_SHARED (managed), TK_MEM_HOST (pinned host) or TK_MEM_DEVICE.
+        pub fn initKind(device: *Device, count: usize, kind: c_int) !Self {
             var p: ?*anyopaque = null;
-            try check(c.tk_buffer_alloc(device.ctx, count * @sizeOf(T), c.TK_MEM_SHARED, &p));
+            try check(c.tk_buffer_alloc(device.ctx, count * @sizeOf(T), kind, &p));
             return .{ .handle = @ptrCast(@alignCast(p.?)), .count = count, .device = device };
         }
 

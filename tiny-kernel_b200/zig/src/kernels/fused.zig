@@ -109,6 +109,32 @@ pub const FusedInt4FFN = struct {
             out.handle, if (h) |b| b.handle else null, m, hidden, inter, group_size, eps,
             if (residual) c.TK_FFN_RESIDUAL else 0));
     }
+
+    /// forward() with x and out in pinned host memory (Device.createHostBuffer): at 1-2 rows the
+    /// kernel reads x and writes out over the host link itself, and repeated calls with the same
+    /// arguments replay one recorded CUDA graph (TK_FFN_HOST_IO).
+    pub fn forwardHostIo(
+        self: *FusedInt4FFN,
+        x: *cuda.Buffer(f32),
+        norm_weight: *cuda.Buffer(f32),
+        gate: quantized.Int4Weights,
+        up: quantized.Int4Weights,
+        down: quantized.Int4Weights,
+        out: *cuda.Buffer(f32),
+        m: u32,
+        hidden: u32,
+        inter: u32,
+        group_size: u32,
+        eps: f32,
+        residual: bool,
+    ) !void {
+        const g = gate.raw();
+        const u = up.raw();
+        const d = down.raw();
+        try cuda.check(c.tk_int4_ffn(self.device.ctx, x.handle, norm_weight.handle, &g, &u, &d,
+            out.handle, null, m, hidden, inter, group_size, eps,
+            c.TK_FFN_HOST_IO | (if (residual) c.TK_FFN_RESIDUAL else 0)));
+    }
 };
 
 /// Tensor-parallel INT4 FFN: rank r of `nranks` holds the gate/up columns and down rows
