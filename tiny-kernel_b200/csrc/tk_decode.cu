@@ -88,6 +88,13 @@ __device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned 
   }
 }
 
+// Items (groups touched) of CTA b's range in phase P.
+__device__ __forceinline__ int phase_items(const DecPhase& P, unsigned b) {
+  if (b >= P.ctas) return 0;
+  const unsigned beg = P.units * b / P.ctas, end = P.units * (b + 1) / P.ctas;
+  return (int)((end - 1) / (unsigned)P.spg - beg / (unsigned)P.spg + 1);
+}
+
 __device__ __forceinline__ void it_start(It& it, const DecodeParams& p, unsigned b) {
   it.ph = 0;
   it.i = it.n = it.cu = it.grp = it.s0 = it.s1 = it.last_s1 = 0;
@@ -212,33 +219,53 @@ __device__ __forceinline__ bool dec_wait_full(uint64_t* bar, uint32_t par, volat
   }
 }
 
-// Consumer warp `slice`: all of this CTA's items of phase `ph` (it.ph == ph on entry), dp2a
-// arithmetic; each finished segment's partial sums are stored as tagged words.  Records: the
-// group's (rec_by_item == 0: rec + absolute group * frag_bytes, the x records) or the item's
-// (rec + i * frag_bytes, the phase's h records).
-// Returns false on an abort.
+// Per-stage item descriptors, written by the producer lane before it arms a stage (the stage's
+// full barrier orders them before the consumers' reads): everything a consumer needs about the
+// item in the stage, so the consumer loop carries no work-split iterator.
+//   x: absolute group of the item (x records) | item index within the phase << 16 (h records)
+//   y: first k-step | end k-step << 8 | segment end << 16 | column slices of the tile << 24
+//   z: column unit | segment (this CTA's range within the unit) << 16
+__shared__ uint4 s_desc[kMaxStages];
+
+__device__ __forceinline__ uint4 item_desc(const DecPhase& P, const It& it, unsigned b) {
+  uint4 d;
+  d.x = (unsigned)it_group(it) | ((unsigned)it.i << 16);
+  const bool seg_end = it_seg_end(it);
+  d.y = (unsigned)it.s0 | ((unsigned)it.s1 << 8) | ((unsigned)seg_end << 16) |
+        ((unsigned)it_slices(it) << 24);
+  int c0 = 0;
+  if (seg_end) dec_nseg(P, it.cu, &c0);
+  d.z = (unsigned)it.cu | ((unsigned)((int)b - c0) << 16);
+  d.w = 0u;
+  return d;
+}
+
+// Consumer warp `slice`: the n items of this CTA in phase P, dp2a arithmetic; each finished
+// segment's partial sums are stored as tagged words.  Records: the group's (rec_by_item == 0:
+// rec + absolute group * frag_bytes, the x records) or the item's (rec + i * frag_bytes, the
+// phase's h records).  Returns false on an abort.
 template <int MT, int GS>
-__device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, It& it,
-                              unsigned b, int slice, int lane, uint8_t* tiles, uint8_t* auxs,
-                              uint64_t* full, uint64_t* empty, int& slot, uint32_t& parity,
-                              long long& consumed, const uint8_t* rec, bool rec_by_item,
-                              unsigned tag, volatile int* abort, unsigned long long* wait_ns,
-                              unsigned long long* first_ns, unsigned long long* last_ns) {
-  constexpr int R = GS / 2;                 // packed rows per group
+__device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int n, int slice, int lane,
+                              uint8_t* tiles, uint8_t* auxs, uint64_t* full, uint64_t* empty,
+                              int& slot, uint32_t& parity, long long& consumed, const uint8_t* rec,
+                              bool rec_by_item, unsigned tag, volatile int* abort,
+                              unsigned long long* wait_ns, unsigned long long* first_ns,
+                              unsigned long long* last_ns) {
+  constexpr int R = GS / 2;  // packed rows per group
   // rows per chunk: 16 at one row (the chunk pair fully unrolled), 8 at two (a rolled loop over
   // chunk pairs, which keeps the two rows' accumulators and chunks in registers)
   constexpr int HB = MT == 1 ? (R <= 32 ? R / 2 : 16) : (R <= 16 ? R / 2 : 8);
   constexpr int NCH = R / HB;  // chunks per item (2 to 8)
   constexpr int kPairUnroll = MT == 1 ? NCH / 2 : 1;
   constexpr int tok_stride = dp_tok_stride(GS);
+  if (n <= 0) return true;
   const int S = p.stages;
   const int fb = p.frag_bytes;
   auto stage_tile = [&](int sl) { return tiles + (size_t)sl * p.tile_stage_bytes + slice * kTileCols; };
   auto stage_aux = [&](int sl) { return auxs + (size_t)sl * p.aux_stage_bytes; };
-  auto item_rec = [&](const It& x) {
-    return rec + (size_t)(rec_by_item ? x.i : it_group(x)) * fb;
+  auto item_rec = [&](const uint4& d) {
+    return rec + (size_t)(rec_by_item ? (d.x >> 16) : (d.x & 0xffffu)) * fb;
   };
-  if (it.ph != ph) return true;
   uint32_t wA[HB], wB[HB];
   uint4 XA[MT][HB / 4], XB[MT][HB / 4];
   DpMeta<MT> Mc, Mn;
@@ -255,31 +282,34 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
     *last_ns = t1;
     return r;
   };
+  // the first chunk (rows, activations) and the metadata of the item described by d in stage sl
+  auto load_first = [&](int sl, const uint4& d, DpMeta<MT>& M) {
+    const uint8_t* r = item_rec(d);
+    const int s0 = (int)(d.y & 0xffu), s1 = (int)((d.y >> 8) & 0xffu);
+    dp_load_meta<MT, GS>(stage_aux(sl), r, slice, lane, s0, s1, M);
+    dp_load_rows_all<HB>(stage_tile(sl), 0, lane, wA);
+    dp_load_x_in<MT, HB>(r, tok_stride, 0, s0 * kStepRows, s1 * kStepRows, XA);
+  };
   if (!wait_stage(slot, parity)) return false;
   if (wait_ns) *first_ns = global_timer_ns();
-  {
-    const uint8_t* r = item_rec(it);
-    dp_load_meta<MT, GS>(stage_aux(slot), r, slice, lane, it.s0, it.s1, Mc);
-    dp_load_rows_all<HB>(stage_tile(slot), 0, lane, wA);
-    dp_load_x_in<MT, HB>(r, tok_stride, 0, it.s0 * kStepRows, it.s1 * kStepRows, XA);
-  }
-  for (;;) {
-    const int r0 = it.s0 * kStepRows, r1 = it.s1 * kStepRows;
+  uint4 d = s_desc[slot];
+  load_first(slot, d, Mc);
+  for (int i = 0;; ++i) {
+    const int r0 = (int)(d.y & 0xffu) * kStepRows, r1 = (int)((d.y >> 8) & 0xffu) * kStepRows;
     const uint8_t* tl = stage_tile(slot);
-    const uint8_t* r = item_rec(it);
-    const bool seg_end = it_seg_end(it);
-    It nx = it;
-    it_next(nx, p, b);
+    const uint8_t* r = item_rec(d);
+    const bool seg_end = (d.y >> 16) & 1u;
+    const bool more = i + 1 < n;
     const int nslot = slot + 1 == S ? 0 : slot + 1;
     const uint32_t npar = slot + 1 == S ? parity ^ 1u : parity;
-    const bool more = nx.ph == ph;
     const bool prefetch = !seg_end && more;
     bool next_loaded = false, ok = true;
+    uint4 nd = d;
     int aL[MT][4], aH[MT][4];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) aL[m][i] = aH[m][i] = 0;
+      for (int q = 0; q < 4; ++q) aL[m][q] = aH[m][q] = 0;
 #pragma unroll kPairUnroll
     for (int c = 0; c < NCH; c += 2) {
       dp_load_rows_all<HB>(tl, (c + 1) * HB, lane, wB);
@@ -300,10 +330,8 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
         if (!__all_sync(0xffffffffu, nready) && !wait_stage(nslot, npar)) {
           ok = false;
         } else {
-          const uint8_t* nr = item_rec(nx);
-          dp_load_meta<MT, GS>(stage_aux(nslot), nr, slice, lane, nx.s0, nx.s1, Mn);
-          dp_load_rows_all<HB>(stage_tile(nslot), 0, lane, wA);
-          dp_load_x_in<MT, HB>(nr, tok_stride, 0, nx.s0 * kStepRows, nx.s1 * kStepRows, XA);
+          nd = s_desc[nslot];
+          load_first(nslot, nd, Mn);
           next_loaded = true;
         }
       }
@@ -314,33 +342,26 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int ph, 
     slot = nslot;
     parity = npar;
     if (seg_end) {
-      if (slice < it_slices(it)) {
-        int c0 = 0;
-        dec_nseg(P, it.cu, &c0);
-        const int seg = (int)b - c0;
+      if (slice < (int)(d.y >> 24)) {
+        const int cu = (int)(d.z & 0xffffu), seg = (int)(d.z >> 16);
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          unsigned long long* dst = dec_part<MT>(P, it.cu, seg, m) + slice * kTileCols + 4 * lane;
+          unsigned long long* dst = dec_part<MT>(P, cu, seg, m) + slice * kTileCols + 4 * lane;
           st_cg_u64x2(dst, tagged(y[4 * m], tag), tagged(y[4 * m + 1], tag));
           st_cg_u64x2(dst + 2, tagged(y[4 * m + 2], tag), tagged(y[4 * m + 3], tag));
         }
       }
 #pragma unroll
-      for (int i = 0; i < 4 * MT; ++i) y[i] = 0.f;
+      for (int q = 0; q < 4 * MT; ++q) y[q] = 0.f;
     }
     if (!ok) return false;
-    if (!more) {
-      it = nx;
-      return true;
-    }
+    if (!more) return true;
     if (!next_loaded) {
       if (!wait_stage(slot, parity)) return false;
-      const uint8_t* nr = item_rec(nx);
-      dp_load_meta<MT, GS>(stage_aux(slot), nr, slice, lane, nx.s0, nx.s1, Mn);
-      dp_load_rows_all<HB>(stage_tile(slot), 0, lane, wA);
-      dp_load_x_in<MT, HB>(nr, tok_stride, 0, nx.s0 * kStepRows, nx.s1 * kStepRows, XA);
+      nd = s_desc[slot];
+      load_first(slot, nd, Mn);
     }
-    it = nx;
+    d = nd;
     Mc = Mn;
   }
 }
@@ -668,6 +689,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
         if (s_abort) break;
         const DecPhase& P = p.ph[it.ph];
+        s_desc[ws] = item_desc(P, it, b);
         issue_item(maps, P, it, tiles + (size_t)ws * p.tile_stage_bytes,
                    auxs + (size_t)ws * p.aux_stage_bytes, &full[ws], pol);
         s_armed = ++G;
@@ -771,8 +793,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     if (threadIdx.x == 0) dec_trace(p, 1);
     if (s_abort) ok = false;
 
-    It it;
-    it_start(it, p, b);
     // trace of consumer warp 0: stage waits per phase, item counts, first / last phase-B stage
     const bool tw = p.trace && warp == 0;
     // the A phases (x records), then per B phase its records and its items: one inlined copy of
@@ -781,10 +801,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     int nitems = 0;
 #pragma unroll 1
     for (int q = 0; q < p.na; ++q) {
-      nitems += it.ph == q ? it.n : 0;
+      const int n = phase_items(p.ph[q], b);
+      nitems += n;
       if (ok)
-        ok = consume_phase<MT, GS>(p, p.ph[q], q, it, b, slice, lane, tiles, auxs, full, empty,
-                                   slot, parity, consumed, rec0, false, tag, abort,
+        ok = consume_phase<MT, GS>(p, p.ph[q], n, slice, lane, tiles, auxs, full, empty, slot,
+                                   parity, consumed, rec0, false, tag, abort,
                                    tw ? &wt : nullptr, &ft, &lt);
     }
     if (threadIdx.x == 0) {
@@ -818,10 +839,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       named_barrier(1, kNC * 32);
       if (*abort) ok = false;
       if (threadIdx.x == 0 && j == 0) dec_trace(p, 3);
-      nitems += it.ph == q ? it.n : 0;
+      const int n = phase_items(p.ph[q], b);
+      nitems += n;
       if (ok)
-        ok = consume_phase<MT, GS>(p, p.ph[q], q, it, b, slice, lane, tiles, auxs, full, empty,
-                                   slot, parity, consumed, recq, true, tag, abort,
+        ok = consume_phase<MT, GS>(p, p.ph[q], n, slice, lane, tiles, auxs, full, empty, slot,
+                                   parity, consumed, recq, true, tag, abort,
                                    tw ? &wt : nullptr, &ft, &lt);
     }
     if (threadIdx.x == 0 && nb > 0) {
