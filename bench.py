@@ -100,13 +100,13 @@ def load_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def load_traffic(m, n_gpus):
-    """Per-launch DRAM bytes of the engine from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "int4_ffn_engine_traffic.json")
+def load_traffic(key):
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "int4_ffn_decode_traffic.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return d.get(f"m{m}_tp{n_gpus}")
+        return d.get(key)
     except Exception:
         return None
 
@@ -641,8 +641,8 @@ def main():
             except Exception as e:
                 cpu_base = {"value": None, "unit": "GB/s", "cores": None, "kind": "port",
                             "sample": f"unavailable: {e}"}
-        traffic = (load_traffic(m, world) if (args.model == "8b" and L == 1 and not matvec)
-                   else None)
+        traffic = (load_traffic(f"mv_m{m}") if matvec and world == 1 else
+                   load_traffic(f"m{m}_tp{world}") if (args.model == "8b" and L == 1) else None)
         if path == 3:
             kern = ("tk::int4_decode_kernel (qmatmul_int4, one phase)" if matvec else
                     "tk::int4_decode_kernel (FFN: gate/up, h, down, y in one launch)")

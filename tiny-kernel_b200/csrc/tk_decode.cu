@@ -88,6 +88,23 @@ __device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned 
   }
 }
 
+// Whether CTA b's range of an A phase touches a group in [g0, g1) (the x records it needs).
+__device__ __forceinline__ bool a_range_needs(const DecodeParams& p, unsigned b, int g0, int g1) {
+  for (int q = 0; q < p.na; ++q) {
+    const DecPhase& P = p.ph[q];
+    if (b >= P.ctas) continue;
+    const unsigned beg = P.units * b / P.ctas, end = P.units * (b + 1) / P.ctas;
+    const unsigned per = (unsigned)(P.groups * P.spg);
+    if (end - beg >= per) return true;  // every group of a column unit
+    const int gf = (int)((beg / (unsigned)P.spg) % (unsigned)P.groups);
+    const int gl = (int)(((end - 1) / (unsigned)P.spg) % (unsigned)P.groups);
+    const bool in = gf <= gl ? (g0 <= gl && g1 > gf)                   // [gf, gl]
+                             : (g1 > gf || g0 <= gl);                  // [gf, G) and [0, gl]
+    if (in) return true;
+  }
+  return false;
+}
+
 // Items (groups touched) of CTA b's range in phase P.
 __device__ __forceinline__ int phase_items(const DecPhase& P, unsigned b) {
   if (b >= P.ctas) return 0;
@@ -755,7 +772,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 #pragma unroll
         for (int m = 0; m < MT; ++m) rms[m] = s_rms[m];
       }
+      // the records of the groups this CTA's gate/up (or matvec) range touches
       for (int ch = warp; ch < nchunks; ch += kNC) {
+        if (!a_range_needs(p, b, ch * kTileCols / GS, (ch + 1) * kTileCols / GS)) continue;
         float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
         if (p.norm_w) w4 = *reinterpret_cast<const float4*>(ws + ch * kTileCols + 4 * lane);
 #pragma unroll
