@@ -88,19 +88,41 @@ __device__ __forceinline__ void it_seek(It& it, const DecodeParams& p, unsigned 
   }
 }
 
-// Whether CTA b's range of an A phase touches a group in [g0, g1) (the x records it needs).
-__device__ __forceinline__ bool a_range_needs(const DecodeParams& p, unsigned b, int g0, int g1) {
-  for (int q = 0; q < p.na; ++q) {
+// The groups CTA b's ranges of the A phases touch (the x records it needs): per A phase an
+// interval [gf, gl] of a column unit's groups, wrapping past the last group when gl < gf, or all.
+struct NeedGroups {
+  int gf[kDecMaxPhases], gl[kDecMaxPhases];
+  bool all;
+};
+
+__device__ __forceinline__ NeedGroups a_range_groups(const DecodeParams& p, unsigned b) {
+  NeedGroups n;
+  n.all = false;
+#pragma unroll
+  for (int q = 0; q < kDecMaxPhases; ++q) {
+    n.gf[q] = 1;  // empty unless set
+    n.gl[q] = 0;
     const DecPhase& P = p.ph[q];
-    if (b >= P.ctas) continue;
+    if (q >= p.na || b >= P.ctas) continue;
     const unsigned beg = P.units * b / P.ctas, end = P.units * (b + 1) / P.ctas;
-    const unsigned per = (unsigned)(P.groups * P.spg);
-    if (end - beg >= per) return true;  // every group of a column unit
-    const int gf = (int)((beg / (unsigned)P.spg) % (unsigned)P.groups);
-    const int gl = (int)(((end - 1) / (unsigned)P.spg) % (unsigned)P.groups);
-    const bool in = gf <= gl ? (g0 <= gl && g1 > gf)                   // [gf, gl]
-                             : (g1 > gf || g0 <= gl);                  // [gf, G) and [0, gl]
-    if (in) return true;
+    if (end - beg >= (unsigned)(P.groups * P.spg)) n.all = true;  // every group of a unit
+    n.gf[q] = (int)((beg / (unsigned)P.spg) % (unsigned)P.groups);
+    n.gl[q] = (int)(((end - 1) / (unsigned)P.spg) % (unsigned)P.groups);
+  }
+  return n;
+}
+
+// Whether a group in [g0, g1) is among the needed ones.
+__device__ __forceinline__ bool needs_groups(const DecodeParams& p, const NeedGroups& n, unsigned b,
+                                             int g0, int g1) {
+  if (n.all) return true;
+#pragma unroll
+  for (int q = 0; q < kDecMaxPhases; ++q) {
+    if (q >= p.na || b >= p.ph[q].ctas) continue;
+    const int gf = n.gf[q], gl = n.gl[q];
+    if (gf <= gl ? (g0 <= gl && g1 > gf)    // [gf, gl]
+                 : (g1 > gf || g0 <= gl))   // [gf, G) and [0, gl]
+      return true;
   }
   return false;
 }
@@ -444,7 +466,7 @@ __device__ bool tp_exchange(const DecodeParams& p, int m, int col, int j, int la
 template <int MT>
 __device__ bool reduce_task(const DecodeParams& p, int q0, int q1, int task, unsigned tag,
                             unsigned ttag, int lane, volatile int* abort, const float* res_stash) {
-  constexpr int B = kDecReduceBatch;  // segments per lane per batch
+  constexpr int B = kDecReduceBatch / MT;  // segments per lane per batch
   const int col = task * 8 + (lane >> 2), j = lane & 3;
   const int cu = col / kWideCols, cl = col % kWideCols;  // output phases cover every tile
 #pragma unroll 1
@@ -497,7 +519,8 @@ __device__ bool reduce_task(const DecodeParams& p, int q0, int q1, int task, uns
 // loaded 8 / MT at a time, all of a batch in flight, and summed in segment order.
 template <int MT, int GS>
 __device__ bool build_h_record(const DecodeParams& p, int j, int grp, bool write_h, uint8_t* rec,
-                               unsigned tag, int lane, volatile int* abort) {
+                               unsigned tag, int lane, volatile int* abort, int part = 0,
+                               int nparts = 1, float* xbuf = nullptr, int bar = 0) {
   constexpr int kSB = 8 / MT;              // segments in flight per batch
   constexpr bool kSplit = GS / 4 <= 16;  // a half warp per matrix
   constexpr int kMats = kSplit ? 1 : 2;  // matrices summed per lane
@@ -507,6 +530,7 @@ __device__ bool build_h_record(const DecodeParams& p, int j, int grp, bool write
   const int ta = c0 / kWideCols - A.wt0, cl = c0 % kWideCols;
   const int li = kSplit ? (lane & 15) : lane;
   const bool owner = li < GS / 4;
+  bool failed = false;
   float acc[kMats][MT][4];
 #pragma unroll
   for (int q = 0; q < kMats; ++q)
@@ -516,10 +540,13 @@ __device__ bool build_h_record(const DecodeParams& p, int j, int grp, bool write
   for (int q = 0; q < kMats; ++q) {
     const int mat = kSplit ? (lane >> 4) : q;
     const int cu = ta * 2 + mat;
-    const int ns = dec_nseg(A, cu, nullptr);
-    // warp-uniform batch count: the larger of the two matrices' segment counts
+    const int nst = dec_nseg(A, cu, nullptr);
+    // this warp's share of the segments (all of them, or a contiguous part)
+    const int sa = nst * part / nparts, ns = nst * (part + 1) / nparts;
+    // warp-uniform batch bound: the larger of the two matrices' segment ends
     const int nsw = kSplit ? max(ns, __shfl_xor_sync(0xffffffffu, ns, 16)) : ns;
-    for (int base = 0; base < nsw; base += kSB) {
+    const int saw = kSplit ? min(sa, __shfl_xor_sync(0xffffffffu, sa, 16)) : sa;
+    for (int base = saw; base < nsw && !failed; base += kSB) {
       uint64_t t0 = 0;
       for (;;) {
         ulonglong2 va[kSB][MT], vb[kSB][MT];
@@ -527,7 +554,7 @@ __device__ bool build_h_record(const DecodeParams& p, int j, int grp, bool write
         for (int i = 0; i < kSB; ++i)
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
-            if (owner && base + i < ns) {
+            if (owner && base + i >= sa && base + i < ns) {
               const unsigned long long* src = dec_part<MT>(A, cu, base + i, m) + cl + 4 * li;
               va[i][m] = ld_cg_u64x2(src);
               vb[i][m] = ld_cg_u64x2(src + 2);
@@ -555,9 +582,39 @@ __device__ bool build_h_record(const DecodeParams& p, int j, int grp, bool write
             }
           break;
         }
-        if (!dec_poll_again(t0, abort, p.err, p.timeout_ns, lane)) return false;
+        if (!dec_poll_again(t0, abort, p.err, p.timeout_ns, lane)) {
+          failed = true;  // a part still meets its partners at the barrier below
+          break;
+        }
       }
     }
+  }
+  if (nparts > 1) {
+    // the parts' sums meet in shared memory (the x records' area, free after the A phases) and
+    // the first part's warp adds them in part order
+    float* mine = xbuf + (size_t)part * (kMats * MT * 4 * 32);
+#pragma unroll
+    for (int q = 0; q < kMats; ++q)
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mine[((q * MT + m) * 4 + i) * 32 + lane] = acc[q][m][i];
+    named_barrier(bar, nparts * 32);
+    if (failed || *abort) return false;
+    if (part != 0) return true;
+#pragma unroll
+    for (int q = 0; q < kMats; ++q)
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float s = 0.f;
+          for (int r = 0; r < nparts; ++r)
+            s += xbuf[(size_t)r * (kMats * MT * 4 * 32) + ((q * MT + m) * 4 + i) * 32 + lane];
+          acc[q][m][i] = s;
+        }
+  } else if (failed) {
+    return false;
   }
   const bool holder = lane < GS / 4;  // lanes 0 .. GS/4 - 1 hold the group's h
 #pragma unroll
@@ -773,8 +830,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         for (int m = 0; m < MT; ++m) rms[m] = s_rms[m];
       }
       // the records of the groups this CTA's gate/up (or matvec) range touches
+      const NeedGroups need = a_range_groups(p, b);
       for (int ch = warp; ch < nchunks; ch += kNC) {
-        if (!a_range_needs(p, b, ch * kTileCols / GS, (ch + 1) * kTileCols / GS)) continue;
+        if (!needs_groups(p, need, b, ch * kTileCols / GS, (ch + 1) * kTileCols / GS)) continue;
         float4 w4 = make_float4(1.f, 1.f, 1.f, 1.f);
         if (p.norm_w) w4 = *reinterpret_cast<const float4*>(ws + ch * kTileCols + 4 * lane);
 #pragma unroll
@@ -842,15 +900,24 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const int q = p.na + j;
       uint8_t* recq = recb + (size_t)j * p.recb_items * p.frag_bytes;
       // the records of this CTA's items of B phase q: warp w builds items w, w + 8, ...
-      if (ok && b < p.ph[q].ctas) {
+      // With fewer items than warps (small phases: tensor-parallel shards) the warps of an item
+      // share its gate/up segments (parts of a contiguous range each, summed in part order in the
+      // x records' area, which the A phases no longer need).
+      const int nbi = phase_items(p.ph[q], b);
+      constexpr int kPartFloats = (GS / 4 <= 16 ? 1 : 2) * MT * 4 * 32;
+      int parts = nbi > 0 && nbi < kNC ? kNC / nbi : 1;
+      if ((size_t)nbi * parts * kPartFloats * sizeof(float) > (size_t)p.ph[0].groups * p.frag_bytes)
+        parts = 1;
+      if (ok && nbi > 0) {
         It bi;
         bi.ph = q;
         it_seek(bi, p, b);
         for (int i = 0; bi.ph == q && ok; ++i) {
-          if (i % kNC == warp)
-            ok = build_h_record<MT, GS>(p, j, it_group(bi),
-                                        p.h_out && it_tile(bi) == 0 && bi.s0 == 0,
-                                        recq + (size_t)i * p.frag_bytes, tag, lane, abort);
+          if (parts > 1 ? i == warp / parts : i % kNC == warp)
+            ok = build_h_record<MT, GS>(
+                p, j, it_group(bi), p.h_out && it_tile(bi) == 0 && bi.s0 == 0,
+                recq + (size_t)i * p.frag_bytes, tag, lane, abort, warp % parts, parts,
+                reinterpret_cast<float*>(rec0) + (size_t)i * parts * kPartFloats, 2 + i);
           it_next(bi, p, b);
         }
       }

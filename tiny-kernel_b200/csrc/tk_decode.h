@@ -26,7 +26,7 @@ constexpr int kDecConsumers = 8;                      // consumer warps (one per
 constexpr int kDecThreads = (kDecConsumers + 1) * 32;  // + the producer warp
 constexpr int kDecEpochSlots = 1024;  // launch counters: CTA b reads slot b, writes b + k*grid
 constexpr int kDecMaxItemsB = 64;     // phase-B items of one CTA whose records live in smem
-constexpr int kDecReduceBatch = 8;    // partials in flight per lane of a reduction task
+constexpr int kDecReduceBatch = 16;   // partials in flight per lane of a reduction task (/ rows)
 constexpr int kDecMaxTasksPerCta = 16;  // reduction tasks per CTA whose residual smem holds
 
 // error bits of the device error word (shared with the engine's)
