@@ -117,7 +117,7 @@ struct tk_device {
   int engine_ctas = 0;    // TK_ENGINE_CTAS: CTAs of the engine's launches (0: one per SM)
   int down_prefetch = 1;  // TK_DOWN_PREFETCH=0 turns off the L2 prefetch of the down projection
   int decode_enabled = 1;  // TK_DECODE=0 routes batch 1-2 through the streaming engine instead
-  ScratchBuf dec;          // decode kernel: launch epochs + tagged partial sums of both phases
+  ScratchBuf dec;          // decode kernel: launch epochs + tagged partial sums of its phases
   ScratchBuf io;           // TK_FFN_HOST_IO staging of x and out
   size_t dec_xdev_bytes = 0;  // the decode scratch's tagged host-x area
   // While a synchronous host-buffer call is being recorded into a graph: the pinned word its
@@ -178,6 +178,9 @@ int scratch_ensure(tk_device* d, ScratchBuf& b, size_t need) {
   size_t cap = std::max<size_t>(need, 4096);
   TK_CUDA_TRY(cudaMalloc(&b.ptr, cap));
   TK_CUDA_TRY(cudaMemset(b.ptr, 0, cap));
+  // the memset runs on the legacy stream, which the device's non-blocking stream does not wait
+  // for: finish it before any kernel can use the buffer
+  TK_CUDA_TRY(cudaDeviceSynchronize());
   b.cap = cap;
   ++d->scratch_gen;  // graphs recorded over the old buffers are stale
   return TK_OK;
@@ -1048,7 +1051,8 @@ int tk_device_create(int ordinal, tk_device** out) {
       cudaHostAlloc(&d->err_host, kErrHostSlots * sizeof(unsigned), cudaHostAllocDefault) !=
           cudaSuccess)
     return cleanup(fail(TK_ERR_NOMEM, "scratch allocation failed"));
-  if (cudaMemset(d->sync, 0, sizeof(SyncState)) != cudaSuccess || cudaMemset(d->err, 0, 256) != cudaSuccess)
+  if (cudaMemset(d->sync, 0, sizeof(SyncState)) != cudaSuccess || cudaMemset(d->err, 0, 256) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess)  // legacy-stream memsets: done before any kernel
     return cleanup(fail(TK_ERR_CUDA, "scratch init failed"));
   *out = d;
   return TK_OK;
@@ -1097,6 +1101,7 @@ int tk_device_check_error(tk_device* d) {
   TK_CUDA_TRY(cudaMemset(d->sync, 0, sizeof(SyncState)));
   for (auto* b : {&d->counters[0], &d->counters[1], &d->dec})
     if (b->ptr) TK_CUDA_TRY(cudaMemset(b->ptr, 0, b->cap));
+  TK_CUDA_TRY(cudaDeviceSynchronize());  // the memsets (legacy stream) before the next kernel
   return fail(TK_ERR_TIMEOUT, "device-side bounded wait gave up (error bits 0x%x)", h);
 }
 
@@ -1108,6 +1113,7 @@ int tk_device_trace_enable(tk_device* d, int enable) {
     TK_CUDA_TRY(cudaDeviceSynchronize());
     TK_CUDA_TRY(cudaMalloc(&d->trace, (size_t)d->sm_count * kTraceEvents * 8));
     TK_CUDA_TRY(cudaMemset(d->trace, 0, (size_t)d->sm_count * kTraceEvents * 8));
+    TK_CUDA_TRY(cudaDeviceSynchronize());
   } else if (!enable && d->trace) {
     TK_CUDA_TRY(cudaDeviceSynchronize());
     TK_CUDA_TRY(cudaFree(d->trace));
