@@ -41,6 +41,11 @@
  *   TK_FFN_SPLIT        gate/up tile ranges of the engine's FFN, 1..4 (default 1)
  *   TK_DOWN_PREFETCH=0  no L2 prefetch of the down projection at the gate/up -> down switch
  *   TK_DECODE=0         1-2 rows run the streaming engine instead of the decode kernel
+ *   TK_DECODE_PDL=0     the decode kernel is a cooperative launch that starts only after the
+ *                       preceding kernel of its stream has finished (default: a programmatic
+ *                       dependent launch whose CTAs are set up, and prefetch their first weights
+ *                       into L2, while that kernel finishes; the kernel still reads nothing the
+ *                       preceding kernel may write before it has completed)
  *   TK_TP_NCCL=1        tk_tp groups use NCCL for every exchange (read at tk_tp_create)
  *   TK_TP_FUSED=0       tk_tp groups do not fuse the batch 1-2 FFN's exchange into the decode
  *                       kernel (read at tk_tp_create)

@@ -200,6 +200,35 @@ __device__ __forceinline__ void issue_item(const TmapPack& maps, const DecPhase&
             (uint32_t)(ns * kZeroBytes), bar, pol);
 }
 
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// issue_item's copies as L2 prefetches (weights, scales, zero points: read-only inputs).
+__device__ __forceinline__ void prefetch_item(const TmapPack& maps, const DecPhase& P, const It& it) {
+  const int mat = it.cu & (it.nmat - 1);
+  const int wt = it_tile(it);
+  const int ns = it_slices(it);
+  const int row0 = it_group(it) * it.spg * kStepRows;
+  const int x = wt * (kWideCols / 8);
+  if (it.s0 == 0 && it.s1 == it.spg) {
+    tma_prefetch_2d(&maps.map[P.map_base + 2 * mat], x, row0);
+  } else {
+    for (int s = it.s0; s < it.s1; ++s)
+      tma_prefetch_2d(&maps.map[P.map_base + 2 * mat + 1], x, row0 + s * kStepRows);
+  }
+  const int col0 = wt * kWideCols;
+  const size_t g = (size_t)it_group(it);
+  bulk_prefetch_l2(P.scales[mat] + g * P.N + col0, (uint32_t)(ns * kScaleBytes));
+  bulk_prefetch_l2(P.zeros[mat] + g * (P.N / 2) + col0 / 2, (uint32_t)(ns * kZeroBytes));
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned long long tagged(float v, unsigned tag) {
   return ((unsigned long long)tag << 32) | __float_as_uint(v);
 }
@@ -707,6 +736,25 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       mbar_init(&empty[i], kNC);
     }
     fence_mbar_init();
+    s_armed = p.pro_stages;
+    s_abort = 0;
+    s_never = 0;
+  }
+  __syncthreads();
+  if (warp == kProducerWarp && lane == 0) {
+    // the first ring's worth of weight items into L2 while a preceding launch may still run
+    It it;
+    it_start(it, p, b);
+    for (int i = 0; i < S && it.ph < p.nph; ++i) {
+      prefetch_item(maps, p.ph[it.ph], it);
+      it_next(it, p, b);
+    }
+  }
+  if (threadIdx.x == 0) {
+    // the next launch of the stream may be scheduled now; this one reads nothing a preceding
+    // kernel writes before that kernel has completed
+    griddep_launch_dependents();
+    griddep_wait();
     // the prologue copies go out first (x rows, then the norm weight, contiguous over the first
     // pro_stages stages' tiles): everything the consumers do first waits for them
     const uint32_t xrow = (uint32_t)p.ph[0].K * 4u;
@@ -718,9 +766,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         bulk_load(tiles + (size_t)m * xrow, p.x + (size_t)m * p.ldx, xrow, &full[0], pol);
     if (p.norm_w) bulk_load(tiles + (size_t)p.m * xrow, p.norm_w, xrow, &full[0], pol);
     for (int i = 1; i < p.pro_stages; ++i) mbar_arrive(&full[i]);
-    s_armed = p.pro_stages;
-    s_abort = 0;
-    s_never = 0;
     s_tag = p.epoch[b] + 1u;
     s_ttag = p.tp_n > 1 ? p.tp_epoch[b] + 1u : 0u;
     dec_trace(p, 0);
@@ -985,8 +1030,16 @@ cudaError_t dec_launch_mt(const TmapPack& maps, const DecodeParams& p, int grid,
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  if (p.pdl) {
+    // every CTA must become resident (they wait on one another): one CTA per SM and grid <= SMs
+    // give that on a device this launch does not share; the bounded waits end in an error
+    // otherwise
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, int4_decode_kernel<MT, GS>, maps, p);

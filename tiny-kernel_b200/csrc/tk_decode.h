@@ -84,6 +84,11 @@ struct DecodeParams {
   unsigned* err;
   unsigned long long timeout_ns;
   unsigned long long* trace;  // optional [grid][kTraceEvents] global-timer stamps
+  // 1: launched with programmatic stream serialization (the launch may start while the
+  // preceding kernel of the stream finishes; it reads nothing that kernel may write before
+  // griddepcontrol.wait, only L2-prefetches its first weight items), not as a cooperative launch;
+  // 0: a cooperative launch
+  int pdl;
   // Tensor-parallel exchange fused into the reduction (tp_n > 1, the FFN of one rank's shard):
   // each reduction task stores its columns' partial y as tagged words into every rank's area
   // (plain peer stores over NVLink), then sums the tp_n ranks' words of those columns in rank

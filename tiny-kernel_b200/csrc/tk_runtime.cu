@@ -117,6 +117,7 @@ struct tk_device {
   int engine_ctas = 0;    // TK_ENGINE_CTAS: CTAs of the engine's launches (0: one per SM)
   int down_prefetch = 1;  // TK_DOWN_PREFETCH=0 turns off the L2 prefetch of the down projection
   int decode_enabled = 1;  // TK_DECODE=0 routes batch 1-2 through the streaming engine instead
+  int decode_pdl = 1;      // TK_DECODE_PDL=0: cooperative launches without programmatic overlap
   ScratchBuf dec;          // decode kernel: launch epochs + tagged partial sums of its phases
   ScratchBuf io;           // TK_FFN_HOST_IO staging of x and out
   size_t dec_xdev_bytes = 0;  // the decode scratch's tagged host-x area
@@ -737,6 +738,7 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   p.err = d->err;
   p.timeout_ns = d->timeout_ns;
   p.trace = d->trace;
+  p.pdl = d->decode_pdl;
   if (d->trace)
     TK_CUDA_TRY(cudaMemsetAsync(d->trace, 0, (size_t)d->sm_count * kTraceEvents * 8, st));
   int blocks = 0;
@@ -1042,6 +1044,7 @@ int tk_device_create(int ordinal, tk_device** out) {
   if (const char* env = std::getenv("TK_DOWN_PREFETCH")) d->down_prefetch = std::atoi(env);
   if (const char* env = std::getenv("TK_ENGINE_CTAS")) d->engine_ctas = std::atoi(env);
   if (const char* env = std::getenv("TK_DECODE")) d->decode_enabled = std::atoi(env);
+  if (const char* env = std::getenv("TK_DECODE_PDL")) d->decode_pdl = std::atoi(env);
   if (const char* env = std::getenv("TK_WAIT_TIMEOUT_MS"))
     d->timeout_ns = (unsigned long long)std::atoll(env) * 1000000ull;
   if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess)
