@@ -1,6 +1,6 @@
 // tk_decode.h -- parameters of the batch 1-2 decode kernel (tk_decode.cu).
 //
-// One persistent, cooperative launch (one CTA per SM) computes either
+// One persistent launch (one CTA per SM, all resident) computes either
 //   qmatmul_int4 (src/kernels/shaders.zig:442-501):  phase A = y[m][N] = x . W
 // or the INT4 Llama FFN (src/bench.zig:266-341 + the down projection and residual of
 // src/model/llama.zig:220-231):
