@@ -585,7 +585,9 @@ def main():
                                           ob_host.nbytes, None))
         check(Lb.tk_device_synchronize(dev.handle))
 
-    for i in range(3):
+    # untimed: every weight copy once (a synchronous host-buffer call records its graph the first
+    # time it meets a set of arguments)
+    for i in range(max(3, copies)):
         e2e_step(i)
     if pg is not None:
         pg.barrier()
