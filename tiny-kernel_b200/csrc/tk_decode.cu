@@ -181,7 +181,7 @@ __device__ __forceinline__ void issue_item(const TmapPack& maps, const DecPhase&
   const int mat = it.cu & (it.nmat - 1);
   const int wt = it_tile(it);
   const int ns = it_slices(it);
-  const uint32_t bytes = (uint32_t)((it.s1 - it.s0) * kStepRows * kRowBytes +
+  const uint32_t bytes = (uint32_t)(it.spg * kStepRows * kRowBytes +
                                     ns * (kScaleBytes + kZeroBytes));
   mbar_arrive_expect_tx(bar, bytes);
   const int row0 = it_group(it) * it.spg * kStepRows;
@@ -189,9 +189,15 @@ __device__ __forceinline__ void issue_item(const TmapPack& maps, const DecPhase&
   if (it.s0 == 0 && it.s1 == it.spg) {
     tma_load_2d(tile, &maps.map[P.map_base + 2 * mat], bar, x, row0, pol);
   } else {
-    for (int s = it.s0; s < it.s1; ++s)
-      tma_load_2d(tile + s * kStepRows * kRowBytes, &maps.map[P.map_base + 2 * mat + 1], bar, x,
-                  row0 + s * kStepRows, pol);
+    // a partial item: its k-steps, and zero rows for the group's others (so the consumers need
+    // no row masks: zero codes contribute nothing, and the zero-point sums cover its k-steps only)
+    for (int s = 0; s < it.spg; ++s) {
+      if (s >= it.s0 && s < it.s1)
+        tma_load_2d(tile + s * kStepRows * kRowBytes, &maps.map[P.map_base + 2 * mat + 1], bar, x,
+                    row0 + s * kStepRows, pol);
+      else
+        tma_load_2d(tile + s * kStepRows * kRowBytes, &maps.map[kZeroMap], bar, 0, 0, pol);
+    }
   }
   const int col0 = wt * kWideCols;
   const size_t g = (size_t)it_group(it);
@@ -356,14 +362,13 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int n, i
     const int s0 = (int)(d.y & 0xffu), s1 = (int)((d.y >> 8) & 0xffu);
     dp_load_meta<MT, GS>(stage_aux(sl), r, slice, lane, s0, s1, M);
     dp_load_rows_all<HB>(stage_tile(sl), 0, lane, wA);
-    dp_load_x_in<MT, HB>(r, tok_stride, 0, s0 * kStepRows, s1 * kStepRows, XA);
+    dp_load_x<MT, HB>(r, tok_stride, 0, XA);
   };
   if (!wait_stage(slot, parity)) return false;
   if (wait_ns) *first_ns = global_timer_ns();
   uint4 d = s_desc[slot];
   load_first(slot, d, Mc);
   for (int i = 0;; ++i) {
-    const int r0 = (int)(d.y & 0xffu) * kStepRows, r1 = (int)((d.y >> 8) & 0xffu) * kStepRows;
     const uint8_t* tl = stage_tile(slot);
     const uint8_t* r = item_rec(d);
     const bool seg_end = (d.y >> 16) & 1u;
@@ -381,7 +386,7 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int n, i
 #pragma unroll kPairUnroll
     for (int c = 0; c < NCH; c += 2) {
       dp_load_rows_all<HB>(tl, (c + 1) * HB, lane, wB);
-      dp_load_x_in<MT, HB>(r, tok_stride, (c + 1) * HB, r0, r1, XB);
+      dp_load_x<MT, HB>(r, tok_stride, (c + 1) * HB, XB);
       bool nready = false;
       if (c + 2 == NCH) {
         // every byte of this stage is loaded (in issue order before the arrival)
@@ -392,7 +397,7 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int n, i
       dp_compute<MT, HB>(wA, XA, aL, aH);
       if (c + 2 < NCH) {
         dp_load_rows_all<HB>(tl, (c + 2) * HB, lane, wA);
-        dp_load_x_in<MT, HB>(r, tok_stride, (c + 2) * HB, r0, r1, XA);
+        dp_load_x<MT, HB>(r, tok_stride, (c + 2) * HB, XA);
       } else if (prefetch) {
         // the next item's first chunk while this item's last chunk computes
         if (!__all_sync(0xffffffffu, nready) && !wait_stage(nslot, npar)) {

@@ -77,9 +77,8 @@ __device__ __forceinline__ void dp_load_rows(const uint8_t* tl, int rb, int r0, 
   }
 }
 
-// Packed bytes of rows [rb, rb + RB) of this lane's 4 columns, whatever the item's row range:
-// for a partial item the rows outside it hold bytes of an earlier copy, which dp_load_x_in
-// pairs with zero activations.
+// Packed bytes of rows [rb, rb + RB) of this lane's 4 columns, whatever the item's row range
+// (the decode kernel fills a partial item's other k-steps with zero rows).
 template <int RB>
 __device__ __forceinline__ void dp_load_rows_all(const uint8_t* tl, int rb, int lane,
                                                  uint32_t (&w)[RB]) {
@@ -97,22 +96,6 @@ __device__ __forceinline__ void dp_load_x(const uint8_t* rec, int tok_stride, in
     const uint4* xp = reinterpret_cast<const uint4*>(rec + (size_t)m * tok_stride) + rb / 4;
 #pragma unroll
     for (int q = 0; q < RB / 4; ++q) X[m][q] = xp[q];
-  }
-}
-
-// dp_load_x with the activations of rows outside [r0, r1) (whole k-steps of 8 rows) as zero.
-template <int MT, int RB>
-__device__ __forceinline__ void dp_load_x_in(const uint8_t* rec, int tok_stride, int rb, int r0,
-                                             int r1, uint4 (&X)[MT][RB / 4]) {
-#pragma unroll
-  for (int m = 0; m < MT; ++m) {
-    const uint4* xp = reinterpret_cast<const uint4*>(rec + (size_t)m * tok_stride) + rb / 4;
-#pragma unroll
-    for (int q = 0; q < RB / 4; ++q) {
-      const uint4 v = xp[q];
-      const bool in = rb + 4 * q >= r0 && rb + 4 * q < r1;
-      X[m][q] = in ? v : make_uint4(0u, 0u, 0u, 0u);
-    }
   }
 }
 

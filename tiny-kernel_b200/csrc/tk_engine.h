@@ -155,7 +155,8 @@ struct EngineParams {
 };
 
 struct TmapPack {
-  CUtensorMap map[6];  // per matrix: group-box map, step-box map
+  CUtensorMap map[7];  // per matrix: group-box map, step-box map; [6]: one k-step of zero rows
 };
+constexpr int kZeroMap = 6;
 
 }  // namespace tk

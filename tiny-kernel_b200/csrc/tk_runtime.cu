@@ -120,6 +120,7 @@ struct tk_device {
   int decode_pdl = 1;      // TK_DECODE_PDL=0: cooperative launches without programmatic overlap
   ScratchBuf dec;          // decode kernel: launch epochs + tagged partial sums of its phases
   ScratchBuf io;           // TK_FFN_HOST_IO staging of x and out
+  ScratchBuf zero_rows;    // one k-step of zero packed rows (the decode kernel's partial items)
   size_t dec_xdev_bytes = 0;  // the decode scratch's tagged host-x area
   // While a synchronous host-buffer call is being recorded into a graph: the pinned word its
   // decode kernel reports a failure to, and whether a kernel took it (if none did, the graph
@@ -682,6 +683,10 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   p.x_dev = host_io ? reinterpret_cast<unsigned long long*>(base + off) : nullptr;
   TmapPack maps;
   std::memset(&maps, 0, sizeof(maps));
+  if ((stt = scratch_ensure(d, d->zero_rows, (size_t)kStepRows * kRowBytes)) != TK_OK) return stt;
+  if ((stt = weight_tmap(d, d->zero_rows.ptr, kRowBytes, kStepRows, (uint32_t)kStepRows,
+                         &maps.map[kZeroMap])) != TK_OK)
+    return stt;
   if ((stt = matrix_tmaps(d, a0->w_packed, ffn ? inter : n, k, gs, maps, 0)) != TK_OK) return stt;
   if (ffn) {
     if ((stt = matrix_tmaps(d, a1->w_packed, inter, k, gs, maps, 2)) != TK_OK) return stt;
@@ -1070,7 +1075,7 @@ void tk_device_destroy(tk_device* d) {
     cudaFreeHost(g.err_host);
   }
   for (auto* b : {&d->frag[0], &d->partials[0], &d->partials[1], &d->counters[0],
-                  &d->counters[1], &d->g_x16, &d->g_h16, &d->g_part, &d->dec, &d->io})
+                  &d->counters[1], &d->g_x16, &d->g_h16, &d->g_part, &d->dec, &d->io, &d->zero_rows})
     if (b->ptr) cudaFree(b->ptr);
   if (d->sync) cudaFree(d->sync);
   if (d->err) cudaFree(d->err);
