@@ -759,6 +759,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // the next launch of the stream may be scheduled now; this one reads nothing a preceding
     // kernel writes before that kernel has completed
     griddep_launch_dependents();
+    if (p.norm_w) bulk_prefetch_l2(p.norm_w, (uint32_t)p.ph[0].K * 4u);  // a read-only input
     griddep_wait();
     // the prologue copies go out first (x rows, then the norm weight, contiguous over the first
     // pro_stages stages' tiles): everything the consumers do first waits for them
