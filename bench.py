@@ -77,16 +77,16 @@ def arithmetic(path, m):
         return ("int4->f16 x f16 -> f32",
                 "INT4 weights dequantised to f16, f16 activations (and f16 h between the GEMMs), "
                 "tcgen05 MMA with f32 accumulation, f32 output")
-    if path in (1, 3):
-        if m <= 2:
-            return ("int4 x int16 -> int32 -> f32",
-                    "INT4 weights x activations quantised to int16 per group (one power-of-two "
-                    "scale), dp2a with exact int32 group sums, f32 scale and accumulation, f32 "
-                    "output")
+    if path == 3:
+        return ("int4 x int16 -> int32 -> f32",
+                "INT4 weights x activations quantised to int16 per group (one power-of-two "
+                "scale), dp2a with exact int32 group sums, f32 scale and accumulation, f32 "
+                "output" + (" (chunks of 4 rows)" if m > 4 else ""))
+    if path == 1:
         return ("int4 x int8 hi/lo -> int32 -> f32",
                 "INT4 weights x activations split into int8 hi + lo/256 parts per group, int8 "
                 "tensor-core MMA with exact int32 group sums, f32 scale and accumulation, f32 "
-                "output (chunks of 4 rows; a 1-2 row remainder takes the int16 dp2a path)")
+                "output (chunks of 4 rows)")
     return ("f32", "f32 dequantisation and accumulation (CUDA cores)")
 
 
@@ -699,7 +699,7 @@ def main():
                 "l2_guard": f"{copies} weight copies x {L} block(s) = "
                             f"{copies * L * shard_w_bytes / 1e6:.0f} MB per GPU (> 3x L2)",
                 "launch": "cuda-graph" if graph is not None else "stream",
-                "path": {3: "decode kernel (batch 1-2)", 2: "tcgen05 GEMM",
+                "path": {3: "decode kernel (1-4 rows per launch)", 2: "tcgen05 GEMM",
                          1: "streaming engine"}.get(path, "CUDA-core"),
                 "arithmetic": arith,
                 "bytes_per_step": step_bytes_total,

@@ -157,11 +157,12 @@ int tk_buffer_download_async(tk_device *dev, void *dst_host, const void *src_dev
  * x f32 [m][k], out f32 [m][n].  The reference computes row 0 only and requires
  * k <= 4096; this entry point computes all m rows and any k with k % group_size == 0,
  * group_size % 8 == 0, n even.  Shapes with n % 128 == 0, k % 128 == 0 and
- * group_size in {16, 32, 64, 128} (16-byte aligned pointers) run TMA-fed kernels: at 1-2 rows
+ * group_size in {16, 32, 64, 128} (16-byte aligned pointers) run TMA-fed kernels: at 1-4 rows
  * the decode kernel (one persistent launch, dp2a on the CUDA cores against activations
- * quantised to int16 per group), at 3-15 rows the streaming engine in chunks of 4 rows (int8
- * tensor-core MMAs, mma.sync, against int8 hi/lo activation parts), from 16 rows the tcgen05
- * dequant-to-f16 GEMM (tk_qmatmul_int4_path); other legal shapes run a plain CUDA-core kernel. */
+ * quantised to int16 per group), from 5 rows the tcgen05 dequant-to-f16 GEMM; shapes either
+ * does not take run the streaming engine in chunks of 4 rows (int8 tensor-core MMAs, mma.sync,
+ * against int8 hi/lo activation parts; tk_qmatmul_int4_path); other legal shapes run a plain
+ * CUDA-core kernel. */
 int tk_qmatmul_int4(tk_device *dev, const float *x, const uint8_t *w_packed,
                     const uint16_t *scales, const uint8_t *zeros, float *out, uint32_t m,
                     uint32_t k, uint32_t n, uint32_t group_size);
@@ -342,7 +343,7 @@ int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *sca
  * waiting for stages in phase A and in phase B, the CTA's phase-A and phase-B item counts, the
  * ns at which the last phase-B stage was in hand, and (x in host memory) the ns at which the
  * CTA held the whole of x.
- * A launch of the batch >= 16 GEMM overwrites the buffer with SM-clock cycle counts instead,
+ * A launch of the batch >= 5 GEMM overwrites the buffer with SM-clock cycle counts instead,
  * for CTAs x + X * (y + Y * z) below sm_count: TMA producer waiting for free ring stages,
  * producer total, MMA issuer waiting for dequantised tiles, MMA waiting for TMA stages, MMA
  * total, first dequantiser warp waiting for TMA stages, waiting for free A stages, its total. */
@@ -362,7 +363,7 @@ int tk_device_trace_read(tk_device *dev, uint64_t *out, size_t max_values, size_
  *  - Synchronous: it waits for its work and reads the error word back before it returns, so
  *    it cannot be recorded into a CUDA graph.
  *  - Results are within the path's tolerance of tk_qmatmul_int4's, not always identical: every
- *    row count runs the streaming engine in chunks of 4 rows (m >= 16 does not take the
+ *    row count runs the streaming engine in chunks of 4 rows (m >= 5 does not take the
  *    tensor-core GEMM), and shapes the engine does not take run the CUDA-core kernel.
  *  - Its bounded device-side waits give up after a fixed 2 s (TK_WAIT_TIMEOUT_MS is not read).
  * It allocates nothing: the engine's scratch is one static device array of
@@ -379,10 +380,9 @@ int tk_qmatmul_int4_noalloc(const float *x, const uint8_t *w_packed, const uint1
                             uint32_t n, uint32_t group_size, void *stream);
 
 /* Which path tk_qmatmul_int4 would take for a shape with 16-byte aligned buffers and the
- * default device settings (148 SMs, 227 KB of shared memory per block): 3 = the batch 1-2 decode
- * kernel (m <= 2 whose records and ring fit shared memory), 2 = tcgen05 GEMM (m >= 16),
- * 1 = streaming engine (other m < 16, or a shape the GEMM does not tile), 0 = CUDA-core fallback,
- * <0 = invalid shape.
+ * default device settings (148 SMs, 227 KB of shared memory per block): 3 = the decode kernel
+ * (m <= 4 whose records and ring fit shared memory), 2 = tcgen05 GEMM (m >= 5), 1 = streaming
+ * engine (a shape neither of those takes), 0 = CUDA-core fallback, <0 = invalid shape.
  * No counterpart in the reference (one shader serves every shape there). */
 int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t group_size);
 

@@ -29,6 +29,24 @@ def tkdev():
 
 
 @pytest.fixture(scope="session")
+def tkdev_engine():
+    """A second device on GPU 0 whose 1-4-row calls take the streaming engine (TK_DECODE=0, read
+    when the device is created) instead of the decode kernel."""
+    import tiny_kernel as tk
+    old = os.environ.get("TK_DECODE")
+    os.environ["TK_DECODE"] = "0"
+    try:
+        dev = tk.init(0)
+    finally:
+        if old is None:
+            del os.environ["TK_DECODE"]
+        else:
+            os.environ["TK_DECODE"] = old
+    yield dev
+    dev.deinit()
+
+
+@pytest.fixture(scope="session")
 def torch_cuda():
     import torch
     assert torch.cuda.is_available(), "GPU test needs CUDA"

@@ -39,17 +39,18 @@ def test_calls_without_gpu():
     L = _lib.lib()
     assert L.tk_abi_version() == 1
     assert L.tk_status_string(_lib.TK_ERR_TIMEOUT) == b"device-side wait timed out"
-    assert L.tk_qmatmul_int4_path(1, 4096, 14336, 64) == 3   # the batch 1-2 decode kernel
-    assert L.tk_qmatmul_int4_path(3, 4096, 14336, 64) == 1   # the streaming engine
+    assert L.tk_qmatmul_int4_path(1, 4096, 14336, 64) == 3   # the decode kernel (1-4 rows)
+    assert L.tk_qmatmul_int4_path(3, 4096, 14336, 64) == 3   # its four-row instantiation
     assert L.tk_qmatmul_int4_path(1, 4800, 14336, 48) == 0
     assert L.tk_qmatmul_int4_path(1, 4096, 14335, 64) == -1
     assert L.tk_qmatmul_int4_path(1, 100, 64, 8) == -1
     assert L.tk_qmatmul_int4_path(16, 4096, 14336, 64) == 2
-    assert L.tk_qmatmul_int4_path(16, 4096, 14464, 64) == 1   # 14464 % 256 != 0
-    assert L.tk_qmatmul_int4_path(15, 4096, 14336, 64) == 1
+    assert L.tk_qmatmul_int4_path(16, 4096, 14464, 64) == 3   # 14464 % 256 != 0: 4-row decodes
+    assert L.tk_qmatmul_int4_path(15, 4096, 14336, 64) == 2   # the GEMM from 5 rows
+    assert L.tk_qmatmul_int4_path(5, 4096, 14336, 64) == 2
     assert L.tk_int4_ffn_path(1, 4096, 14336, 64) == 3
     assert L.tk_int4_ffn_path(2, 8192, 28672, 64) == 3
-    assert L.tk_int4_ffn_path(4, 4096, 14336, 64) == 1
+    assert L.tk_int4_ffn_path(4, 4096, 14336, 64) == 3
     assert L.tk_int4_ffn_path(16, 4096, 14336, 64) == 2
     assert L.tk_int4_ffn_path(16, 4800, 9600, 48) == 0
 

@@ -1,13 +1,13 @@
 """Within-group dynamic range: qmatmul_int4 (src/kernels/shaders.zig:442-501) on activations whose
-groups mix values near 1e3 with values near 1e-3, on every path (decode kernel at 1-2 rows,
-streaming engine at 4, tcgen05 GEMM at 16).
+groups mix values near 1e3 with values near 1e-3, on every path (decode kernel at 1, 2 and 4 rows,
+the streaming engine at 4 rows (TK_DECODE=0), tcgen05 GEMM at 16).
 
 The reference computes in f32 (shaders.zig:481-497), so each of its output columns carries f32
 relative precision whatever the spread inside a group.  The paths here quantise activations per
 weight group:
-  1-2 rows  int16 with one power-of-two scale per group (max |x| * 2^e in [2^14, 2^15)):
+  decode    int16 with one power-of-two scale per group (max |x| * 2^e in [2^14, 2^15)):
             |x - x^| <= 2^-14 max|x_g|
-  3-4 rows  int8 hi + lo/256 parts at a scale with max |x| * 2^e in [32, 64):
+  engine    int8 hi + lo/256 parts at a scale with max |x| * 2^e in [32, 64):
             |x - x^| <= 2^-13 max|x_g|
   16+ rows  f16 activations and f16 dequantised weights, f32 accumulation: per product
             <= 2^-10 relative
@@ -69,12 +69,15 @@ def _case(seed, m):
     return x, M, kind
 
 
-@pytest.mark.parametrize("m", [1, 2, 4, 16])
-def test_within_group_dynamic_range(torch_cuda, tkdev, m):
+@pytest.mark.parametrize("m,engine", [(1, False), (2, False), (4, False), (4, True), (16, False)])
+def test_within_group_dynamic_range(torch_cuda, tkdev, tkdev_engine, m, engine):
     torch = torch_cuda
     x, M, kind = _case(41 + m, m)
-    path = ops.path(m, K, N, GS)
-    assert path == {1: 3, 2: 3, 4: 1, 16: 2}[m], path
+    if engine:
+        tkdev, path = tkdev_engine, 1
+    else:
+        path = ops.path(m, K, N, GS)
+        assert path == {1: 3, 2: 3, 4: 3, 16: 2}[m], path
     w, s, z = mat_dev(torch, M)
     out = torch.empty((m, N), dtype=torch.float32, device="cuda")
     ops.qmatmul_int4(tkdev, dev(torch, x), w, s, z, out, m, K, N, GS)

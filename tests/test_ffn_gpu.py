@@ -17,6 +17,7 @@ TOL = 1e-3
 # The engine's activation quantisation (x and h): int16 per group at 1-2 rows (2^-15 of each
 # group's max |x|), int8 hi + lo/256 parts at 3-4 rows (2^-13).
 PRECISION = 7e-4
+GEMM_PRECISION = 8e-4  # the tcgen05 GEMM path (5+ rows)
 EPS = 1e-5
 
 
@@ -38,7 +39,7 @@ def run_ffn(torch, tkdev, x, W, residual=False, inplace=False, want_h=True):
     (2, 512, 1024, 32),
     (3, 384, 256, 128),
     (4, 128, 128, 16),
-    (6, 256, 512, 64),        # > 4 rows: chunks of 4
+    (6, 256, 512, 64),        # > 4 rows: the tcgen05 GEMM
 ])
 def test_ffn_vs_oracle(torch_cuda, tkdev, m, hidden, inter, gs):
     W = data.make_ffn(21, hidden, inter, gs)
@@ -47,7 +48,8 @@ def test_ffn_vs_oracle(torch_cuda, tkdev, m, hidden, inter, gs):
     ref, ref_h = oracle.ffn_f64(x, W.norm_w, W.gate, W.up, W.down, EPS, return_h=True)
     eh, ey = oracle.normwise_err(h, ref_h), oracle.normwise_err(y, ref)
     assert eh <= TOL and ey <= TOL, (eh, ey)
-    assert eh <= PRECISION and ey <= PRECISION, (eh, ey)
+    bar = GEMM_PRECISION if ops.ffn_path(m, hidden, inter, gs) == 2 else PRECISION
+    assert eh <= bar and ey <= bar, (eh, ey)
 
 
 def test_ffn_residual_and_inplace(torch_cuda, tkdev):
@@ -91,7 +93,7 @@ def test_ffn_deterministic(torch_cuda, tkdev):
     (2, 4096, 14336, 64, True),    # residual from the kernel's own copy of x
     (1, 512, 1024, 64, True),
     (2, 256, 512, 32, True),
-    (3, 384, 256, 128, False),     # the engine: staged through device scratch
+    (3, 384, 256, 128, False),     # the decode kernel at three rows (four-row instantiation)
     (16, 512, 1024, 64, True),     # the tcgen05 GEMM: staged
 ])
 def test_ffn_host_io_matches_device_buffers(torch_cuda, tkdev, m, hidden, inter, gs, residual):

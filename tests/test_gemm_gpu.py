@@ -1,6 +1,6 @@
-"""GPU parity of the batch >= 16 path: the tcgen05 INT4 GEMM (qmatmul_int4 and the FFN).
+"""GPU parity of the batch >= 5 path: the tcgen05 INT4 GEMM (qmatmul_int4 and the FFN).
 
-From 16 rows on, qmatmul_int4 (src/kernels/shaders.zig:442-501) and the INT4 FFN
+From 5 rows on, qmatmul_int4 (src/kernels/shaders.zig:442-501) and the INT4 FFN
 (src/bench.zig:266-341 + the down projection and residual of src/model/llama.zig:220-231)
 run as GEMMs on the 5th-generation tensor cores: weights dequantised to f16 in shared memory,
 activations (and the FFN's h) in f16, f32 accumulation.  Bar: the path's normwise max error

@@ -19,6 +19,7 @@ TOL = 1e-3          # normwise max relative error vs f64 (the path's contract)
 # scale, dp2a, exact int32 sums) at 1-2 rows, about 2e-5; int8 hi + lo/256 parts (int8 tensor-core
 # MMAs, exact int32 sums) at 3-4 rows, about 1e-4.
 PRECISION = 5e-4
+GEMM_PRECISION = 8e-4  # the tcgen05 GEMM path (5+ rows): f16 activations and dequantised weights
 
 
 def f32_reference_order(x, M):
@@ -75,14 +76,15 @@ ENGINE_CASES = [
 
 @pytest.mark.parametrize("m,K,N,gs", ENGINE_CASES)
 def test_qmatmul_engine_vs_oracle(torch_cuda, tkdev, m, K, N, gs):
-    assert ops.path(m, K, N, gs) in (1, 3)
+    path = ops.path(m, K, N, gs)
+    assert path in (1, 3) if m <= 4 else path in (1, 2), path
     M = data.make_int4_matrix(1000 + m, f"q{K}x{N}", K, N, gs)
     x = data.make_x(7, f"x{m}x{K}", m, K)
     y = run_qmatmul(torch_cuda, tkdev, x, M)
     ref = oracle.qmatmul_f64(x, M.w, M.s, M.z, K, N, gs)
     err = oracle.normwise_err(y, ref)
     assert err <= TOL, err
-    assert err <= PRECISION, err
+    assert err <= (GEMM_PRECISION if path == 2 else PRECISION), err
 
 
 @pytest.mark.parametrize("m,K,N,gs", [(1, 40, 10, 8), (2, 192, 94, 24), (1, 96, 256, 48),

@@ -161,7 +161,7 @@ def test_tp_ffn_native_group_vs_oracle(torch_cuda, tmp_path, world):
     cases = [(1, 4096, 14336, 64, False),   # config 1: the exchange fused into the decode kernel
              (1, 1024, 2048, 64, True),     # residual added once
              (2, 1024, 2048, 64, True),     # two rows, fused
-             (4, 1024, 2048, 64, False),    # the engine + the peer-memory all-reduce
+             (4, 1024, 2048, 64, False),    # four rows: fused as well
              (16, 1024, 2048, 64, False)]   # batch 16: the tcgen05 GEMM on each shard
     out = tmp_path / "errs_native.npy"
     mp.start_processes(_rank_native, args=(world, unique_id(), cases, str(out)), nprocs=world,
@@ -171,8 +171,8 @@ def test_tp_ffn_native_group_vs_oracle(torch_cuda, tmp_path, world):
     print(f"TP{world}: exchanges {exch.tolist()}, errors {errs.tolist()}")
     assert len(errs) == 3 * len(cases)
     assert np.all(errs <= TOL), errs
-    if exch[3] == 1:  # the group maps its peers: 1-2 rows take the fused exchange
-        assert exch[0] == exch[1] == exch[2] == 2, exch
+    if exch[4] == 1:  # the group maps its peers: 1-4 rows take the fused exchange
+        assert exch[0] == exch[1] == exch[2] == exch[3] == 2, exch
     # every rank holds the same sum, bit for bit
     ref = np.load(f"{out}.out0.npy")
     for r in range(1, world):

@@ -326,9 +326,10 @@ __device__ bool consume_phase(const DecodeParams& p, const DecPhase& P, int n, i
                               unsigned long long* wait_ns, unsigned long long* first_ns,
                               unsigned long long* last_ns) {
   constexpr int R = GS / 2;  // packed rows per group
-  // rows per chunk: 16 at one row (the chunk pair fully unrolled), 8 at two (a rolled loop over
-  // chunk pairs, which keeps the two rows' accumulators and chunks in registers)
-  constexpr int HB = MT == 1 ? (R <= 32 ? R / 2 : 16) : (R <= 16 ? R / 2 : 8);
+  // rows per chunk: 16 at one row (the chunk pair fully unrolled), 8 at two, 4 at four (a rolled
+  // loop over chunk pairs, which keeps the rows' accumulators and chunks in registers)
+  constexpr int HB = MT == 1 ? (R <= 32 ? R / 2 : 16)
+                             : MT == 2 ? (R <= 16 ? R / 2 : 8) : (R <= 8 ? R / 2 : 4);
   constexpr int NCH = R / HB;  // chunks per item (2 to 8)
   constexpr int kPairUnroll = MT == 1 ? NCH / 2 : 1;
   constexpr int tok_stride = dp_tok_stride(GS);
@@ -555,7 +556,7 @@ template <int MT, int GS>
 __device__ bool build_h_record(const DecodeParams& p, int j, int grp, bool write_h, uint8_t* rec,
                                unsigned tag, int lane, volatile int* abort, int part = 0,
                                int nparts = 1, float* xbuf = nullptr, int bar = 0) {
-  constexpr int kSB = 8 / MT;              // segments in flight per batch
+  constexpr int kSB = MT >= 4 ? 1 : 8 / MT;  // segments in flight per batch
   constexpr bool kSplit = GS / 4 <= 16;  // a half warp per matrix
   constexpr int kMats = kSplit ? 1 : 2;  // matrices summed per lane
   const DecPhase& A = p.ph[j];
@@ -1098,8 +1099,8 @@ cudaError_t decode_occupancy(int mt, int gs, size_t smem, int* blocks) {
     size_t smem;
     int blocks;
   };
-  static Last last[kMaxDevices][2][4] = {};
-  const int mi = mt == 1 ? 0 : mt == 2 ? 1 : -1;
+  static Last last[kMaxDevices][3][4] = {};
+  const int mi = mt == 1 ? 0 : mt == 2 ? 1 : mt == 4 ? 2 : -1;
   const int gi = gs == 16 ? 0 : gs == 32 ? 1 : gs == 64 ? 2 : gs == 128 ? 3 : -1;
   if (mi < 0 || gi < 0) return cudaErrorInvalidValue;
   int dev = 0;
@@ -1112,7 +1113,8 @@ cudaError_t decode_occupancy(int mt, int gs, size_t smem, int* blocks) {
     *blocks = L->blocks;
     return cudaSuccess;
   }
-  e = mt == 1 ? dec_occupancy_gs<1>(gs, smem, blocks) : dec_occupancy_gs<2>(gs, smem, blocks);
+  e = mt == 1 ? dec_occupancy_gs<1>(gs, smem, blocks)
+      : mt == 2 ? dec_occupancy_gs<2>(gs, smem, blocks) : dec_occupancy_gs<4>(gs, smem, blocks);
   if (L) *L = (e == cudaSuccess) ? Last{smem, *blocks} : Last{0, 0};
   return e;
 }
@@ -1122,6 +1124,7 @@ cudaError_t decode_launch(int mt, int gs, const TmapPack& maps, const DecodePara
   switch (mt) {
     case 1: return dec_launch_gs<1>(gs, maps, p, grid, smem, stream);
     case 2: return dec_launch_gs<2>(gs, maps, p, grid, smem, stream);
+    case 4: return dec_launch_gs<4>(gs, maps, p, grid, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }

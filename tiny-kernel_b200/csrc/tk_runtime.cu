@@ -590,7 +590,7 @@ bool dec_plan(const DecodeParams& p, int m, int mt, int gs, bool norm, int smem_
   DecPlan pl;
   pl.tile_stage_bytes = ((gs / 16) * kStepRows * kRowBytes + 127) & ~127;
   pl.aux_stage_bytes = kSlices * (kScaleBytes + kZeroBytes);
-  pl.frag_bytes = record_bytes(gs, mt);
+  pl.frag_bytes = mt * dp_tok_stride(gs);  // the int16 records of every row (dp2a at any mt)
   for (int q = p.na; q < p.nph; ++q) pl.recb_items = std::max(pl.recb_items, dec_max_items(p.ph[q]));
   if (pl.recb_items > kDecMaxItemsB) return false;
   const DecPhase& A = p.ph[0];
@@ -627,23 +627,27 @@ struct TpFuse {
   unsigned* epoch;
 };
 
+// Rows one decode launch takes, and the instantiation (rows in registers) for m of them.
+constexpr int kDecMaxRows = 4;
+int dec_mt(int m) { return m <= 2 ? m : 4; }
+
 bool decode_shape(int m, int k, int n, int inter, int gs, int grid, bool ffn) {
-  if (m < 1 || m > 2 || !(gs == 16 || gs == 32 || gs == 64 || gs == 128)) return false;
+  if (m < 1 || m > kDecMaxRows || !(gs == 16 || gs == 32 || gs == 64 || gs == 128)) return false;
   DecodeParams p;
   std::memset(&p, 0, sizeof(p));
   dec_phases(p, ffn, k, n, inter, gs, grid, 1);
   DecPlan pl;
-  return dec_plan(p, m, m, gs, ffn, kDecSmemLimit - kStaticSmemReserve, &pl);
+  return dec_plan(p, m, dec_mt(m), gs, ffn, kDecSmemLimit - kStaticSmemReserve, &pl);
 }
 
-// One decode launch for m <= 2 rows: qmatmul_int4 (gate == nullptr) or the FFN.  Returns
+// One decode launch for m <= 4 rows: qmatmul_int4 (gate == nullptr) or the FFN.  Returns
 // TK_ERR_UNSUPPORTED, before enqueuing anything, when the shape does not fit the kernel.
 int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
                const tk_int4_matrix* a0, const tk_int4_matrix* a1, const tk_int4_matrix* down,
                float* out, float* h_out, int m, int k, int n, int inter, int gs, bool residual,
                cudaStream_t st, bool host_io = false, const TpFuse* tpf = nullptr) {
   const bool ffn = down != nullptr;
-  const int mt = m;  // instantiations for 1 and 2 rows
+  const int mt = dec_mt(m);  // instantiations for 1, 2 and 4 rows
   const int grid = engine_grid(d);
   DecodeParams p;
   std::memset(&p, 0, sizeof(p));
@@ -755,7 +759,9 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
 
 // ---- batch >= 16: the tcgen05 GEMM path (tk_gemm.cu) ----------------------------------------
 
-constexpr int kGemmMinRows = 16;
+// From 5 rows the tcgen05 GEMM: a decode launch takes at most 4 rows, and two of them (batch
+// 5-8: 85-122 us per 8B FFN step) cost more than one GEMM over a 16-token tile (about 71 us).
+constexpr int kGemmMinRows = 5;
 
 int gemm_nt(int m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : m <= 128 ? 128 : 256; }
 
@@ -1310,7 +1316,9 @@ int tk_qmatmul_int4_path(uint32_t m, uint32_t k, uint32_t n, uint32_t gs) {
   if (m == 0 || k == 0 || n == 0 || gs == 0 || gs % 8 || k % gs || n % 2) return -1;
   if (!engine_shape(k, n, gs)) return 0;
   if (m >= kGemmMinRows && gemm_shape(k, n, gs, false)) return 2;
-  return decode_shape((int)m, (int)k, (int)n, 0, (int)gs, kDefaultGrid, false) ? 3 : 1;
+  // chunks of up to kDecMaxRows rows, each a decode launch when its instantiation fits
+  const int mc = std::min<int>((int)m, kDecMaxRows);
+  return decode_shape(mc, (int)k, (int)n, 0, (int)gs, kDefaultGrid, false) ? 3 : 1;
 }
 
 int tk_int4_ffn_path(uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs) {
@@ -1320,7 +1328,8 @@ int tk_int4_ffn_path(uint32_t m, uint32_t hidden, uint32_t inter, uint32_t gs) {
   if (!engine_shape(hidden, inter, gs) || !engine_shape(inter, hidden, gs)) return 0;
   if (m >= kGemmMinRows && gemm_shape(hidden, inter, gs, true) && gemm_shape(inter, hidden, gs, false))
     return 2;
-  return decode_shape((int)m, (int)hidden, 0, (int)inter, (int)gs, kDefaultGrid, true) ? 3 : 1;
+  const int mc = std::min<int>((int)m, kDecMaxRows);
+  return decode_shape(mc, (int)hidden, 0, (int)inter, (int)gs, kDefaultGrid, true) ? 3 : 1;
 }
 
 int tk_qmatmul_int4_async(tk_device* d, const float* x, const uint8_t* w, const uint16_t* s,
@@ -1342,7 +1351,7 @@ int tk_qmatmul_int4_async(tk_device* d, const float* x, const uint8_t* w, const 
     return qmatmul_gemm(d, x, w, s, z, out, (int)m, (int)k, (int)n, (int)gs, cs);
   for (uint32_t r = 0; r < m; r += 4) {
     const uint32_t mm = std::min<uint32_t>(4, m - r);
-    if (mm <= 2 && d->decode_enabled) {
+    if ((int)mm <= kDecMaxRows && d->decode_enabled) {
       const tk_int4_matrix a{w, s, z};
       st = decode_run(d, x + (size_t)r * k, nullptr, 0.f, &a, nullptr, nullptr, out + (size_t)r * n,
                       nullptr, (int)mm, (int)k, (int)n, 0, (int)gs, false, cs);
@@ -1452,7 +1461,7 @@ int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const t
     const bool aligned = aligned16(x) && aligned16(norm_w) && aligned16(out) &&
                          (!h_out || aligned16(h_out)) && matrix_aligned(gate) &&
                          matrix_aligned(up) && matrix_aligned(down);
-    if (m <= 2 && d->decode_enabled && aligned && engine_shape(hidden, inter, gs) &&
+    if ((int)m <= kDecMaxRows && d->decode_enabled && aligned && engine_shape(hidden, inter, gs) &&
         engine_shape(inter, hidden, gs)) {
       st = decode_run(d, x, norm_w, eps, gate, up, down, out, h_out, (int)m, (int)hidden, 0,
                       (int)inter, (int)gs, residual, cs, true);
@@ -1480,7 +1489,7 @@ int tk_int4_ffn_async(tk_device* d, const float* x, const float* norm_w, const t
   if (fast) {
     for (uint32_t r = 0; r < m; r += 4) {
       const uint32_t mm = std::min<uint32_t>(4, m - r);
-      if (mm <= 2 && d->decode_enabled) {
+      if ((int)mm <= kDecMaxRows && d->decode_enabled) {
         st = decode_run(d, x + (size_t)r * hidden, norm_w, eps, gate, up, down,
                         out + (size_t)r * hidden, h_out ? h_out + (size_t)r * inter : nullptr,
                         (int)mm, (int)hidden, 0, (int)inter, (int)gs, residual, cs);
@@ -2048,7 +2057,8 @@ int tk_int4_ffn_tp_exchange(tk_tp* tp, uint32_t m, uint32_t hidden, uint32_t int
   if (!tp) return fail(TK_ERR_ARG, "tp is NULL");
   if (tp->nranks == 1) return 0;
   if (!tp->p2p) return 0;
-  if (tp->fused && m <= 2 && tp->dev->decode_enabled && (size_t)m * hidden <= kTpFuseWords &&
+  if (tp->fused && (int)m <= kDecMaxRows && tp->dev->decode_enabled &&
+      (size_t)m * hidden <= kTpFuseWords &&
       tk_int4_ffn_path(m, hidden, inter, gs) == 3)
     return 2;
   return (size_t)m * hidden <= tk::kP2PMaxFloats ? 1 : 0;
