@@ -9,17 +9,18 @@ weight group:
             |x - x^| <= 2^-14 max|x_g|
   engine    int8 hi + lo/256 parts at a scale with max |x| * 2^e in [32, 64):
             |x - x^| <= 2^-13 max|x_g|
-  16+ rows  f16 activations and f16 dequantised weights, f32 accumulation: per product
+  GEMM      f16 activations and f16 dequantised weights, f32 accumulation: per product
             <= 2^-10 relative
-followed by exact int32 sums (1-4 rows) and f32 scaling.  So an output column carried only by a
-group's small values is exact to the group's fixed point at 1-4 rows -- its error is bounded by
-the group maximum, not by the column's own size -- and to f16 precision at 16+ rows.  The test
+followed by exact int32 sums (decode, engine) and f32 scaling.  So an output column carried only
+by a group's small values is exact to the group's fixed point on the decode kernel and the engine
+-- its error is bounded by the group maximum, not by the column's own size -- and to f16
+precision on the GEMM.  The test
 builds exactly that case and asserts, column by column:
   * every path: the componentwise bound of its arithmetic above;
   * every path: columns carried by the large values within 1e-3 relative;
   * the GEMM path: columns carried only by the small values within 2e-3 relative;
   * every path: the normwise contract (1e-3).
-The relative error of the small-value columns at 1-4 rows is printed (it is the loss the
+The relative error of the small-value columns of the fixed-point paths is printed (it is the loss the
 fixed-point groups make on this adversarial case).
 """
 import numpy as np
