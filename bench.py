@@ -571,12 +571,20 @@ def main():
     # (TK_FFN_HOST_IO: the kernel reads x and writes y over the host link).  Otherwise (matvec,
     # stacks, tensor parallel): queue the upload, the step and the download, then wait once.
     host_io = (not matvec) and L == 1 and pg is None and group is None
+    if host_io:
+        # the C-ABI call a host (the reference's Zig, any FFI) makes: tk_int4_ffn with its
+        # arguments built once per weight copy, as a caller holding its buffers would
+        from tiny_kernel._lib import TK_FFN_HOST_IO
+        hio_args = []
+        for c in range(copies):
+            nw, g, u, d = mats[c][0]
+            hio_args.append((dev.handle, C.c_void_p(xb_host.ptr), C.c_void_p(nw.data_ptr()),
+                             C.byref(g), C.byref(u), C.byref(d), C.c_void_p(ob_host.ptr), None,
+                             m, hidden, inter, GS, C.c_float(EPS), TK_FFN_HOST_IO))
 
     def e2e_step(i):
         if host_io:
-            nw, g, u, d = mats[i % copies][0]
-            ops.int4_ffn(dev, xb_host.ptr, nw, g, u, d, ob_host.ptr, m, hidden, inter, GS, eps=EPS,
-                         host_io=True, sync=True)
+            check(Lb.tk_int4_ffn(*hio_args[i % copies]))
             return
         check(Lb.tk_buffer_upload_async(dev.handle, xd.data_ptr(), xb_host.ptr, xb_host.nbytes,
                                         None))
