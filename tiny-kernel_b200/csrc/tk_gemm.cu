@@ -85,9 +85,12 @@ __device__ __forceinline__ uint32_t hsubmul(uint32_t q, uint32_t z, uint32_t s) 
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Bounded wait that also adds the cycles it took to *acc.
+// Bounded wait that also adds the cycles it took to *acc when `timed` (tracing: the clock is
+// read only then).
 __device__ __forceinline__ bool gemm_wait_timed(uint64_t* bar, uint32_t parity, unsigned* err,
-                                                unsigned long long timeout_ns, long long* acc) {
+                                                unsigned long long timeout_ns, long long* acc,
+                                                bool timed) {
+  if (!timed) return gemm_wait(bar, parity, err, timeout_ns);
   const long long c0 = clock64();
   const bool ok = gemm_wait(bar, parity, err, timeout_ns);
   *acc += clock64() - c0;
@@ -150,8 +153,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem = tmem_slot;
   const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   unsigned long long* trace = (p.trace && cta < p.trace_ctas) ? p.trace + (size_t)cta * kTraceEvents : nullptr;
-  const long long t_start = clock64();
-  long long tw0 = 0, tw1 = 0;  // cycles in this warp's two kinds of waits
+  const bool tr = trace != nullptr;
+  const long long t_start = tr ? clock64() : 0;
+  long long tw0 = 0, tw1 = 0;  // cycles in this warp's two kinds of waits (traced)
 
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------------
@@ -165,7 +169,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (; i < nsteps; ++i, r.next(SR)) {
       bool ok = true;
       if (i >= SR && lane == 0)
-        ok = gemm_wait_timed(&empty_r[r.s], r.ph ^ 1u, p.err, p.timeout_ns, &tw0);
+        ok = gemm_wait_timed(&empty_r[r.s], r.ph ^ 1u, p.err, p.timeout_ns, &tw0, tr);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       uint8_t* st = rring + (size_t)r.s * p.raw_stage_bytes;
       const int k0 = (ks0 + i) * kGemmKStep;
@@ -204,8 +208,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < nsteps; ++i, ra.next(SA), rr.next(SR)) {
       bool ok = true;
       if (lane == 0)
-        ok = gemm_wait_timed(&full_a[ra.s], ra.ph, p.err, p.timeout_ns, &tw0) &&
-             gemm_wait_timed(&full_r[rr.s], rr.ph, p.err, p.timeout_ns, &tw1);
+        ok = gemm_wait_timed(&full_a[ra.s], ra.ph, p.err, p.timeout_ns, &tw0, tr) &&
+             gemm_wait_timed(&full_r[rr.s], rr.ph, p.err, p.timeout_ns, &tw1, tr);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       tcgen05_fence_after();
       const uint32_t xa = smem_addr(rring + (size_t)rr.s * p.raw_stage_bytes + L::X);
@@ -248,8 +252,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t rring_s = smem_addr(rring), aring_s = smem_addr(aring);
     RingPos rr, ra;
     for (int i = 0; i < nsteps; ++i, rr.next(SR), ra.next(SA)) {
-      if (!gemm_wait_timed(&full_r[rr.s], rr.ph, p.err, p.timeout_ns, &tw0)) break;
-      if (i >= SA && !gemm_wait_timed(&empty_a[ra.s], ra.ph ^ 1u, p.err, p.timeout_ns, &tw1))
+      if (!gemm_wait_timed(&full_r[rr.s], rr.ph, p.err, p.timeout_ns, &tw0, tr)) break;
+      if (i >= SA && !gemm_wait_timed(&empty_a[ra.s], ra.ph ^ 1u, p.err, p.timeout_ns, &tw1, tr))
         break;
       const uint32_t st = rring_s + (uint32_t)rr.s * (uint32_t)p.raw_stage_bytes;
       // scales of columns 4l .. 4l+3 as (4l, 4l+2) and (4l+1, 4l+3) pairs; zero points the
@@ -270,11 +274,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t e1 = hsubmul((w8 & 0x000F000Fu) | 0x64006400u, zl13, s13);
         const uint32_t o0 = hsubmul((w & 0x00F000F0u) | 0x54005400u, zh02, s02);
         const uint32_t o1 = hsubmul((w8 & 0x00F000F0u) | 0x54005400u, zh13, s13);
-        // k rows 2r and 2r+1 of the group: row j at j * 128, chunk ^ j
-        const uint32_t ce = ((chunk ^ (uint32_t)(2 * r)) - chunk) << 4;
-        const uint32_t co = ((chunk ^ (uint32_t)(2 * r + 1)) - chunk) << 4;
-        st_shared_v2(ab + (uint32_t)(2 * r) * 128u + ce, e0, e1);
-        st_shared_v2(ab + (uint32_t)(2 * r + 1) * 128u + co, o0, o1);
+        // k rows 2r and 2r+1 of the group at A rows gemm_kperm(2r), gemm_kperm(2r+1) (the
+        // activations' k order): row j at j * 128, chunk ^ j
+        constexpr int je[4] = {gemm_kperm(0), gemm_kperm(2), gemm_kperm(4), gemm_kperm(6)};
+        constexpr int jo[4] = {gemm_kperm(1), gemm_kperm(3), gemm_kperm(5), gemm_kperm(7)};
+        const uint32_t ce = ((chunk ^ (uint32_t)je[r]) - chunk) << 4;
+        const uint32_t co = ((chunk ^ (uint32_t)jo[r]) - chunk) << 4;
+        st_shared_v2(ab + (uint32_t)je[r] * 128u + ce, e0, e1);
+        st_shared_v2(ab + (uint32_t)jo[r] * 128u + co, o0, o1);
       }
       fence_proxy_async_smem();  // the A tiles are read by tcgen05.mma (async proxy)
       __syncwarp();
@@ -311,7 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (p.epi == kGemmSiluMul) {
             const float h = a0 / (1.0f + expf(-a0)) * a1;
             const size_t o = (size_t)tok * p.N + colt[0] + cl;
-            p.h16[o] = __float2half_rn(h);
+            p.h16[(size_t)tok * p.N + gemm_kperm(colt[0] + cl)] = __float2half_rn(h);
             if (p.h32) p.h32[o] = h;
           } else if (p.epi == kGemmStore) {
             const size_t o0 = (size_t)tok * p.N + colt[0] + cl, o1 = (size_t)tok * p.N + colt[1] + cl;
@@ -347,12 +354,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //               rows of the step), (t, ch) from (w-2)/4.  Lane l (j = l/4, u = l%4) loads the
 //               32-bit words of packed rows 32ch + 8c + 2u + e (c in 0..3, e in {0,1}) at
 //               columns 32q + 4j .. 32q + 4j + 3 (rows 2 apart inside a quad: with the swizzle
-//               the warp's loads hit 32 distinct banks) and stores them with tcgen05.st.16x256b,
-//               whose thread layout holds exactly those cells: column (packed row)
-//               32ch + 8c + 2u + e of lanes j + 8i' + 16h for byte i = 2h + i'.  So
+//               the warp's loads hit 32 distinct banks) and stores their cells with
+//               tcgen05.st.16x256b, whose thread layout holds exactly those: column
+//               32ch + 8c + 2u + e' of lanes j + 8i' + 16h for byte i = 2h + i'.  So
 //               tensor-memory lane 32q + l holds output column 32q + 4(l%8) + l/8.
-//   A cell is one packed byte: f16 pair (k even, k odd) = (1024 + lo, 64 + hi) by the exponent
-//   constants 0x6400 / 0x5400, minus (1024 + z, 64 + z) (exact), times (s, s) (one rounding).
+//   The two words of a lane at packed rows 2p and 2p + 1 (e = 0, 1) give the cells of tensor-memory
+//   columns 2p (e' = 0) and 2p + 1 (e' = 1): one byte permute puts byte i of both words in bytes
+//   0 and 2, and one mask + or makes the f16 pair (1024 + lo, 1024 + lo') -- k = 4p, 4p + 2 -- or
+//   (64 + hi, 64 + hi') -- k = 4p + 1, 4p + 3 -- by the exponent constants 0x6400 / 0x5400; minus
+//   (1024 + z, 1024 + z) or (64 + z, 64 + z) (exact), times (s, s) (one rounding).  The MMA's k
+//   order is thus 4p, 4p + 2, 4p + 1, 4p + 3: the activations' order (gemm_kperm).
 // A step's tensor-memory stores complete (tcgen05.wait::st) after the next step's cells are
 // computed, so the store latency overlaps that work.
 __device__ __forceinline__ int tm_lane_column(int l) { return 4 * (l & 7) + (l >> 3); }
@@ -373,6 +384,9 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
   constexpr uint32_t kAStageCols = kGemmTiles * kGemmTmKStep / 2;  // 128
   constexpr uint32_t kTmemCols = 512;
   static_assert(kAcol0 + SA * kAStageCols <= kTmemCols, "tensor memory");
+  // traced: global-timer stamps of the CTA's entry, its setup, the dequantisers' loop end, the
+  // epilogue end and the exit (slots 10-14)
+  const unsigned long long g_entry = p.trace ? global_timer_ns() : 0ull;
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint8_t* rring = smem;
   uint8_t* xring = smem + (size_t)p.raw_stages * kRaw;
@@ -411,8 +425,13 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
   const uint32_t tmem = tmem_slot;
   const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   unsigned long long* trace = (p.trace && cta < p.trace_ctas) ? p.trace + (size_t)cta * kTraceEvents : nullptr;
-  const long long t_start = clock64();
-  long long tw0 = 0, tw1 = 0;
+  const bool tr = trace != nullptr;
+  const long long t_start = tr ? clock64() : 0;
+  long long tw0 = 0, tw1 = 0;  // traced wait cycles
+  if (tr && threadIdx.x == 0) {
+    trace[10] = g_entry;
+    trace[11] = global_timer_ns();
+  }
 
   if (warp == 0) {
     // ------------------------------- TMA producer -------------------------------------
@@ -424,7 +443,7 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
     for (; i < nsteps; ++i, r.next(SR), ia = (ia + 1 == spa) ? 0 : ia + 1) {
       if (ia == 0) {
         if (na >= SX && lane == 0)
-          ok = gemm_wait_timed(&empty_x[rx.s], rx.ph ^ 1u, p.err, p.timeout_ns, &tw0);
+          ok = gemm_wait_timed(&empty_x[rx.s], rx.ph ^ 1u, p.err, p.timeout_ns, &tw0, tr);
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         const int gb = ((ks0 + i) * kGemmTmKStep) >> lg;
         uint8_t* xs = xring + (size_t)rx.s * kGemmAuxStageBytes;
@@ -440,7 +459,7 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
         ++na;
       }
       if (i >= SR && lane == 0)
-        ok = gemm_wait_timed(&empty_r[r.s], r.ph ^ 1u, p.err, p.timeout_ns, &tw0);
+        ok = gemm_wait_timed(&empty_r[r.s], r.ph ^ 1u, p.err, p.timeout_ns, &tw0, tr);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       uint8_t* st = rring + (size_t)r.s * kRaw;
       const int k0 = (ks0 + i) * kGemmTmKStep;
@@ -473,8 +492,8 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
     for (int i = 0; i < nsteps; ++i, ra.next(SA), rr.next(SR)) {
       bool ok = true;
       if (lane == 0)
-        ok = gemm_wait_timed(&full_a[ra.s], ra.ph, p.err, p.timeout_ns, &tw0) &&
-             gemm_wait_timed(&full_r[rr.s], rr.ph, p.err, p.timeout_ns, &tw1);
+        ok = gemm_wait_timed(&full_a[ra.s], ra.ph, p.err, p.timeout_ns, &tw0, tr) &&
+             gemm_wait_timed(&full_r[rr.s], rr.ph, p.err, p.timeout_ns, &tw1, tr);
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       tcgen05_fence_after();
       const uint32_t xa = smem_addr(rring + (size_t)rr.s * kRaw + kX);
@@ -525,7 +544,7 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
     int pend_r = -1, pend_a = -1, pend_x = -1;  // stages of the step whose stores are pending
     long long t_comp = 0, t_cells = 0;          // traced: cycles completing stores, computing
     auto complete_pending = [&]() {
-      const long long c0 = clock64();
+      const long long c0 = tr ? clock64() : 0;
       tmem_st_wait();
       tcgen05_fence_before();
       __syncwarp();
@@ -534,23 +553,23 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
         mbar_arrive(&empty_r[pend_r]);
         if (pend_x >= 0) mbar_arrive(&empty_x[pend_x]);
       }
-      t_comp += clock64() - c0;
+      if (tr) t_comp += clock64() - c0;
     };
     int ia = 0;  // steps into the current scale stage
     for (int i = 0; i < nsteps; ++i, rr.next(SR), ra.next(SA)) {
       if (ia == 0) {
-        if (!gemm_wait_timed(&full_x[rx.s], rx.ph, p.err, p.timeout_ns, &tw0)) break;
+        if (!gemm_wait_timed(&full_x[rx.s], rx.ph, p.err, p.timeout_ns, &tw0, tr)) break;
         gb = ((ks0 + i) * kGemmTmKStep) >> lg;
       }
-      if (!gemm_wait_timed(&full_r[rr.s], rr.ph, p.err, p.timeout_ns, &tw0)) break;
-      if (i >= SA && !gemm_wait_timed(&empty_a[ra.s], ra.ph ^ 1u, p.err, p.timeout_ns, &tw1)) break;
+      if (!gemm_wait_timed(&full_r[rr.s], rr.ph, p.err, p.timeout_ns, &tw0, tr)) break;
+      if (i >= SA && !gemm_wait_timed(&empty_a[ra.s], ra.ph ^ 1u, p.err, p.timeout_ns, &tw1, tr)) break;
       tcgen05_fence_after();
-      const long long c_cells = clock64();
+      const long long c_cells = tr ? clock64() : 0;
       const uint32_t st = rbase + (uint32_t)rr.s * (uint32_t)kRaw;
       const uint32_t xs = xbase + (uint32_t)rx.s * (uint32_t)kGemmAuxStageBytes;
       const int k0 = (ks0 + i) * kGemmTmKStep;
       uint32_t h0[16], h1[16];  // the two 16x256b.x4 stores (lane halves h = 0, 1)
-      uint32_t sp[4], zp[4];
+      uint32_t sp[4], zl[4], zh[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         if (c == 0 || ((uint32_t)(16 * c) & gmask) == 0u) {
@@ -567,25 +586,28 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
             const uint32_t z = (zz >> (4 * b)) & 0xFu;
-            zp[b] = (0x6400u | z) | ((0x5400u | (z << 4)) << 16);
+            zl[b] = 0x64006400u + z * 0x00010001u;  // (1024 + z, 1024 + z)
+            zh[b] = 0x54005400u + z * 0x00100010u;  // (64 + z, 64 + z)
           }
         }
+        const uint32_t w0 = ld_shared_u32(st + w_off[0] + (uint32_t)(c * 1024));
+        const uint32_t w1 = ld_shared_u32(st + w_off[1] + (uint32_t)(c * 1024));
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const uint32_t w = ld_shared_u32(st + w_off[e] + (uint32_t)(c * 1024));
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const uint32_t v =
-                (__byte_perm(w, 0u, (uint32_t)(b | (4 << 4) | (b << 8) | (4 << 12))) & 0x00F0000Fu) |
-                0x54006400u;
-            const uint32_t cell = hsubmul(v, zp[b], sp[b]);
-            // byte b = 2h + i' -> store h, register 4c + 2i' + e
-            if (b < 2) h0[4 * c + 2 * (b & 1) + e] = cell;
-            else h1[4 * c + 2 * (b & 1) + e] = cell;
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t v = __byte_perm(w0, w1, (uint32_t)(b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12)));
+          const uint32_t lo = hsubmul((v & 0x000F000Fu) | 0x64006400u, zl[b], sp[b]);
+          const uint32_t hi = hsubmul((v & 0x00F000F0u) | 0x54005400u, zh[b], sp[b]);
+          // byte b = 2h + i' -> store h, registers 4c + 2i' + e' (e' = 0: lo, 1: hi)
+          if (b < 2) {
+            h0[4 * c + 2 * (b & 1)] = lo;
+            h0[4 * c + 2 * (b & 1) + 1] = hi;
+          } else {
+            h1[4 * c + 2 * (b & 1)] = lo;
+            h1[4 * c + 2 * (b & 1) + 1] = hi;
           }
         }
       }
-      t_cells += clock64() - c_cells;
+      if (tr) t_cells += clock64() - c_cells;
       if (pend_a >= 0) complete_pending();
       const uint32_t ta = tl + kAStageCols * (uint32_t)ra.s;
       tmem_st_16x256b_x4(ta, h0);
@@ -608,6 +630,7 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
       trace[7] = (unsigned long long)(clock64() - t_start);
       trace[8] = (unsigned long long)t_comp;
       trace[9] = (unsigned long long)t_cells;
+      trace[12] = global_timer_ns();
     }
     // epilogue: lane quarter q, the four warps of a quarter take every fourth 8-token chunk
     bool ok = true;
@@ -630,7 +653,7 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
           if (p.epi == kGemmSiluMul) {
             const float h = a0 / (1.0f + expf(-a0)) * a1;
             const size_t o = (size_t)tok * p.N + colt[0] + cl;
-            p.h16[o] = __float2half_rn(h);
+            p.h16[(size_t)tok * p.N + gemm_kperm(colt[0] + cl)] = __float2half_rn(h);
             if (p.h32) p.h32[o] = h;
           } else if (p.epi == kGemmStore) {
             const size_t o0 = (size_t)tok * p.N + colt[0] + cl, o1 = (size_t)tok * p.N + colt[1] + cl;
@@ -645,9 +668,11 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
       }
     }
   }
+  if (tr && warp == 2 && lane == 0) trace[13] = global_timer_ns();
   tcgen05_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (tr && threadIdx.x == 0) trace[14] = global_timer_ns();
 }
 
 // The dynamic shared-memory attribute of instantiation `slot` (0-2: tensor-memory kernel at 16,

@@ -89,6 +89,17 @@ __host__ __device__ constexpr bool gemm_use_tm(int nt, int k) {
 __host__ __device__ constexpr int gemm_raw_stage_bytes(int nt) {
   return (nt * 128 + kGemmTiles * 4096 + kGemmTiles * 4 * (256 + 64) + 1023) & ~1023;
 }
+// Order of k in the GEMM activations (x16, h16): inside every aligned four k the middle two are
+// swapped, so position j holds k = gemm_kperm(j) (the map is its own inverse).  The
+// tensor-memory dequantiser builds each f16 pair of an A cell from one byte of two adjacent
+// packed rows -- k and k + 2 from the low nibbles, k + 1 and k + 3 from the high ones -- with
+// one byte permute for two cells; the shared-memory dequantiser stores its k rows in the same
+// order.  Only the activations' order changes: a row's dot product is the same sum.
+__host__ __device__ constexpr int gemm_kperm(int j) { return (j & ~3) | ((j & 1) << 1) | ((j >> 1) & 1); }
+__host__ __device__ constexpr long long gemm_kperm(long long j) {
+  return (j & ~3ll) | ((j & 1) << 1) | ((j >> 1) & 1);
+}
+
 // One stage of the dequantised ring: both A tiles.
 constexpr int kGemmAStageBytes = kGemmTiles * kGemmATileBytes;
 

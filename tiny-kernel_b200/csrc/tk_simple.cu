@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <cstdint>
 
+#include "tk_gemm.h"
 #include "tk_internal.h"
 
 namespace tk {
@@ -383,7 +384,8 @@ __global__ void __launch_bounds__(kSampleThreads) softmax_sample_kernel(
   if (threadIdx.x == 0) sampled[0] = s_pick;
 }
 
-// rmsnorm of one row, written as f16 (the activations of the tensor-core GEMM).
+// rmsnorm of one row, written as f16 in the GEMM's k order (the activations of the tensor-core
+// GEMM).
 __global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                    __half* __restrict__ out, int dim, float eps) {
   __shared__ float red[32];
@@ -396,7 +398,7 @@ __global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __r
   const float tot = block_sum(ss, red);
   const float rms = rsqrtf(tot / (float)dim + eps);
   for (int i = threadIdx.x; i < dim; i += blockDim.x)
-    out[off + i] = __float2half_rn(x[off + i] * rms * w[i]);
+    out[off + gemm_kperm(i)] = __float2half_rn(x[off + i] * rms * w[i]);
 }
 
 __global__ void fused_rmsnorm_rope_kernel(const float* __restrict__ x, const float* __restrict__ w,
@@ -446,9 +448,10 @@ __global__ void add_kernel(const float* __restrict__ a, const float* __restrict_
   out[i] = a[i] + b[i];
 }
 
+// x as f16 in the GEMM's k order (rows of a multiple of 4 elements).
 __global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, long long n) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = __float2half_rn(x[i]);
+  if (i < n) y[gemm_kperm(i)] = __float2half_rn(x[i]);
 }
 
 // y[m][n] = sum over splits (in split order) of part[split][m][n] (+ residual[m][n])
