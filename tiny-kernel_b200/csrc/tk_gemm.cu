@@ -364,8 +364,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //   (64 + hi, 64 + hi') -- k = 4p + 1, 4p + 3 -- by the exponent constants 0x6400 / 0x5400; minus
 //   (1024 + z, 1024 + z) or (64 + z, 64 + z) (exact), times (s, s) (one rounding).  The MMA's k
 //   order is thus 4p, 4p + 2, 4p + 1, 4p + 3: the activations' order (gemm_kperm).
-// A step's tensor-memory stores complete (tcgen05.wait::st) after the next step's cells are
-// computed, so the store latency overlaps that work.
+// A step's tensor-memory stores are completed (tcgen05.wait::st) and the step handed to the MMA
+// warp at the end of the same step: the MMA of step i then overlaps the cells of step i + 1, and
+// the dequantisers' wait for a free A stage (three steps back) stays short.  (Completing them
+// after the next step's cells instead hides the store latency but puts a whole step between the
+// cells and the MMA, and the three-stage chain then set the pace: 1.0 us per step.)
 __device__ __forceinline__ int tm_lane_column(int l) { return 4 * (l & 7) + (l >> 3); }
 
 template <int NT>
@@ -499,12 +502,15 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
       const uint32_t xa = smem_addr(rring + (size_t)rr.s * kRaw + kX);
       const uint32_t ta = tmem + kAcol0 + kAStageCols * (uint32_t)ra.s;
       if (leader) {
+        // one descriptor per step: the k offsets add to its address field (shared-memory
+        // addresses stay below 256 KB, so the 14-bit field never carries)
+        const uint64_t bdesc = umma_smem_desc(xa, 16, 1024, 2);
 #pragma unroll
         for (int t = 0; t < kGemmTiles; ++t) {
 #pragma unroll
           for (int kk = 0; kk < kGemmTmKStep / 16; ++kk)
             umma_f16_ts(tmem + (uint32_t)(t * NT), ta + (uint32_t)(64 * t + 8 * kk),
-                        umma_smem_desc(xa + (kk >> 2) * (NT * 128) + (kk & 3) * 32, 16, 1024, 2),
+                        bdesc + (uint64_t)((((kk >> 2) * (NT * 128) + (kk & 3) * 32)) >> 4),
                         idesc, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&empty_a[ra.s]);
@@ -608,7 +614,6 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
         }
       }
       if (tr) t_cells += clock64() - c_cells;
-      if (pend_a >= 0) complete_pending();
       const uint32_t ta = tl + kAStageCols * (uint32_t)ra.s;
       tmem_st_16x256b_x4(ta, h0);
       tmem_st_16x256b_x4(ta + (16u << 16), h1);
@@ -616,6 +621,7 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
       pend_a = ra.s;
       const bool last_of_stage = ia + 1 == spa;
       pend_x = (last_of_stage || i == nsteps - 1) ? rx.s : -1;
+      complete_pending();
       if (last_of_stage) {
         rx.next(SX);
         ia = 0;
@@ -623,7 +629,6 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
         ++ia;
       }
     }
-    if (pend_a >= 0) complete_pending();
     if (trace && warp == 2 && lane == 0) {
       trace[5] = (unsigned long long)tw0;
       trace[6] = (unsigned long long)tw1;
