@@ -346,7 +346,10 @@ int tk_dequant_int4(tk_device *dev, const uint8_t *w_packed, const uint16_t *sca
  * A launch of the batch >= 5 GEMM overwrites the buffer with SM-clock cycle counts instead,
  * for CTAs x + X * (y + Y * z) below sm_count: TMA producer waiting for free ring stages,
  * producer total, MMA issuer waiting for dequantised tiles, MMA waiting for TMA stages, MMA
- * total, first dequantiser warp waiting for TMA stages, waiting for free A stages, its total. */
+ * total, first dequantiser warp waiting for TMA stages, waiting for free A stages, its total,
+ * its cycles completing tensor-memory stores, its cycles computing cells; and (the tensor-memory
+ * kernel, global-timer ns) the CTA's entry, the end of its set-up, the first dequantiser warp's
+ * loop end, its epilogue end and the CTA's exit. */
 #define TK_TRACE_EVENTS 16
 int tk_device_trace_enable(tk_device *dev, int enable);
 int tk_device_trace_read(tk_device *dev, uint64_t *out, size_t max_values, size_t *n_values);
@@ -360,8 +363,7 @@ int tk_device_trace_read(tk_device *dev, uint64_t *out, size_t max_values, size_
  * device-wide synchronisation, or a binding that cannot own a tk_device.  Same layout, shapes
  * and errors as tk_qmatmul_int4, on the calling thread's current CUDA device and on `stream`
  * (NULL = the legacy default stream).
- *  - Synchronous: it waits for its work and reads the error word back before it returns, so
- *    it cannot be recorded into a CUDA graph.
+ *  - Synchronous: it waits for its work and reads the error word back before it returns.
  *  - Results are within the path's tolerance of tk_qmatmul_int4's, not always identical: every
  *    row count runs the streaming engine in chunks of 4 rows (m >= 5 does not take the
  *    tensor-core GEMM), and shapes the engine does not take run the CUDA-core kernel.
