@@ -27,6 +27,7 @@
 #include <mutex>
 
 #include "tk_decode.h"
+#include "tk_internal.h"
 #include "tk_dp2a.cuh"
 #include "tk_ptx.cuh"
 
@@ -1098,6 +1099,7 @@ cudaError_t decode_occupancy(int mt, int gs, size_t smem, int* blocks) {
   struct Last {
     size_t smem;
     int blocks;
+    unsigned gen;
   };
   static Last last[kMaxDevices][3][4] = {};
   const int mi = mt == 1 ? 0 : mt == 2 ? 1 : mt == 4 ? 2 : -1;
@@ -1109,13 +1111,14 @@ cudaError_t decode_occupancy(int mt, int gs, size_t smem, int* blocks) {
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
   Last* L = dev >= 0 && dev < kMaxDevices ? &last[dev][mi][gi] : nullptr;
-  if (L && L->blocks > 0 && L->smem == smem) {
+  const unsigned gen = attr_generation(dev);
+  if (L && L->blocks > 0 && L->smem == smem && L->gen == gen) {
     *blocks = L->blocks;
     return cudaSuccess;
   }
   e = mt == 1 ? dec_occupancy_gs<1>(gs, smem, blocks)
       : mt == 2 ? dec_occupancy_gs<2>(gs, smem, blocks) : dec_occupancy_gs<4>(gs, smem, blocks);
-  if (L) *L = (e == cudaSuccess) ? Last{smem, *blocks} : Last{0, 0};
+  if (L) *L = (e == cudaSuccess) ? Last{smem, *blocks, gen} : Last{0, 0, 0};
   return e;
 }
 

@@ -49,6 +49,7 @@
 
 #include "tk_dp2a.cuh"
 #include "tk_engine.h"
+#include "tk_internal.h"
 #include "tk_ptx.cuh"
 
 namespace tk {
@@ -1390,6 +1391,7 @@ cudaError_t engine_occupancy(int mt, int gs, size_t smem, int* blocks) {
   struct Last {
     size_t smem;
     int blocks;
+    unsigned gen;
   };
   static std::mutex mu;
   static Last last[kMaxDevices][3][4] = {};  // [device][MT 1, 2, 4][GS 16, 32, 64, 128]
@@ -1401,7 +1403,8 @@ cudaError_t engine_occupancy(int mt, int gs, size_t smem, int* blocks) {
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lock(mu);
   Last* L = dev >= 0 && dev < kMaxDevices ? &last[dev][mi][gi] : nullptr;
-  if (L && L->blocks > 0 && L->smem == smem) {
+  const unsigned gen = attr_generation(dev);
+  if (L && L->blocks > 0 && L->smem == smem && L->gen == gen) {
     *blocks = L->blocks;
     return cudaSuccess;
   }
@@ -1410,7 +1413,7 @@ cudaError_t engine_occupancy(int mt, int gs, size_t smem, int* blocks) {
     case 2: e = occupancy_gs<2>(gs, smem, blocks); break;
     default: e = occupancy_gs<4>(gs, smem, blocks); break;
   }
-  if (L) *L = (e == cudaSuccess) ? Last{smem, *blocks} : Last{0, 0};
+  if (L) *L = (e == cudaSuccess) ? Last{smem, *blocks, gen} : Last{0, 0, 0};
   return e;
 }
 

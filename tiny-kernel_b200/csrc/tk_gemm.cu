@@ -33,6 +33,7 @@
 
 #include "tk_engine.h"
 #include "tk_gemm.h"
+#include "tk_internal.h"
 #include "tk_ptx.cuh"
 
 namespace tk {
@@ -683,19 +684,24 @@ __global__ void __launch_bounds__(kGemmTmThreads, 1)
 // The dynamic shared-memory attribute of instantiation `slot` (0-2: tensor-memory kernel at 16,
 // 32, 64 tokens; 3-4: shared-memory kernel at 128, 256), set again only when it is launched on a
 // device with another size than its last launch there: the call costs host time ahead of every
-// launch otherwise.
+// launch otherwise (or in an earlier CUDA context of the device: attr_generation).
 cudaError_t set_smem_attr(const void* kern, int slot, size_t smem) {
   constexpr int kMaxDevices = 64, kSlots = 5;
   static std::mutex mu;
-  static size_t last[kMaxDevices][kSlots] = {};
+  struct Last {
+    size_t smem;
+    unsigned gen;
+  };
+  static Last last[kMaxDevices][kSlots] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lock(mu);
-  size_t* L = dev >= 0 && dev < kMaxDevices ? &last[dev][slot] : nullptr;
-  if (L && *L == smem) return cudaSuccess;
+  Last* L = dev >= 0 && dev < kMaxDevices ? &last[dev][slot] : nullptr;
+  const unsigned gen = attr_generation(dev);
+  if (L && L->smem == smem && L->gen == gen) return cudaSuccess;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (L) *L = e == cudaSuccess ? smem : 0;
+  if (L) *L = e == cudaSuccess ? Last{smem, gen} : Last{0, 0};
   return e;
 }
 

@@ -12,6 +12,12 @@
 
 namespace tk {
 
+// tk_runtime.cu -- generation of the per-device kernel attribute caches (dynamic shared memory,
+// occupancy): tk_device_create bumps it for its device, so an attribute set in an earlier CUDA
+// context of the device (before a cudaDeviceReset) is set again on the next launch.
+unsigned attr_generation(int dev);
+void bump_attr_generation(int dev);
+
 // tk_engine.cu
 int engine_warps_per_cta();
 size_t engine_smem_bytes(int stages, int tile_stage_bytes, int aux_stage_bytes, int rec0_bytes);

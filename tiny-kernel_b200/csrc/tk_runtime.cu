@@ -1007,6 +1007,21 @@ bool matrix_aligned(const tk_int4_matrix* a) {
 
 }  // namespace
 
+namespace tk {
+namespace {
+constexpr int kAttrGenDevices = 64;
+std::atomic<unsigned> g_attr_gen[kAttrGenDevices];
+}  // namespace
+// Starts at 1 (a cache entry's 0 never matches); devices beyond the table share generation 1,
+// which their callers' caches (also limited to 64 devices) do not keep anyway.
+unsigned attr_generation(int dev) {
+  return dev >= 0 && dev < kAttrGenDevices ? g_attr_gen[dev].load(std::memory_order_acquire) + 1u : 1u;
+}
+void bump_attr_generation(int dev) {
+  if (dev >= 0 && dev < kAttrGenDevices) g_attr_gen[dev].fetch_add(1u, std::memory_order_acq_rel);
+}
+}  // namespace tk
+
 extern "C" {
 
 int tk_abi_version(void) { return TK_ABI_VERSION; }
@@ -1041,6 +1056,7 @@ int tk_device_create(int ordinal, tk_device** out) {
     return st;
   };
   if (cudaSetDevice(ordinal) != cudaSuccess) return cleanup(fail(TK_ERR_CUDA, "cudaSetDevice failed"));
+  tk::bump_attr_generation(ordinal);
   if (cudaGetDeviceProperties(&d->prop, ordinal) != cudaSuccess)
     return cleanup(fail(TK_ERR_CUDA, "cudaGetDeviceProperties failed"));
   if (d->prop.major < 10)
