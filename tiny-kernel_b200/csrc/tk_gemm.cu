@@ -1,4 +1,4 @@
-// tk_gemm.cu -- batch >= 16 INT4 GEMM on the 5th-generation tensor cores (tcgen05).
+// tk_gemm.cu -- batch >= 5 INT4 GEMM on the 5th-generation tensor cores (tcgen05).
 //
 // Computes the qmatmul_int4 contraction of the reference (src/kernels/shaders.zig:442-501)
 //     y[m][n] = sum_g scale[g][n] * sum_{k in g} x[m][k] * (q[k][n] - zero[g][n])

@@ -1,11 +1,12 @@
-// tk_gemm.h -- parameters of the batch >= 16 INT4 GEMM (tcgen05 / tensor memory).
+// tk_gemm.h -- parameters of the batch >= 5 INT4 GEMM (tcgen05 / tensor memory).
 //
 // Y[M][N] = X[M][K] . W[K][N] with W in the reference's packed INT4 layout
-// (src/kernels/shaders.zig:442-501): the weights are dequantised in shared memory to f16
-// ((q - z) * scale, one rounding) and multiplied on the 5th-generation tensor cores with f32
-// accumulators in tensor memory.  MMA M = 128 output columns (the dequantised weights, A,
-// MN-major), MMA N = a tile of NT tokens (the f16 activations, B, K-major); both with the
-// 128-byte swizzle.
+// (src/kernels/shaders.zig:442-501): the weights are dequantised to f16 ((q - z) * scale, one
+// rounding) and multiplied on the 5th-generation tensor cores with f32 accumulators in tensor
+// memory.  MMA M = 128 output columns (the dequantised weights, A), MMA N = a tile of NT tokens
+// (the f16 activations, B, K-major, 128-byte swizzle).  Token tiles up to 64: A is written into
+// tensor memory (int4_gemm_tm_kernel); 128 and 256: A is written into shared memory, MN-major
+// with the 128-byte swizzle (int4_gemm_kernel).
 // A CTA computes two 128-column tiles (two matrices at the same columns -- gate and up -- or
 // 256 adjacent columns of one matrix) for NT tokens over a range of K.
 #pragma once

@@ -77,7 +77,7 @@ cudaError_t launch_rmsnorm_f16(const float* x, const float* w, __half* out, int 
 cudaError_t launch_splitk_reduce(const float* part, int splits, long long mn, const float* residual,
                                  float* y, cudaStream_t st);
 
-// tk_gemm.cu -- batch >= 16 GEMM (tcgen05); nt = token tile in {16, 32, 64, 128, 256}
+// tk_gemm.cu -- batch >= 5 GEMM (tcgen05); nt = token tile in {16, 32, 64, 128, 256}
 cudaError_t gemm_launch(int nt, const GemmMaps& maps, const GemmParams& p, dim3 grid, size_t smem,
                         cudaStream_t st);
 

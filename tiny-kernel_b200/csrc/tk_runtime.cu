@@ -111,7 +111,7 @@ struct tk_device {
   ScratchBuf frag[1];      // per-CTA prologue records when they do not fit in shared memory
   ScratchBuf partials[2];  // split-K partial sums: [0] first reduction, [1] second
   ScratchBuf counters[2];  // segment counters per 128-column sub-tile of each
-  // batch >= 16 GEMM path: f16 activations, f16 h, split-K partials
+  // batch >= 5 GEMM path: f16 activations, f16 h, split-K partials
   ScratchBuf g_x16, g_h16, g_part;
   int gemm_enabled = 1;  // TK_GEMM=0 routes every batch through the engine
   int engine_ctas = 0;    // TK_ENGINE_CTAS: CTAs of the engine's launches (0: one per SM)
@@ -757,7 +757,7 @@ int decode_run(tk_device* d, const float* x, const float* norm_w, float eps,
   return TK_OK;
 }
 
-// ---- batch >= 16: the tcgen05 GEMM path (tk_gemm.cu) ----------------------------------------
+// ---- batch >= 5: the tcgen05 GEMM path (tk_gemm.cu) ----------------------------------------
 
 // From 5 rows the tcgen05 GEMM: a decode launch takes at most 4 rows, and two of them (batch
 // 5-8: 85-122 us per 8B FFN step) cost more than one GEMM over a 16-token tile (about 71 us).
@@ -886,7 +886,7 @@ int gemm_splits(tk_device* d, int ctas, int k, int nt) {
   return std::max(1, std::min({steps, d->sm_count / ctas, 16}));
 }
 
-// y[m][n] (+)= x[m][k] . W for m >= 16 rows on the tensor cores.
+// y[m][n] (+)= x[m][k] . W for m >= 5 rows on the tensor cores.
 int qmatmul_gemm(tk_device* d, const float* x, const uint8_t* w, const uint16_t* s,
                  const uint8_t* z, float* out, int m, int k, int n, int gs, cudaStream_t st) {
   const int nt = gemm_nt(m);
@@ -926,7 +926,7 @@ int qmatmul_gemm(tk_device* d, const float* x, const uint8_t* w, const uint16_t*
   return TK_OK;
 }
 
-// The INT4 FFN for m >= 16 rows: rmsnorm (written as f16), gate/up GEMM with silu(gate) * up in its
+// The INT4 FFN for m >= 5 rows: rmsnorm (written as f16), gate/up GEMM with silu(gate) * up in its
 // epilogue (h in f16 for the down GEMM, and in f32 when asked), down GEMM split over K,
 // reduction (+ residual).
 int ffn_gemm(tk_device* d, const float* x, const float* norm_w, const tk_int4_matrix* gate,
